@@ -1,0 +1,258 @@
+"""ctypes binding of the C ABI (include/carbon_rec.h), and a Python device object that
+mirrors the reference's recognizer backend, carbon::PipelineModels
+(carbon/include/carbon/pipeline.h:94-142): set_pages, prefetch_pages, recognize (the
+lines of a group at one bucket width, their CTC decodings and the frames read),
+broken.  Errors raise ``CrecError`` (the reference throws carbon::Error).
+
+The library is built in-tree (carbon_rec/build.py) and loaded from there; there is no
+fallback: without it, or without a B200, opening a device raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "libcarbon_rec.so"
+
+OK, E_INVALID, E_NOMEM, E_CUDA, E_STICKY, E_TIMEOUT, E_MODEL, E_RANGE = range(8)
+INT8, FP16 = 0, 1
+_NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA error", E_STICKY: "sticky CUDA error",
+          E_TIMEOUT: "kernel wait timed out", E_MODEL: "model not supported", E_RANGE: "out of range"}
+
+# every entry point include/carbon_rec.h declares
+EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec_set_pages", "crec_prefetch_pages",
+           "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_width_bucket", "crec_crop_region",
+           "crec_stream", "crec_debug_crops", "crec_debug_value"]
+
+
+class CrecError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{_NAMES.get(code, code)}: {message}")
+        self.code = code
+
+
+class CropRule(C.Structure):
+    _fields_ = [("height", C.c_int), ("width_step", C.c_int), ("frame_px", C.c_int), ("pad_v", C.c_double),
+                ("pad_h", C.c_double), ("flip_margin", C.c_int), ("flip_needs_dark", C.c_int)]
+
+    @classmethod
+    def default(cls, **kw) -> "CropRule":
+        r = cls(32, 8, 4, 0.2, 0.3, 48, 1)
+        for k, v in kw.items():
+            setattr(r, k, v)
+        return r
+
+
+class Config(C.Structure):
+    _fields_ = [("precision", C.c_int), ("device", C.c_int), ("max_lines", C.c_int), ("max_width", C.c_int),
+                ("max_columns", C.c_int64), ("max_pages", C.c_int), ("max_page_bytes", C.c_int64),
+                ("crop", CropRule), ("model", C.c_void_p), ("model_bytes", C.c_size_t)]
+
+
+class Page(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("width", C.c_int), ("height", C.c_int), ("stride", C.c_int64)]
+
+
+class RowRuns(C.Structure):
+    _fields_ = [("runs", C.c_void_p), ("count", C.c_int)]
+
+
+class Box(C.Structure):
+    _fields_ = [("x0", C.c_double), ("y0", C.c_double), ("x1", C.c_double), ("y1", C.c_double)]
+
+
+class Lines(C.Structure):
+    _fields_ = [("counts", C.c_void_p), ("lengths", C.c_void_p), ("offsets", C.c_void_p), ("ids", C.c_void_p),
+                ("frames", C.c_void_p), ("probs", C.c_void_p), ("capacity", C.c_int64), ("total", C.c_int64)]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The CUDA library; raises if it was not built (there is no CPU fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with carbon_rec/build.py (nvcc, sm_100a)")
+        L = C.CDLL(str(LIB_PATH))
+        p, i, i64 = C.c_void_p, C.c_int, C.c_int64
+        L.crec_open.argtypes = [C.POINTER(Config), C.POINTER(p)]
+        L.crec_close.argtypes = [p]
+        L.crec_last_error.argtypes = [p]
+        L.crec_last_error.restype = C.c_char_p
+        L.crec_is_broken.argtypes = [p]
+        L.crec_set_pages.argtypes = [p, p, i, p]
+        L.crec_prefetch_pages.argtypes = [p, p, i, p]
+        L.crec_set_pages_device.argtypes = [p, p, i]
+        L.crec_recognize.argtypes = [p, p, p, i, i, C.POINTER(Lines)]
+        L.crec_recognize_lines.argtypes = [p, p, p, p, i, C.POINTER(Lines)]
+        L.crec_recognize_crops.argtypes = [p, p, i, p, p, i, C.POINTER(Lines)]
+        L.crec_width_bucket.argtypes = [i]
+        L.crec_crop_region.argtypes = [C.POINTER(Box), C.POINTER(CropRule), p, C.POINTER(i)]
+        L.crec_stream.argtypes = [p]
+        L.crec_stream.restype = p
+        L.crec_debug_crops.argtypes = [p, p, i]
+        L.crec_debug_value.argtypes = [p, i, p, i64]
+        _lib = L
+    return _lib
+
+
+def width_bucket(crop_width: int) -> int:
+    return lib().crec_width_bucket(int(crop_width))
+
+
+def crop_region(box, rule: CropRule | None = None):
+    rule = rule or CropRule.default()
+    b = Box(*[float(v) for v in box])
+    reg = np.zeros(4, np.float64)
+    w = C.c_int()
+    lib().crec_crop_region(C.byref(b), C.byref(rule), reg.ctypes.data, C.byref(w))
+    return reg, w.value
+
+
+@dataclass
+class CtcLine:
+    """carbon::CtcLine: ids (blanks dropped, repeats collapsed), first frames, probabilities."""
+    ids: np.ndarray
+    frames: np.ndarray
+    probs: np.ndarray
+
+
+def _boxes(boxes) -> np.ndarray:
+    b = np.ascontiguousarray(np.asarray(boxes, np.float64).reshape(-1, 4))
+    return b
+
+
+class RecDevice:
+    """One GPU's recognizer (the PipelineModels recognizer methods), over the C ABI."""
+
+    def __init__(self, model_blob: bytes, precision: int = INT8, device: int = 0, max_lines: int = 256,
+                 max_width: int = 2048, max_columns: int = 0, max_pages: int = 64, max_page_bytes: int = 0,
+                 crop: CropRule | None = None):
+        L = lib()
+        self._blob = C.create_string_buffer(bytes(model_blob), len(model_blob))
+        self.crop = crop or CropRule.default()
+        cfg = Config(precision, device, max_lines, max_width, max_columns, max_pages, max_page_bytes, self.crop,
+                     C.cast(self._blob, C.c_void_p), len(model_blob))
+        h = C.c_void_p()
+        rc = L.crec_open(C.byref(cfg), C.byref(h))
+        self._h = h
+        if rc != OK:
+            msg = L.crec_last_error(h).decode() if h else ""
+            L.crec_close(h)
+            self._h = None
+            raise CrecError(rc, msg)
+        self.max_lines, self.max_width = max_lines, max_width
+        self._keep: list = []
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().crec_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def _check(self, rc: int) -> None:
+        if rc != OK:
+            raise CrecError(rc, lib().crec_last_error(self._h).decode())
+
+    @property
+    def broken(self) -> bool:
+        return bool(lib().crec_is_broken(self._h))
+
+    @property
+    def stream(self) -> int:
+        return lib().crec_stream(self._h)
+
+    def set_pages(self, pages, rows=None) -> None:
+        """pages: list of 2-d uint8 arrays (paper 255); rows: per page a list of (first, last) row runs or None."""
+        arr = [np.ascontiguousarray(p, np.uint8) for p in pages]
+        descs = (Page * max(1, len(arr)))(*[Page(a.ctypes.data, a.shape[1], a.shape[0], a.strides[0]) for a in arr])
+        runs = None
+        keep = []
+        if rows is not None:
+            rr = []
+            for r in rows:
+                if r:
+                    a = np.ascontiguousarray(np.asarray(r, np.int32).reshape(-1))
+                    keep.append(a)
+                    rr.append(RowRuns(a.ctypes.data, len(a) // 2))
+                else:
+                    rr.append(RowRuns(None, 0))
+            runs = (RowRuns * len(rr))(*rr)
+        self._check(lib().crec_set_pages(self._h, descs, len(arr), runs))
+
+    def set_pages_device(self, pages) -> None:
+        """pages: list of (device pointer, width, height, stride) already in this GPU's memory."""
+        descs = (Page * max(1, len(pages)))(*[Page(int(d), int(w), int(hh), int(s)) for d, w, hh, s in pages])
+        self._check(lib().crec_set_pages_device(self._h, descs, len(pages)))
+
+    def prefetch_pages(self, pages, rows=None) -> None:
+        arr = [np.ascontiguousarray(p, np.uint8) for p in pages]
+        descs = (Page * max(1, len(arr)))(*[Page(a.ctypes.data, a.shape[1], a.shape[0], a.strides[0]) for a in arr])
+        self._check(lib().crec_prefetch_pages(self._h, descs, len(arr), None))
+
+    def _lines(self, n: int, cap: int):
+        bufs = dict(counts=np.zeros(n, np.int32), lengths=np.zeros(n, np.int32), offsets=np.zeros(n, np.int32),
+                    ids=np.zeros(cap, np.int32), frames=np.zeros(cap, np.int32), probs=np.zeros(cap, np.float32))
+        s = Lines(*[bufs[k].ctypes.data for k in ("counts", "lengths", "offsets", "ids", "frames", "probs")], cap, 0)
+        return bufs, s
+
+    @staticmethod
+    def _unpack(bufs, n: int):
+        out = []
+        for i in range(n):
+            o, k = int(bufs["offsets"][i]), int(bufs["counts"][i])
+            out.append(CtcLine(bufs["ids"][o:o + k].copy(), bufs["frames"][o:o + k].copy(), bufs["probs"][o:o + k].copy()))
+        return out, bufs["lengths"].copy()
+
+    def recognize(self, page_of, boxes, bw: int):
+        """PipelineModels::recognize: (list of CtcLine, lengths) for boxes of pages page_of at bucket width bw."""
+        po = np.ascontiguousarray(page_of, np.int32)
+        b = _boxes(boxes)
+        n = len(po)
+        bufs, s = self._lines(n, max(1, n * (bw // self.crop.frame_px)))
+        self._check(lib().crec_recognize(self._h, po.ctypes.data, b.ctypes.data, n, int(bw), C.byref(s)))
+        return self._unpack(bufs, n)
+
+    def recognize_lines(self, page_of, boxes, bw=None):
+        """Any number of lines, each at its own bucket width (bw[i], or the width ladder's bucket)."""
+        po = np.ascontiguousarray(page_of, np.int32)
+        b = _boxes(boxes)
+        n = len(po)
+        bwa = None if bw is None else np.ascontiguousarray(bw, np.int32)
+        cap = max(1, n * (self.max_width // self.crop.frame_px))
+        bufs, s = self._lines(n, cap)
+        self._check(lib().crec_recognize_lines(self._h, po.ctypes.data, b.ctypes.data,
+                                               None if bwa is None else bwa.ctypes.data, n, C.byref(s)))
+        return self._unpack(bufs, n)
+
+    def recognize_crops(self, crops, widths, bw):
+        """Ready crops [n, height, pitch] uint8 (line i's first bw[i] columns finished and padded), their crop
+        widths: (list of CtcLine, lengths)."""
+        c = np.ascontiguousarray(crops, np.uint8)
+        n, _, pitch = c.shape
+        w = np.ascontiguousarray(widths, np.int32)
+        b = np.ascontiguousarray(bw, np.int32)
+        bufs, s = self._lines(n, max(1, int(b.sum()) // self.crop.frame_px))
+        self._check(lib().crec_recognize_crops(self._h, c.ctypes.data, int(pitch), w.ctypes.data, b.ctypes.data, n,
+                                               C.byref(s)))
+        return self._unpack(bufs, n)
+
+    def arm_crops(self, pitch: int) -> None:
+        self._check(lib().crec_debug_crops(self._h, None, int(pitch)))
+
+    def crops(self, n: int, pitch: int) -> np.ndarray:
+        out = np.zeros((n, self.crop.height, pitch), np.uint8)
+        self._check(lib().crec_debug_crops(self._h, out.ctypes.data, int(pitch)))
+        return out
+
+    def value(self, index: int, nbytes: int, dtype=np.uint8) -> np.ndarray:
+        out = np.zeros(nbytes, np.uint8)
+        self._check(lib().crec_debug_value(self._h, int(index), out.ctypes.data, nbytes))
+        return out.view(dtype)

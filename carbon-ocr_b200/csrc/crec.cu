@@ -1,0 +1,1143 @@
+// The C ABI (include/carbon_rec.h) over the sm_100a kernels: the model blob read into device
+// weights, the group layout, tensor maps, launches and results.
+//
+// A run's lines lie end to end along the width of one tensor per layer: line i at input
+// columns [seg_i, seg_i + bw_i), gaps of `gap` columns between them (and before the first)
+// holding the zero point, so every convolution of every line reads exactly the borders the
+// reference's executor gives a batch of that bucket width (carbon/src/net/net.cpp:100-160),
+// and each layer is one launch over the whole run whatever the mix of widths.  A gap is as
+// wide as the widest padding any layer reads, in input columns; segments and gaps are whole
+// multiples of the network's horizontal stride.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/carbon_rec.h"
+#include "conv_gemm.cuh"
+#include "crop_stem.cuh"
+#include "dw_head.cuh"
+#include "sm100.cuh"
+
+using namespace crec;
+
+namespace {
+
+constexpr int kKindConv = 0, kKindDw = 1, kKindResize = 2;
+constexpr size_t kGuard = 64 << 10;
+
+struct Value {
+  int c = 0, u8 = 0, ph = 0, pw = 0, zero = 0;
+  float scale = 1.0f;
+  // layout
+  int h = 0;       // rows
+  int shift = 0;   // log2 of input columns per column
+  int phys = -1;   // the value whose memory holds it (itself, or a Resize's source)
+  int extra = 0;   // log2 of the nearest upsampling read in place: physical column = column >> extra
+  int cp = 0;      // channels padded to 16
+  bool real = false;
+  uint8_t* alloc = nullptr;
+  uint8_t* base = nullptr;  // first (top border) row
+  long long pitch = 0;      // bytes a row
+  size_t bytes = 0;
+};
+
+struct Layer {
+  int kind, in, out, residual, kh, kw, sh, sw, pt, pl, pb, pr, cin, cout, relu, fh, fw, res_fh, res_shift, int8;
+  std::vector<int8_t> w8;  // [cout][cin/g][kh][kw]
+  std::vector<float> wf, wsc, bias;
+  // device
+  uint8_t* wimg = nullptr;
+  int32_t* colsum = nullptr;
+  float* scale = nullptr;
+  float* dbias = nullptr;
+  int8_t* dw8 = nullptr;  // depthwise [taps][cp], stem [cout][taps]
+  float* dwf = nullptr;
+  int nkb = 0, last_steps = 0, nt = 0, n_tiles = 0, stages = 0, nchunk = 0, chunks = 0;
+  uint32_t stage_bytes = 0, a_bytes = 0, b_bytes = 0, smem = 0;
+};
+
+template <class T>
+T rd(const uint8_t*& p) {
+  T v;
+  std::memcpy(&v, p, sizeof v);
+  p += sizeof v;
+  return v;
+}
+
+long long round_up(long long v, long long m) { return (v + m - 1) / m * m; }
+int round16(int v) { return (v + 15) / 16 * 16; }
+int log2i(int v) {
+  int s = 0;
+  while ((1 << s) < v) ++s;
+  return (1 << s) == v ? s : -1;
+}
+
+// carbon/src/net/net.cpp:84-90 (quantize), the input table's arithmetic.
+uint8_t quantize_in(float v, float scale, int zero) {
+  float r = v / scale;
+  r = std::min(4194304.0f, std::max(-4194304.0f, r));
+  volatile float t = r + 12582912.0f;
+  r = t - 12582912.0f;
+  r += static_cast<float>(zero);
+  return static_cast<uint8_t>(std::min(255.0f, std::max(0.0f, r)));
+}
+
+uint16_t half_bits(float f) {
+  const __half h = __float2half_rn(f);
+  uint16_t b;
+  std::memcpy(&b, &h, 2);
+  return b;
+}
+float half_round(float f) { return __half2float(__float2half_rn(f)); }
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+}  // namespace
+
+struct crec_handle {
+  crec_config cfg{};
+  std::string error;
+  bool broken = false;
+  int device = 0, sms = 0;
+  bool int8 = true;
+  int eb = 1;
+  cudaStream_t stream = nullptr;
+  EncodeTiled encode = nullptr;
+  // model
+  std::vector<Value> v;
+  std::vector<Layer> l;
+  int inp = 0, outv = 0, height = 32;
+  int gap = 8, max_shift = 0, head_shift = 0;
+  long long max_cols = 0;  // input columns a run holds
+  uint8_t* in_table = nullptr;
+  float* head_table = nullptr;
+  // pages
+  std::vector<PageDesc> pages;  // device pointers
+  uint8_t* page_mem = nullptr;
+  size_t page_cap = 0;
+  bool pages_owned = true;
+  PageDesc* d_pages = nullptr;
+  int max_pages = 0;
+  // run buffers
+  LineDesc* d_lines = nullptr;
+  LineDesc* h_lines = nullptr;  // pinned
+  uint8_t* d_mask = nullptr;
+  uint8_t* h_mask = nullptr;  // pinned
+  int* d_frame0 = nullptr;
+  int* d_length = nullptr;
+  int* h_frame0 = nullptr;  // pinned [max_lines]
+  int* h_length = nullptr;
+  int32_t* d_frame_id = nullptr;
+  float* d_frame_prob = nullptr;
+  int32_t* d_count = nullptr;
+  int32_t* d_ids = nullptr;
+  int32_t* d_frames = nullptr;
+  float* d_probs = nullptr;
+  int32_t* h_count = nullptr;  // pinned
+  int32_t* h_ids = nullptr;
+  int32_t* h_frames = nullptr;
+  float* h_probs = nullptr;
+  int* d_err = nullptr;
+  int* h_err = nullptr;
+  uint8_t* d_crops = nullptr;  // debug copy of the finished crops
+  int crops_pitch = 0;
+  uint8_t* d_crops_in = nullptr;  // ready crops given by crec_recognize_crops
+  int crops_in_pitch = 0;
+  const uint8_t* run_crops = nullptr;  // this run's ready crops on the device, or null
+  // the last run
+  int last_n = 0;
+  long long last_cols = 0;
+  std::vector<int> last_seg, last_bw;
+};
+
+namespace {
+
+int set_error(crec_handle* h, int code, const std::string& msg) {
+  if (h) h->error = msg;
+  return code;
+}
+
+int cuda_status(crec_handle* h, cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return CREC_OK;
+  // the errors after which a context can run nothing more (carbon/src/cuda/pipeline_cuda.cpp:344-363)
+  switch (e) {
+    case cudaErrorIllegalAddress:
+    case cudaErrorLaunchFailure:
+    case cudaErrorIllegalInstruction:
+    case cudaErrorMisalignedAddress:
+    case cudaErrorInvalidAddressSpace:
+    case cudaErrorInvalidPc:
+    case cudaErrorHardwareStackError:
+    case cudaErrorAssert:
+    case cudaErrorECCUncorrectable:
+    case cudaErrorDevicesUnavailable:
+    case cudaErrorLaunchTimeout:
+    case cudaErrorUnknown:
+      h->broken = true;
+      return set_error(h, CREC_E_STICKY, std::string(what) + ": " + cudaGetErrorString(e));
+    case cudaErrorMemoryAllocation:
+      cudaGetLastError();
+      return set_error(h, CREC_E_NOMEM, std::string(what) + ": " + cudaGetErrorString(e));
+    default:
+      cudaGetLastError();
+      return set_error(h, CREC_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+#define CK(call)                                           \
+  do {                                                     \
+    const int rc_ = cuda_status(h, (call), #call);         \
+    if (rc_ != CREC_OK) return rc_;                        \
+  } while (0)
+
+template <class T>
+int dev_alloc(crec_handle* h, T** p, size_t count) {
+  CK(cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(count, 1) * sizeof(T)));
+  return CREC_OK;
+}
+template <class T>
+int host_alloc(crec_handle* h, T** p, size_t count) {
+  CK(cudaHostAlloc(reinterpret_cast<void**>(p), std::max<size_t>(count, 1) * sizeof(T), cudaHostAllocDefault));
+  return CREC_OK;
+}
+template <class T>
+int upload(crec_handle* h, T** d, const std::vector<T>& v) {
+  int rc = dev_alloc(h, d, v.size());
+  if (rc) return rc;
+  if (!v.empty()) CK(cudaMemcpy(*d, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+  return CREC_OK;
+}
+
+// The model blob (carbon_rec/netdef.py, RecNet.to_blob).
+int read_model(crec_handle* h, const uint8_t* blob, size_t len) {
+  if (!blob || len < 48 || std::memcmp(blob, "CRECMDL1", 8) != 0) return set_error(h, CREC_E_MODEL, "not a CRECMDL1 model blob");
+  const uint8_t* p = blob + 8;
+  const uint8_t* end = blob + len;
+  if (rd<uint32_t>(p) != 1) return set_error(h, CREC_E_MODEL, "model blob version");
+  const uint32_t kind = rd<uint32_t>(p);
+  const uint32_t nv = rd<uint32_t>(p), nl = rd<uint32_t>(p);
+  h->inp = static_cast<int>(rd<uint32_t>(p));
+  h->outv = static_cast<int>(rd<uint32_t>(p));
+  h->height = static_cast<int>(rd<uint32_t>(p));
+  rd<uint32_t>(p);
+  if ((kind == 0) != h->int8)
+    return set_error(h, CREC_E_MODEL, h->int8 ? "CREC_INT8 needs the Q/DQ file's blob" : "CREC_FP16 needs the float file's blob");
+  if (nv > 4096 || nl > 4096) return set_error(h, CREC_E_MODEL, "model blob sizes");
+  h->v.resize(nv);
+  for (auto& v : h->v) {
+    if (p + 24 > end) return set_error(h, CREC_E_MODEL, "model blob truncated");
+    v.c = static_cast<int>(rd<uint32_t>(p));
+    v.u8 = static_cast<int>(rd<uint32_t>(p));
+    v.scale = rd<float>(p);
+    v.zero = rd<int32_t>(p);
+    v.ph = static_cast<int>(rd<uint32_t>(p));
+    v.pw = static_cast<int>(rd<uint32_t>(p));
+    if (!h->int8) {
+      v.u8 = 0;
+      v.zero = 0;
+    }
+  }
+  h->l.resize(nl);
+  for (auto& l : h->l) {
+    if (p + 84 > end) return set_error(h, CREC_E_MODEL, "model blob truncated");
+    int* f = &l.kind;
+    for (int k = 0; k < 20; ++k) f[k] = (k == 3) ? rd<int32_t>(p) : static_cast<int>(rd<uint32_t>(p));
+    if (l.in < 0 || l.in >= static_cast<int>(nv) || l.out < 0 || l.out >= static_cast<int>(nv) ||
+        l.residual >= static_cast<int>(nv))
+      return set_error(h, CREC_E_MODEL, "model blob value index");
+    if (l.kind == kKindResize) continue;
+    const int groups = l.kind == kKindDw ? l.cin : 1;
+    const size_t nw = static_cast<size_t>(l.cout) * (l.cin / groups) * l.kh * l.kw;
+    if (l.int8) {
+      if (p + ((nw + 3) / 4 * 4) + 4 * l.cout > end) return set_error(h, CREC_E_MODEL, "model blob truncated");
+      l.w8.assign(reinterpret_cast<const int8_t*>(p), reinterpret_cast<const int8_t*>(p) + nw);
+      p += (nw + 3) / 4 * 4;
+      l.wsc.resize(l.cout);
+      std::memcpy(l.wsc.data(), p, 4 * l.cout);
+      p += 4 * l.cout;
+    } else {
+      if (p + 4 * nw > end) return set_error(h, CREC_E_MODEL, "model blob truncated");
+      l.wf.resize(nw);
+      std::memcpy(l.wf.data(), p, 4 * nw);
+      p += 4 * nw;
+    }
+    if (p + 4 * l.cout > end) return set_error(h, CREC_E_MODEL, "model blob truncated");
+    l.bias.resize(l.cout);
+    std::memcpy(l.bias.data(), p, 4 * l.cout);
+    p += 4 * l.cout;
+  }
+  if (p != end) return set_error(h, CREC_E_MODEL, "model blob has trailing bytes");
+  return CREC_OK;
+}
+
+// Shapes through the network, which values need memory, the gap; refuses what the kernels do not run.
+int plan_model(crec_handle* h) {
+  auto& V = h->v;
+  auto& L = h->l;
+  if (L.size() < 2) return set_error(h, CREC_E_MODEL, "a recognizer of at least a stem and a head");
+  for (auto& v : V) v.h = -1;
+  V[h->inp].h = h->height;
+  V[h->inp].shift = 0;
+  V[h->inp].phys = h->inp;
+  for (size_t i = 0; i < L.size(); ++i) {
+    const Layer& l = L[i];
+    Value& x = V[l.in];
+    Value& y = V[l.out];
+    if (x.h < 0) return set_error(h, CREC_E_MODEL, "layers out of order");
+    if (l.kind == kKindResize) {
+      const int s = log2i(l.fw);
+      if (l.fh != 1 || s < 0 || s > x.shift) return set_error(h, CREC_E_MODEL, "a Resize other than a 2^k widening");
+      y.h = x.h;
+      y.shift = x.shift - s;
+      y.phys = x.phys;
+      y.extra = x.extra + s;
+      continue;
+    }
+    const int s = log2i(l.sw);
+    if (s < 0 || l.kh > 3 || l.res_fh != 1) return set_error(h, CREC_E_MODEL, "a convolution this build does not run");
+    y.h = (x.h + l.pt + l.pb - l.kh) / l.sh + 1;
+    y.shift = x.shift + s;
+    y.phys = l.out;
+    y.extra = 0;
+    y.real = true;
+    if (i == 0) {
+      if (l.in != h->inp || l.kind != kKindConv || l.cin != 1 || l.kh * l.kw > 9 || l.residual >= 0 || l.cout > 256 ||
+          l.pt != l.pb || l.pl != l.pr)
+        return set_error(h, CREC_E_MODEL, "the first layer must be a 1-channel convolution of at most 3x3");
+    } else if (static_cast<int>(i) == static_cast<int>(L.size()) - 1) {
+      if (l.out != h->outv || l.kind != kKindConv || l.kh != 1 || l.kw != 1 || y.h != 1 || l.residual >= 0)
+        return set_error(h, CREC_E_MODEL, "the last layer must be a 1x1 head on one row");
+      if (h->int8 && !y.u8) return set_error(h, CREC_E_MODEL, "the INT8 head's output must be quantized (Q/DQ)");
+      if (x.extra) return set_error(h, CREC_E_MODEL, "a head reading an upsampling");
+      y.real = false;  // fused with CTC: never written
+    } else {
+      if (l.in == h->inp) return set_error(h, CREC_E_MODEL, "only the first layer reads the input");
+      if (l.kind == kKindConv && x.extra) return set_error(h, CREC_E_MODEL, "a dense convolution reading an upsampling");
+      if (l.kind == kKindDw && (l.sh != 1 || l.sw != 1)) return set_error(h, CREC_E_MODEL, "a strided depthwise convolution");
+    }
+    if (l.int8 != (h->int8 ? 1 : 0)) return set_error(h, CREC_E_MODEL, "mixed int8 and float layers");
+  }
+  int max_shift = 0, gap = 1;
+  for (auto& v : V) {
+    if (v.h < 0) continue;
+    max_shift = std::max(max_shift, v.shift + v.extra);
+    gap = std::max(gap, v.pw << v.shift);
+    v.cp = round16(std::max(v.c, 1));
+  }
+  h->max_shift = max_shift;
+  h->gap = static_cast<int>(round_up(gap, std::max(8, 1 << max_shift)));
+  h->head_shift = V[h->outv].shift;
+  return CREC_OK;
+}
+
+// The 128-byte swizzle of a K-major operand block: byte b of row j.
+inline size_t swz(int j, int b) { return static_cast<size_t>(j) * 128 + (((b >> 4) ^ (j & 7)) << 4) + (b & 15); }
+
+// A dense layer's (or the head's) weights as the swizzled image the kernels bulk-copy:
+// [n tile][ky][kb][nt rows][128 bytes]; byte `off` of kernel row ky's window is (kx, channel, byte).
+std::vector<uint8_t> weight_image(const crec_handle* h, const Layer& l, int cp_in, int nt, int n_tiles, int nkb) {
+  const int eb = h->eb, taps = l.kh * l.kw, window = l.kw * cp_in * eb;
+  std::vector<uint8_t> img(static_cast<size_t>(n_tiles) * l.kh * nkb * nt * 128, 0);
+  for (int n = 0; n < n_tiles; ++n)
+    for (int ky = 0; ky < l.kh; ++ky)
+      for (int kb = 0; kb < nkb; ++kb) {
+        uint8_t* blk = img.data() + (static_cast<size_t>((n * l.kh + ky) * nkb + kb)) * nt * 128;
+        for (int j = 0; j < nt; ++j) {
+          const int co = n * nt + j;
+          if (co >= l.cout) continue;
+          for (int b = 0; b < 128; ++b) {
+            const int off = kb * 128 + b;
+            if (off >= window) break;
+            const int kx = off / (cp_in * eb), rem = off % (cp_in * eb), c = rem / eb, byte = rem % eb;
+            if (c >= l.cin) continue;
+            const size_t wi = (static_cast<size_t>(co) * l.cin + c) * taps + ky * l.kw + kx;
+            uint8_t val;
+            if (h->int8) {
+              val = static_cast<uint8_t>(l.w8[wi]);
+            } else {
+              const uint16_t hb = half_bits(l.wf[wi]);
+              val = static_cast<uint8_t>(byte ? hb >> 8 : hb & 0xff);
+            }
+            blk[swz(j, b)] = val;
+          }
+        }
+      }
+  return img;
+}
+
+int setup_layer(crec_handle* h, size_t li) {
+  Layer& l = h->l[li];
+  if (l.kind == kKindResize) return CREC_OK;
+  const Value& x = h->v[l.in];
+  const Value& y = h->v[l.out];
+  const int taps = l.kh * l.kw;
+  const int cpo = li + 1 == h->l.size() ? 0 : y.cp;
+  int rc;
+  // per-channel constants, padded
+  const int npad = std::max({cpo, round16(l.cout), 16}) + 256;
+  std::vector<float> scale(npad, 0.0f), bias(npad, 0.0f);
+  std::vector<int32_t> colsum(npad, 0);
+  for (int j = 0; j < l.cout; ++j) {
+    bias[j] = l.bias[j];
+    if (h->int8) {
+      scale[j] = x.scale * l.wsc[j];  // carbon/src/net/net.cpp:703
+      const int per = l.kind == kKindDw ? 1 : l.cin;
+      int32_t s = 0;
+      for (int k = 0; k < per * taps; ++k) s += l.w8[static_cast<size_t>(j) * per * taps + k];
+      colsum[j] = s;
+    }
+  }
+  if ((rc = upload(h, &l.scale, scale)) || (rc = upload(h, &l.dbias, bias)) || (rc = upload(h, &l.colsum, colsum)))
+    return rc;
+  if (li == 0) {  // the stem: [cout][taps]
+    if (h->int8) {
+      if ((rc = upload(h, &l.dw8, l.w8))) return rc;
+    } else {
+      std::vector<float> wf(l.wf.size());
+      for (size_t i = 0; i < wf.size(); ++i) wf[i] = half_round(l.wf[i]);
+      if ((rc = upload(h, &l.dwf, wf))) return rc;
+    }
+    return CREC_OK;
+  }
+  if (l.kind == kKindDw) {  // [taps][cp]
+    const int cp = y.cp;
+    if (h->int8) {
+      std::vector<int8_t> w(static_cast<size_t>(taps) * cp, 0);
+      for (int c = 0; c < l.cout; ++c)
+        for (int t = 0; t < taps; ++t) w[static_cast<size_t>(t) * cp + c] = l.w8[static_cast<size_t>(c) * taps + t];
+      if ((rc = upload(h, &l.dw8, w))) return rc;
+    } else {
+      std::vector<float> w(static_cast<size_t>(taps) * cp, 0.0f);
+      for (int c = 0; c < l.cout; ++c)
+        for (int t = 0; t < taps; ++t) w[static_cast<size_t>(t) * cp + c] = half_round(l.wf[static_cast<size_t>(c) * taps + t]);
+      if ((rc = upload(h, &l.dwf, w))) return rc;
+    }
+    return CREC_OK;
+  }
+  const int window = l.kw * x.cp * h->eb;
+  l.nkb = (window + 127) / 128;
+  l.last_steps = (window - (l.nkb - 1) * 128 + 31) / 32;
+  if (li + 1 == h->l.size()) {  // the head
+    if (l.nkb * 16384 > 65536) return set_error(h, CREC_E_MODEL, "a head reading more than 512 bytes a frame");
+    l.nchunk = std::min(h->int8 ? 160 : 80, round16(l.cout));
+    l.chunks = (l.cout + l.nchunk - 1) / l.nchunk;
+    l.nt = l.nchunk;
+    l.n_tiles = l.chunks;
+    l.a_bytes = static_cast<uint32_t>(l.nkb) * 16384;
+    l.b_bytes = static_cast<uint32_t>(l.nkb) * l.nchunk * 128;
+    const uint32_t codes = h->int8 ? 128u * round16(l.cout) : 0u;
+    l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + 128;
+    if (l.smem > 232448) return set_error(h, CREC_E_MODEL, "the head does not fit in shared memory");
+    if (l.last_steps != 4) return set_error(h, CREC_E_MODEL, "the head's channels must fill 128-byte blocks");
+  } else {
+    l.nt = std::min(256, round16(l.cout));
+    l.n_tiles = (y.cp + l.nt - 1) / l.nt;
+    l.a_bytes = 16384;
+    l.b_bytes = static_cast<uint32_t>(l.nt) * 128;
+    l.stage_bytes = l.a_bytes + l.b_bytes;
+    l.stages = std::min<int>(8, (200 * 1024) / l.stage_bytes);
+    l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 4) * 8 + 16;
+  }
+  const std::vector<uint8_t> img = weight_image(h, l, x.cp, l.nt, l.n_tiles, l.nkb);
+  if ((rc = upload(h, &l.wimg, img))) return rc;
+  return CREC_OK;
+}
+
+int alloc_values(crec_handle* h) {
+  for (size_t i = 0; i < h->v.size(); ++i) {
+    Value& v = h->v[i];
+    if (!v.real) continue;
+    const long long cols = h->max_cols >> v.shift;
+    v.pitch = cols * v.cp * h->eb;
+    v.bytes = static_cast<size_t>(v.h + 2 * v.ph) * v.pitch + 2 * kGuard;
+    CK(cudaMalloc(&v.alloc, v.bytes));
+    CK(cudaMemset(v.alloc, h->int8 ? v.zero : 0, v.bytes));
+    v.base = v.alloc + kGuard;
+  }
+  return CREC_OK;
+}
+
+int encode_map(crec_handle* h, CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+               uint64_t s2) {
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {s1, s2};
+  const cuuint32_t box[3] = {128, 128, 1};
+  const cuuint32_t es[3] = {1, 1, 1};
+  const CUresult r = h->encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(h, CREC_E_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return CREC_OK;
+}
+
+// Launches every layer for the lines laid out in h_lines (already on the device), `cols` input columns.
+int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
+  cudaStream_t s = h->stream;
+  const Layer& stem = h->l[0];
+  const Value& x0 = h->v[h->inp];
+  const Value& s0 = h->v[stem.out];
+  {
+    CropParams p{};
+    p.pages = h->d_pages;
+    p.lines = h->d_lines;
+    p.n = n;
+    p.height = h->height;
+    p.flip_margin = h->cfg.crop.flip_margin;
+    p.flip_needs_dark = h->cfg.crop.flip_needs_dark;
+    p.crops_out = keep_crops ? h->d_crops : nullptr;
+    p.crops_pitch = h->crops_pitch;
+    p.crops_in = h->run_crops;
+    p.crops_in_pitch = h->crops_in_pitch;
+    p.kh = stem.kh;
+    p.kw = stem.kw;
+    p.sh = stem.sh;
+    p.sw = stem.sw;
+    p.pt = stem.pt;
+    p.pl = stem.pl;
+    p.cout = stem.cout;
+    p.cp_out = s0.cp;
+    p.w8 = stem.dw8;
+    p.wf = stem.dwf;
+    p.scale = stem.scale;
+    p.bias = stem.dbias;
+    p.in_table = h->in_table;
+    p.in_zero = x0.zero;
+    p.out_zero = s0.zero;
+    p.relu = stem.relu;
+    p.out_inv_scale = h->int8 ? 1.0f / s0.scale : 1.0f;
+    p.out = s0.base;
+    p.out_ph = s0.ph;
+    p.out_pitch = s0.pitch;
+    p.out_shift = s0.shift;
+    p.err = h->d_err;
+    const int maxbw = h->cfg.max_width;
+    const size_t smem = ((h->height * maxbw + 15) & ~15) + kMaxSrcRows * kStripCols +
+                        (h->height * kMaxTaps + 2 * h->height + 256 + 8) * 4;
+    if (h->int8)
+      crop_stem_kernel<true><<<n, kCropThreads, smem, s>>>(p);
+    else
+      crop_stem_kernel<false><<<n, kCropThreads, smem, s>>>(p);
+    CK(cudaGetLastError());
+  }
+  for (size_t li = 1; li < h->l.size(); ++li) {
+    const Layer& l = h->l[li];
+    if (l.kind == kKindResize) continue;
+    const Value& x = h->v[l.in];
+    const Value& y = h->v[l.out];
+    const Value& xp = h->v[x.phys];
+    const int oh = y.h;
+    const long long ow = cols >> y.shift;
+    if (li + 1 == h->l.size()) {
+      HeadParams p{};
+      int rc = encode_map(h, &p.tmap, xp.base + static_cast<long long>(xp.ph) * xp.pitch,
+                          static_cast<uint64_t>(l.nkb) * 128, static_cast<uint64_t>(ow), 1,
+                          static_cast<uint64_t>(x.cp) * h->eb, static_cast<uint64_t>(xp.pitch));
+      if (rc) return rc;
+      p.wimg = l.wimg;
+      p.nkb = l.nkb;
+      p.classes = l.cout;
+      p.nchunk = l.nchunk;
+      p.chunks = l.chunks;
+      p.ow = static_cast<int>(ow);
+      p.num_tiles = static_cast<int>((ow + 127) / 128);
+      p.a_bytes = l.a_bytes;
+      p.b_bytes = l.b_bytes;
+      p.colsum = l.colsum;
+      p.scale = l.scale;
+      p.bias = l.dbias;
+      p.in_zero = x.zero;
+      p.out_zero = y.zero;
+      p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
+      p.table = h->head_table;
+      p.mask8 = h->d_mask;
+      p.out_shift = y.shift;
+      p.frame_id = h->d_frame_id;
+      p.frame_prob = h->d_frame_prob;
+      p.err = h->d_err;
+      const int grid = std::min(p.num_tiles, h->sms);
+      if (h->int8) {
+        CK(cudaFuncSetAttribute(head_ctc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+        head_ctc_kernel<true><<<grid, kHeadThreads, l.smem, s>>>(p);
+      } else {
+        CK(cudaFuncSetAttribute(head_ctc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+        head_ctc_kernel<false><<<grid, kHeadThreads, l.smem, s>>>(p);
+      }
+      CK(cudaGetLastError());
+      continue;
+    }
+    if (l.kind == kKindDw) {
+      DwParams p{};
+      p.in = xp.base;
+      p.in_ph = xp.ph;
+      p.in_cp = xp.cp;
+      p.in_shift = x.extra;
+      p.in_zero = x.zero;
+      p.in_pitch = xp.pitch;
+      p.kh = l.kh;
+      p.kw = l.kw;
+      p.pt = l.pt;
+      p.pl = l.pl;
+      p.oh = oh;
+      p.ow = static_cast<int>(ow);
+      p.c = l.cout;
+      p.cp = y.cp;
+      p.w8 = l.dw8;
+      p.wf = l.dwf;
+      p.scale = l.scale;
+      p.bias = l.dbias;
+      p.out_zero = y.zero;
+      p.relu = l.relu;
+      p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
+      p.out = y.base;
+      p.out_ph = y.ph;
+      p.out_pitch = y.pitch;
+      p.mask8 = h->d_mask;
+      p.out_shift = y.shift;
+      const long long total = static_cast<long long>(oh) * ow * (y.cp / 16);
+      const int grid = static_cast<int>((total + 255) / 256);
+      if (h->int8)
+        dw_kernel<true><<<grid, 256, 0, s>>>(p);
+      else
+        dw_kernel<false><<<grid, 256, 0, s>>>(p);
+      CK(cudaGetLastError());
+      continue;
+    }
+    ConvParams p{};
+    const long long in_pitch = xp.pitch;
+    const uint64_t px = static_cast<uint64_t>(x.cp) * h->eb;
+    for (int ky = 0; ky < l.kh; ++ky) {
+      const uint8_t* base = xp.base + static_cast<long long>(ky - l.pt + xp.ph) * in_pitch - static_cast<long long>(l.pl) * px;
+      int rc = encode_map(h, &p.tmap[ky], base, static_cast<uint64_t>(l.nkb) * 128, static_cast<uint64_t>(ow),
+                          static_cast<uint64_t>(oh), static_cast<uint64_t>(l.sw) * px,
+                          static_cast<uint64_t>(l.sh) * in_pitch);
+      if (rc) return rc;
+    }
+    p.wimg = l.wimg;
+    p.kh = l.kh;
+    p.nkb = l.nkb;
+    p.last_steps = l.last_steps;
+    p.nt = l.nt;
+    p.n_tiles = l.n_tiles;
+    p.oh = oh;
+    p.ow = static_cast<int>(ow);
+    p.m_per_row = static_cast<int>((ow + 127) / 128);
+    p.num_tiles = oh * p.m_per_row * l.n_tiles;
+    p.stages = l.stages;
+    p.stage_bytes = l.stage_bytes;
+    p.a_bytes = l.a_bytes;
+    p.b_bytes = l.b_bytes;
+    p.out = y.base;
+    p.out_ph = y.ph;
+    p.out_pitch = y.pitch;
+    p.cp_out = y.cp;
+    p.c_out = l.cout;
+    p.ebytes = h->eb;
+    p.colsum = l.colsum;
+    p.scale = l.scale;
+    p.bias = l.dbias;
+    p.in_zero = x.zero;
+    p.out_zero = y.zero;
+    p.relu = l.relu;
+    p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
+    if (l.residual >= 0) {
+      const Value& r = h->v[l.residual];
+      const Value& rp = h->v[r.phys];
+      p.res = rp.base;
+      p.res_ph = rp.ph;
+      p.res_cp = rp.cp;
+      p.res_shift = rp.shift - y.shift;
+      p.res_zero = r.zero;
+      p.res_pitch = rp.pitch;
+      p.res_scale = r.scale;
+    }
+    p.mask8 = h->d_mask;
+    p.out_shift = y.shift;
+    p.err = h->d_err;
+    const int grid = std::min(p.num_tiles, h->sms);
+    if (h->int8) {
+      CK(cudaFuncSetAttribute(conv_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+      conv_gemm_kernel<true><<<grid, kConvThreads, l.smem, s>>>(p);
+    } else {
+      CK(cudaFuncSetAttribute(conv_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+      conv_gemm_kernel<false><<<grid, kConvThreads, l.smem, s>>>(p);
+    }
+    CK(cudaGetLastError());
+  }
+  CollapseParams c{};
+  c.frame_id = h->d_frame_id;
+  c.frame_prob = h->d_frame_prob;
+  c.line_frame0 = h->d_frame0;
+  c.length = h->d_length;
+  c.n = n;
+  c.count = h->d_count;
+  c.ids = h->d_ids;
+  c.frames = h->d_frames;
+  c.probs = h->d_probs;
+  collapse_kernel<<<(n + 127) / 128, 128, 0, s>>>(c);
+  CK(cudaGetLastError());
+  return CREC_OK;
+}
+
+// One device run over lines [0, n) with bucket widths bw[i]: lay out, launch, fetch, pack into out
+// starting at out->total.
+int run_lines(crec_handle* h, const int32_t* page_of, const crec_box* boxes, const int* bw, int n, crec_lines* out,
+              int line0, const uint8_t* crops = nullptr, int crops_pitch = 0, const int32_t* widths = nullptr) {
+  const crec_crop_rule& rule = h->cfg.crop;
+  long long seg = h->gap;
+  h->last_seg.resize(n);
+  h->last_bw.resize(n);
+  h->run_crops = nullptr;
+  for (int i = 0; i < n; ++i) {
+    double reg[4] = {0, 0, 1, 1};
+    int width = 0;
+    if (crops) {
+      width = widths[i];
+      if (width <= 0 || width > bw[i] || bw[i] > crops_pitch)
+        return set_error(h, CREC_E_RANGE, "recognize_crops: line " + std::to_string(line0 + i) + " width " +
+                                              std::to_string(width) + ", bucket " + std::to_string(bw[i]));
+      LineDesc& d = h->h_lines[i];
+      d.x0 = d.y0 = 0;
+      d.x1 = d.y1 = 1;
+      d.page = 0;
+      d.width = width;
+      d.bw = bw[i];
+      d.seg = static_cast<int>(seg);
+      h->last_seg[i] = static_cast<int>(seg);
+      h->last_bw[i] = bw[i];
+      h->h_frame0[i] = static_cast<int>(seg >> h->head_shift);
+      h->h_length[i] = std::min(bw[i] >> h->head_shift, width / rule.frame_px);
+      seg += bw[i] + h->gap;
+      continue;
+    }
+    crec_crop_region(&boxes[i], &rule, reg, &width);
+    if (page_of[i] < 0 || page_of[i] >= static_cast<int>(h->pages.size()))
+      return set_error(h, CREC_E_INVALID, "line " + std::to_string(line0 + i) + ": page " + std::to_string(page_of[i]) + " not set");
+    if (width > bw[i])
+      return set_error(h, CREC_E_RANGE, "crop_lines: line " + std::to_string(line0 + i) + " is " + std::to_string(width) +
+                                            " px wide, the batch " + std::to_string(bw[i]));
+    const double scale_x = (reg[2] - reg[0]) / width, scale_y = (reg[3] - reg[1]) / rule.height;
+    if (scale_x > 7.0 || scale_y > 7.0 || (reg[3] - reg[1]) + 2 * std::max(1.0, scale_y) + 2 > kMaxSrcRows)
+      return set_error(h, CREC_E_RANGE, "line " + std::to_string(line0 + i) + ": a downscale beyond this build's filter reach");
+    LineDesc& d = h->h_lines[i];
+    d.x0 = reg[0];
+    d.y0 = reg[1];
+    d.x1 = reg[2];
+    d.y1 = reg[3];
+    d.page = page_of[i];
+    d.width = width;
+    d.bw = bw[i];
+    d.seg = static_cast<int>(seg);
+    h->last_seg[i] = static_cast<int>(seg);
+    h->last_bw[i] = bw[i];
+    h->h_frame0[i] = static_cast<int>(seg >> h->head_shift);
+    h->h_length[i] = std::min(bw[i] >> h->head_shift, width / rule.frame_px);
+    seg += bw[i] + h->gap;
+  }
+  const long long cols = round_up(seg, 128LL << h->max_shift);
+  if (cols > h->max_cols) return set_error(h, CREC_E_RANGE, "a run wider than the configured columns");
+  for (int i = 0; i < n; ++i) h->h_lines[i].next_seg = i + 1 < n ? h->h_lines[i + 1].seg : static_cast<int>(cols);
+  std::memset(h->h_mask, 0, static_cast<size_t>(cols / 8));
+  for (int i = 0; i < n; ++i)
+    std::memset(h->h_mask + h->last_seg[i] / 8, 1, static_cast<size_t>(h->last_bw[i] / 8));
+  cudaStream_t s = h->stream;
+  CK(cudaMemcpyAsync(h->d_lines, h->h_lines, sizeof(LineDesc) * n, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(h->d_mask, h->h_mask, static_cast<size_t>(cols / 8), cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(h->d_frame0, h->h_frame0, sizeof(int) * n, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(h->d_length, h->h_length, sizeof(int) * n, cudaMemcpyHostToDevice, s));
+  CK(cudaMemsetAsync(h->d_err, 0, sizeof(int), s));
+  if (crops) {
+    CK(cudaMemcpyAsync(h->d_crops_in, crops, static_cast<size_t>(n) * h->height * crops_pitch, cudaMemcpyHostToDevice, s));
+    h->run_crops = h->d_crops_in;
+    h->crops_in_pitch = crops_pitch;
+  }
+  int rc = launch_run(h, n, cols, h->d_crops != nullptr);
+  if (rc) return rc;
+  const size_t frames = static_cast<size_t>(cols >> h->head_shift);
+  CK(cudaMemcpyAsync(h->h_count, h->d_count, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(h->h_ids, h->d_ids, sizeof(int32_t) * frames, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(h->h_frames, h->d_frames, sizeof(int32_t) * frames, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(h->h_probs, h->d_probs, sizeof(float) * frames, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if (*h->h_err) {
+    return set_error(h, CREC_E_TIMEOUT, "a kernel's bounded wait ran out (device error " + std::to_string(*h->h_err) + ")");
+  }
+  h->last_n = n;
+  h->last_cols = cols;
+  for (int i = 0; i < n; ++i) {
+    const int k = h->h_count[i];
+    const int li = line0 + i;
+    out->counts[li] = k;
+    out->lengths[li] = h->h_length[i];
+    out->offsets[li] = static_cast<int32_t>(out->total);
+    if (out->total + k > out->capacity) return set_error(h, CREC_E_RANGE, "crec_lines: capacity too small");
+    const int f0 = h->h_frame0[i];
+    std::memcpy(out->ids + out->total, h->h_ids + f0, sizeof(int32_t) * k);
+    std::memcpy(out->frames + out->total, h->h_frames + f0, sizeof(int32_t) * k);
+    std::memcpy(out->probs + out->total, h->h_probs + f0, sizeof(float) * k);
+    out->total += k;
+  }
+  return CREC_OK;
+}
+
+void free_all(crec_handle* h) {
+  for (auto& v : h->v) cudaFree(v.alloc);
+  for (auto& l : h->l) {
+    cudaFree(l.wimg);
+    cudaFree(l.colsum);
+    cudaFree(l.scale);
+    cudaFree(l.dbias);
+    cudaFree(l.dw8);
+    cudaFree(l.dwf);
+  }
+  cudaFree(h->in_table);
+  cudaFree(h->head_table);
+  if (h->pages_owned) cudaFree(h->page_mem);
+  cudaFree(h->d_pages);
+  cudaFree(h->d_lines);
+  cudaFree(h->d_mask);
+  cudaFree(h->d_frame0);
+  cudaFree(h->d_length);
+  cudaFree(h->d_frame_id);
+  cudaFree(h->d_frame_prob);
+  cudaFree(h->d_count);
+  cudaFree(h->d_ids);
+  cudaFree(h->d_frames);
+  cudaFree(h->d_probs);
+  cudaFree(h->d_err);
+  cudaFree(h->d_crops);
+  cudaFree(h->d_crops_in);
+  cudaFreeHost(h->h_lines);
+  cudaFreeHost(h->h_mask);
+  cudaFreeHost(h->h_frame0);
+  cudaFreeHost(h->h_length);
+  cudaFreeHost(h->h_count);
+  cudaFreeHost(h->h_ids);
+  cudaFreeHost(h->h_frames);
+  cudaFreeHost(h->h_probs);
+  cudaFreeHost(h->h_err);
+  if (h->stream) cudaStreamDestroy(h->stream);
+}
+
+int open_impl(crec_handle* h, const crec_config* c) {
+  h->cfg = *c;
+  if (c->precision != CREC_INT8 && c->precision != CREC_FP16) return set_error(h, CREC_E_INVALID, "precision");
+  if (c->max_lines <= 0 || c->max_width <= 0 || c->max_width > 4096 || c->max_width % 8)
+    return set_error(h, CREC_E_INVALID, "max_lines / max_width");
+  if (c->crop.height <= 0 || c->crop.height > 64 || c->crop.frame_px <= 0 || c->crop.width_step <= 0)
+    return set_error(h, CREC_E_INVALID, "crop rule");
+  h->int8 = c->precision == CREC_INT8;
+  h->eb = h->int8 ? 1 : 2;
+  h->device = c->device;
+  int count = 0;
+  CK(cudaGetDeviceCount(&count));
+  if (c->device < 0 || c->device >= count) return set_error(h, CREC_E_INVALID, "no CUDA device " + std::to_string(c->device));
+  CK(cudaSetDevice(c->device));
+  cudaDeviceProp prop{};
+  CK(cudaGetDeviceProperties(&prop, c->device));
+  if (prop.major != 10) return set_error(h, CREC_E_INVALID, std::string("this build runs on sm_100 (B200); device is ") + prop.name);
+  h->sms = prop.multiProcessorCount;
+  cudaDriverEntryPointQueryResult q{};
+  void* fn = nullptr;
+  CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (!fn || q != cudaDriverEntryPointSuccess) return set_error(h, CREC_E_CUDA, "cuTensorMapEncodeTiled is not available");
+  h->encode = reinterpret_cast<EncodeTiled>(fn);
+  CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+  int rc = read_model(h, static_cast<const uint8_t*>(c->model), c->model_bytes);
+  if (rc) return rc;
+  if (h->height != c->crop.height) return set_error(h, CREC_E_MODEL, "the model reads crops of another height");
+  if ((rc = plan_model(h))) return rc;
+  if (c->crop.width_step % (1 << h->max_shift)) return set_error(h, CREC_E_MODEL, "crop width step and the network's stride");
+  const long long per_line = c->max_width + h->gap;
+  h->max_cols = c->max_columns > 0 ? c->max_columns : static_cast<long long>(c->max_lines) * per_line + h->gap;
+  h->max_cols = round_up(h->max_cols, 128LL << h->max_shift);
+  for (size_t i = 0; i < h->l.size(); ++i)
+    if ((rc = setup_layer(h, i))) return rc;
+  if ((rc = alloc_values(h))) return rc;
+  if (h->int8) {
+    std::vector<uint8_t> t(256);
+    const Value& x = h->v[h->inp];
+    for (int p = 0; p < 256; ++p) t[p] = quantize_in(1.0f - static_cast<float>(p) / 255.0f, x.scale, x.zero);
+    if ((rc = upload(h, &h->in_table, t))) return rc;
+    std::vector<float> tab(256);
+    const Value& y = h->v[h->outv];
+    for (int q = 0; q < 256; ++q) tab[q] = static_cast<float>(q - y.zero) * y.scale;
+    if ((rc = upload(h, &h->head_table, tab))) return rc;
+  }
+  const int ml = c->max_lines;
+  const size_t frames = static_cast<size_t>(h->max_cols >> h->head_shift);
+  h->max_pages = std::max(1, c->max_pages);
+  if ((rc = dev_alloc(h, &h->d_pages, h->max_pages)) || (rc = dev_alloc(h, &h->d_lines, ml)) ||
+      (rc = dev_alloc(h, &h->d_mask, h->max_cols / 8)) || (rc = dev_alloc(h, &h->d_frame0, ml)) ||
+      (rc = dev_alloc(h, &h->d_length, ml)) || (rc = dev_alloc(h, &h->d_frame_id, frames)) ||
+      (rc = dev_alloc(h, &h->d_frame_prob, frames)) || (rc = dev_alloc(h, &h->d_count, ml)) ||
+      (rc = dev_alloc(h, &h->d_ids, frames)) || (rc = dev_alloc(h, &h->d_frames, frames)) ||
+      (rc = dev_alloc(h, &h->d_probs, frames)) || (rc = dev_alloc(h, &h->d_err, 1)))
+    return rc;
+  if ((rc = host_alloc(h, &h->h_lines, ml)) || (rc = host_alloc(h, &h->h_mask, h->max_cols / 8)) ||
+      (rc = host_alloc(h, &h->h_frame0, ml)) || (rc = host_alloc(h, &h->h_length, ml)) ||
+      (rc = host_alloc(h, &h->h_count, ml)) || (rc = host_alloc(h, &h->h_ids, frames)) ||
+      (rc = host_alloc(h, &h->h_frames, frames)) || (rc = host_alloc(h, &h->h_probs, frames)) ||
+      (rc = host_alloc(h, &h->h_err, 1)))
+    return rc;
+  const size_t crop_smem = ((h->height * c->max_width + 15) & ~15) + kMaxSrcRows * kStripCols +
+                           (h->height * kMaxTaps + 2 * h->height + 256 + 8) * 4;
+  CK(cudaFuncSetAttribute(crop_stem_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(crop_smem)));
+  CK(cudaFuncSetAttribute(crop_stem_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(crop_smem)));
+  return CREC_OK;
+}
+
+int pages_common(crec_handle* h, const crec_page* pages, int n) {
+  if (!h) return CREC_E_INVALID;
+  if (h->broken) return set_error(h, CREC_E_STICKY, "the GPU is broken for this process");
+  if (n < 0 || n > h->max_pages || (n > 0 && !pages)) return set_error(h, CREC_E_INVALID, "set_pages: page count");
+  for (int i = 0; i < n; ++i)
+    if (!pages[i].data || pages[i].width <= 0 || pages[i].height <= 0 || pages[i].stride < pages[i].width)
+      return set_error(h, CREC_E_INVALID, "set_pages: page " + std::to_string(i));
+  return CREC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int crec_width_bucket(int w) {
+  for (int b = 32;;) {
+    if (w <= b) return b;
+    if (b >= 2048) return (w + 7) / 8 * 8;
+    const int nb = (static_cast<int>(std::ceil(b * 1.3)) + 7) / 8 * 8;
+    b = std::min(2048, nb);
+  }
+}
+
+int crec_crop_region(const crec_box* box, const crec_crop_rule* r, double* region, int* width) {
+  if (!box || !r || !region || !width) return CREC_E_INVALID;
+  // carbon/src/lines.cpp:33-44: the same expressions, in the same order (built without contraction)
+  const double h = box->y1 - box->y0;
+  const double sy0 = box->y0 - r->pad_v * h, sy1 = box->y1 + r->pad_v * h;
+  const double scale = r->height / (sy1 - sy0);
+  const double w_src = (box->x1 - box->x0) + 2 * r->pad_h * h;
+  const int w = std::max(r->width_step, static_cast<int>(std::ceil(w_src * scale / r->width_step - 1e-6)) * r->width_step);
+  const double extra = (w / scale - w_src) / 2;
+  region[0] = box->x0 - r->pad_h * h - extra;
+  region[1] = sy0;
+  region[2] = box->x1 + r->pad_h * h + extra;
+  region[3] = sy1;
+  *width = w;
+  return CREC_OK;
+}
+
+int crec_open(const crec_config* config, crec_handle** out) {
+  if (!config || !out) return CREC_E_INVALID;
+  *out = nullptr;
+  auto* h = new (std::nothrow) crec_handle();
+  if (!h) return CREC_E_NOMEM;
+  const int rc = open_impl(h, config);
+  *out = h;  // the handle carries the error message even on failure; crec_close frees it
+  return rc;
+}
+
+int crec_close(crec_handle* h) {
+  if (!h) return CREC_OK;
+  cudaSetDevice(h->device);
+  if (h->stream) cudaStreamSynchronize(h->stream);
+  free_all(h);
+  delete h;
+  return CREC_OK;
+}
+
+const char* crec_last_error(const crec_handle* h) { return h ? h->error.c_str() : "no handle"; }
+int crec_is_broken(const crec_handle* h) { return h && h->broken ? 1 : 0; }
+void* crec_stream(crec_handle* h) { return h ? static_cast<void*>(h->stream) : nullptr; }
+
+int crec_set_pages(crec_handle* h, const crec_page* pages, int n, const crec_row_runs* rows) {
+  int rc = pages_common(h, pages, n);
+  if (rc) return rc;
+  CK(cudaSetDevice(h->device));
+  size_t need = 0;
+  for (int i = 0; i < n; ++i) need += (static_cast<size_t>(pages[i].height) * pages[i].width + 255) / 256 * 256;
+  if (!h->pages_owned) {
+    h->page_mem = nullptr;
+    h->page_cap = 0;
+    h->pages_owned = true;
+  }
+  if (need > h->page_cap) {
+    const size_t limit = h->cfg.max_page_bytes > 0 ? static_cast<size_t>(h->cfg.max_page_bytes)
+                                                   : static_cast<size_t>(h->max_pages) * 1700 * 2200;
+    if (need > std::max(limit, h->page_cap)) return set_error(h, CREC_E_RANGE, "set_pages: more page bytes than configured");
+    CK(cudaStreamSynchronize(h->stream));
+    cudaFree(h->page_mem);
+    h->page_mem = nullptr;
+    h->page_cap = 0;
+    CK(cudaMalloc(&h->page_mem, need));
+    h->page_cap = need;
+  }
+  h->pages.resize(n);
+  size_t at = 0;
+  for (int i = 0; i < n; ++i) {
+    const crec_page& pg = pages[i];
+    uint8_t* d = h->page_mem + at;
+    h->pages[i] = {d, pg.width, pg.height, static_cast<long long>(pg.width)};
+    if (rows && rows[i].count > 0 && rows[i].runs) {
+      for (int r = 0; r < rows[i].count; ++r) {
+        const int y0 = std::max(0, rows[i].runs[2 * r]), y1 = std::min(pg.height, rows[i].runs[2 * r + 1]);
+        if (y1 <= y0) continue;
+        CK(cudaMemcpy2DAsync(d + static_cast<size_t>(y0) * pg.width, pg.width, pg.data + y0 * pg.stride, pg.stride,
+                             pg.width, y1 - y0, cudaMemcpyHostToDevice, h->stream));
+      }
+    } else {
+      CK(cudaMemcpy2DAsync(d, pg.width, pg.data, pg.stride, pg.width, pg.height, cudaMemcpyHostToDevice, h->stream));
+    }
+    at += (static_cast<size_t>(pg.height) * pg.width + 255) / 256 * 256;
+  }
+  if (n > 0) CK(cudaMemcpyAsync(h->d_pages, h->pages.data(), sizeof(PageDesc) * n, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaStreamSynchronize(h->stream));  // the caller may reuse its pages now
+  return CREC_OK;
+}
+
+int crec_prefetch_pages(crec_handle* h, const crec_page* pages, int n, const crec_row_runs* rows) {
+  (void)rows;
+  return pages_common(h, pages, n);
+}
+
+int crec_set_pages_device(crec_handle* h, const crec_page* pages, int n) {
+  int rc = pages_common(h, pages, n);
+  if (rc) return rc;
+  CK(cudaSetDevice(h->device));
+  h->pages.resize(n);
+  for (int i = 0; i < n; ++i) h->pages[i] = {pages[i].data, pages[i].width, pages[i].height, static_cast<long long>(pages[i].stride)};
+  if (n > 0) CK(cudaMemcpyAsync(h->d_pages, h->pages.data(), sizeof(PageDesc) * n, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return CREC_OK;
+}
+
+int crec_recognize(crec_handle* h, const int32_t* page_of, const crec_box* boxes, int n, int bw, crec_lines* out) {
+  if (!h) return CREC_E_INVALID;
+  if (h->broken) return set_error(h, CREC_E_STICKY, "the GPU is broken for this process");
+  if (n < 0 || n > h->cfg.max_lines) return set_error(h, CREC_E_RANGE, "recognize: more lines than max_lines");
+  if (bw <= 0 || bw > h->cfg.max_width || bw % h->cfg.crop.width_step || bw % (1 << h->max_shift))
+    return set_error(h, CREC_E_INVALID, "recognize: bucket width " + std::to_string(bw));
+  if (!out || (n > 0 && (!page_of || !boxes || !out->counts || !out->lengths || !out->offsets || !out->ids ||
+                          !out->frames || !out->probs)))
+    return set_error(h, CREC_E_INVALID, "recognize: null arrays");
+  out->total = 0;
+  if (n == 0) return CREC_OK;
+  CK(cudaSetDevice(h->device));
+  std::vector<int> bws(n, bw);
+  return run_lines(h, page_of, boxes, bws.data(), n, out, 0);
+}
+
+int crec_recognize_lines(crec_handle* h, const int32_t* page_of, const crec_box* boxes, const int32_t* bw, int n,
+                         crec_lines* out) {
+  if (!h) return CREC_E_INVALID;
+  if (h->broken) return set_error(h, CREC_E_STICKY, "the GPU is broken for this process");
+  if (n < 0 || !out || (n > 0 && (!page_of || !boxes)))
+    return set_error(h, CREC_E_INVALID, "recognize_lines: arguments");
+  out->total = 0;
+  if (n == 0) return CREC_OK;
+  CK(cudaSetDevice(h->device));
+  std::vector<int> bws(n);
+  for (int i = 0; i < n; ++i) {
+    if (bw) {
+      bws[i] = bw[i];
+    } else {
+      double reg[4];
+      int w = 0;
+      crec_crop_region(&boxes[i], &h->cfg.crop, reg, &w);
+      bws[i] = crec_width_bucket(w);
+    }
+    if (bws[i] <= 0 || bws[i] > h->cfg.max_width || bws[i] % h->cfg.crop.width_step || bws[i] % (1 << h->max_shift))
+      return set_error(h, CREC_E_INVALID, "recognize_lines: line " + std::to_string(i) + " bucket width " + std::to_string(bws[i]));
+  }
+  // runs: as many lines as fit the configured lines and columns
+  for (int a = 0; a < n;) {
+    long long cols = h->gap;
+    int b = a;
+    while (b < n && b - a < h->cfg.max_lines) {
+      const long long next = cols + bws[b] + h->gap;
+      if (round_up(next, 128LL << h->max_shift) > h->max_cols) break;
+      cols = next;
+      ++b;
+    }
+    if (b == a) return set_error(h, CREC_E_RANGE, "recognize_lines: a line wider than the configured columns");
+    const int rc = run_lines(h, page_of + a, boxes + a, bws.data() + a, b - a, out, a);
+    if (rc) return rc;
+    a = b;
+  }
+  return CREC_OK;
+}
+
+int crec_recognize_crops(crec_handle* h, const uint8_t* crops, int pitch, const int32_t* widths, const int32_t* bw,
+                         int n, crec_lines* out) {
+  if (!h) return CREC_E_INVALID;
+  if (h->broken) return set_error(h, CREC_E_STICKY, "the GPU is broken for this process");
+  if (n < 0 || n > h->cfg.max_lines || !out || (n > 0 && (!crops || !widths || !bw)) || pitch <= 0 ||
+      pitch > h->cfg.max_width)
+    return set_error(h, CREC_E_INVALID, "recognize_crops: arguments");
+  out->total = 0;
+  if (n == 0) return CREC_OK;
+  CK(cudaSetDevice(h->device));
+  for (int i = 0; i < n; ++i)
+    if (bw[i] <= 0 || bw[i] > pitch || bw[i] % h->cfg.crop.width_step || bw[i] % (1 << h->max_shift))
+      return set_error(h, CREC_E_INVALID, "recognize_crops: line " + std::to_string(i) + " bucket width " + std::to_string(bw[i]));
+  if (!h->d_crops_in) CK(cudaMalloc(&h->d_crops_in, static_cast<size_t>(h->cfg.max_lines) * h->height * h->cfg.max_width));
+  std::vector<int> bws(bw, bw + n);
+  return run_lines(h, nullptr, nullptr, bws.data(), n, out, 0, crops, pitch, widths);
+}
+
+int crec_debug_crops(crec_handle* h, uint8_t* out, int pitch) {
+  if (!h || pitch <= 0) return CREC_E_INVALID;
+  CK(cudaSetDevice(h->device));
+  if (!out) {  // arm: the runs from now on keep their finished crops
+    cudaFree(h->d_crops);
+    h->d_crops = nullptr;
+    CK(cudaMalloc(&h->d_crops, static_cast<size_t>(h->cfg.max_lines) * h->height * pitch));
+    CK(cudaMemset(h->d_crops, 0, static_cast<size_t>(h->cfg.max_lines) * h->height * pitch));
+    h->crops_pitch = pitch;
+    return CREC_OK;
+  }
+  if (!h->d_crops || h->crops_pitch != pitch) return set_error(h, CREC_E_INVALID, "debug crops not armed at this pitch");
+  CK(cudaMemcpy(out, h->d_crops, static_cast<size_t>(h->last_n) * h->height * pitch, cudaMemcpyDeviceToHost));
+  return CREC_OK;
+}
+
+int crec_debug_value(crec_handle* h, int value, void* out, int64_t capacity) {
+  if (!h || !out || value < 0 || value >= static_cast<int>(h->v.size())) return CREC_E_INVALID;
+  const Value& v = h->v[value];
+  if (v.h < 0) return set_error(h, CREC_E_INVALID, "value not computed");
+  const Value& pv = h->v[v.phys];
+  if (!pv.real) return set_error(h, CREC_E_INVALID, "value not kept in memory (the input or the head's output)");
+  CK(cudaSetDevice(h->device));
+  CK(cudaStreamSynchronize(h->stream));
+  const size_t px = static_cast<size_t>(v.c) * h->eb;
+  size_t need = 0;
+  for (int i = 0; i < h->last_n; ++i) need += static_cast<size_t>(v.h) * (h->last_bw[i] >> v.shift) * px;
+  if (static_cast<int64_t>(need) > capacity) return set_error(h, CREC_E_RANGE, "debug_value: capacity");
+  std::vector<uint8_t> row(static_cast<size_t>(pv.pitch));
+  uint8_t* o = static_cast<uint8_t*>(out);
+  for (int i = 0; i < h->last_n; ++i) {
+    const long long c0 = h->last_seg[i] >> v.shift, w = h->last_bw[i] >> v.shift;
+    for (int y = 0; y < v.h; ++y) {
+      CK(cudaMemcpy(row.data(), pv.base + static_cast<long long>(y + pv.ph) * pv.pitch, row.size(), cudaMemcpyDeviceToHost));
+      for (long long x = 0; x < w; ++x) {
+        const long long pcol = x + c0;  // logical column; the physical one for an upsampling read in place
+        const long long src = (pcol >> v.extra) * pv.cp * h->eb;
+        std::memcpy(o, row.data() + src, px);
+        o += px;
+      }
+    }
+  }
+  return CREC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,160 @@
+/* carbon_rec: Carbon-OCR's line recognition (crop, the recognizer, greedy CTC) on B200
+ * (sm_100a), behind a C ABI.
+ *
+ * These entry points are what a device behind the reference's recognizer-backend interface,
+ * carbon::PipelineModels (carbon/include/carbon/pipeline.h:94-142 of the reference), binds:
+ *
+ *   crec_open / crec_close        the device's construction from a set's recognizer file and
+ *                                 the crop rule (cuda_pipeline_models, pipeline.h:199-200;
+ *                                 CudaModels, carbon/src/cuda/pipeline_cuda.cpp:146)
+ *   crec_set_pages                PipelineModels::set_pages (pipeline.h:120)
+ *   crec_prefetch_pages           PipelineModels::prefetch_pages (pipeline.h:124)
+ *   crec_recognize                PipelineModels::recognize (pipeline.h:131-132)
+ *   crec_is_broken                PipelineModels::broken (pipeline.h:116)
+ *   crec_width_bucket             carbon::width_bucket (carbon/src/engine.cpp:669-675)
+ *   crec_crop_region              carbon::crop_region (carbon/src/lines.cpp:33)
+ *   crec_recognize_lines          the recognize stage's bucketing and runs
+ *                                 (carbon/src/pipeline.cpp:536-603) done on the device side:
+ *                                 any number of lines in as few launches as fit
+ *
+ * Plain pointers and sizes only.  Every call returns a status (CREC_OK or an error code);
+ * no exception crosses the ABI; crec_last_error() gives the message.  A handle drives one
+ * GPU and is not safe to call from two threads at once (the reference's recognize stage
+ * calls its device from one thread, pipeline.h:92-93); open one handle per GPU.
+ */
+#ifndef CARBON_REC_H_
+#define CARBON_REC_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CREC_API __attribute__((visibility("default")))
+#else
+#define CREC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CREC_OK 0
+#define CREC_E_INVALID 1 /* an argument is out of its range */
+#define CREC_E_NOMEM 2   /* device or pinned host memory could not be had */
+#define CREC_E_CUDA 3    /* a CUDA call failed; the handle is still usable */
+#define CREC_E_STICKY 4  /* a sticky CUDA error: this process can use the GPU no more (crec_is_broken) */
+#define CREC_E_TIMEOUT 5 /* a kernel's bounded wait ran out; the run's results are not valid */
+#define CREC_E_MODEL 6   /* the model blob is not one this build runs */
+#define CREC_E_RANGE 7   /* a crop wider than its batch, or more lines or columns than configured */
+
+#define CREC_INT8 0 /* the Q/DQ recognizer: int8 weights, uint8 activations, int32 sums */
+#define CREC_FP16 1 /* the float recognizer: float16 weights and activations, float32 sums */
+
+typedef struct crec_handle crec_handle;
+
+/* carbon::CropRule (carbon/include/carbon/lines.h:23-37). */
+typedef struct crec_crop_rule {
+  int height;     /* px; 32 */
+  int width_step; /* 8 */
+  int frame_px;   /* 4 */
+  double pad_v;   /* 0.2 */
+  double pad_h;   /* 0.3 */
+  int flip_margin;     /* 48; 0: never flip */
+  int flip_needs_dark; /* 1 */
+} crec_crop_rule;
+
+typedef struct crec_config {
+  int precision;   /* CREC_INT8 or CREC_FP16 */
+  int device;      /* CUDA device ordinal */
+  int max_lines;   /* lines one recognize call may hold (the pipeline's line_batch, or more) */
+  int max_width;   /* the widest bucket, px (the reference's ladder ends at 2048) */
+  int64_t max_columns; /* columns of crop width (plus gaps) one run holds on the device; 0: from the two above */
+  int max_pages;       /* pages a set_pages call may hold */
+  int64_t max_page_bytes; /* bytes of pages held on the device; 0: max_pages letter pages at 200 dpi */
+  crec_crop_rule crop;
+  const void* model;   /* the recognizer as a "CRECMDL1" blob (carbon_rec/netdef.py): the Q/DQ file's for
+                          CREC_INT8, the float file's for CREC_FP16 (its weights rounded to float16) */
+  size_t model_bytes;
+} crec_config;
+
+/* carbon::GrayView (lines.h:56-60): a grayscale page, paper 255, rows `stride` bytes apart. */
+typedef struct crec_page {
+  const uint8_t* data;
+  int width, height;
+  int64_t stride;
+} crec_page;
+
+/* carbon::RowRuns (pipeline.h:88-90): the rows [runs[2i], runs[2i+1]) a page's crops read; count 0: all. */
+typedef struct crec_row_runs {
+  const int32_t* runs;
+  int count;
+} crec_row_runs;
+
+/* carbon::LineBox (lines.h:40-42): page pixels, x right, y down. */
+typedef struct crec_box {
+  double x0, y0, x1, y1;
+} crec_box;
+
+/* A run's decodings (carbon::CtcLine, lines.h:107-112), in arrays the caller owns. */
+typedef struct crec_lines {
+  int32_t* counts;  /* [n] characters of line i */
+  int32_t* lengths; /* [n] frames read: min(frames, crop width / frame_px) */
+  int32_t* offsets; /* [n] where line i's characters start in ids, frames and probs */
+  int32_t* ids;     /* class ids, blanks dropped and repeats collapsed */
+  int32_t* frames;  /* each character's first frame */
+  float* probs;     /* each character's highest softmax probability over its run */
+  int64_t capacity; /* room in ids, frames and probs (sum over lines of bw / frame_px always suffices) */
+  int64_t total;    /* characters written */
+} crec_lines;
+
+CREC_API int crec_open(const crec_config* config, crec_handle** out);
+CREC_API int crec_close(crec_handle* h);
+CREC_API const char* crec_last_error(const crec_handle* h);
+/* Whether a sticky error left the GPU unusable for this process (PipelineModels::broken). */
+CREC_API int crec_is_broken(const crec_handle* h);
+
+/* The pages the recognize calls that follow crop from, copied to the GPU (only rows[i]'s runs
+ * where given). The caller may reuse its pages once the call returns. */
+CREC_API int crec_set_pages(crec_handle* h, const crec_page* pages, int n, const crec_row_runs* rows);
+/* The next group's pages, given while the current group is read. This build uploads at
+ * set_pages; the call validates its arguments and returns. */
+CREC_API int crec_prefetch_pages(crec_handle* h, const crec_page* pages, int n, const crec_row_runs* rows);
+/* Pages already in this handle's GPU memory (data are device pointers): used in place. */
+CREC_API int crec_set_pages_device(crec_handle* h, const crec_page* pages, int n);
+
+/* PipelineModels::recognize: the lines boxes[i] of page page_of[i], cropped at bucket width bw
+ * (a multiple of the crop rule's width step), decoded; lengths[i] = min(bw / frame_px, crop
+ * width / frame_px). CREC_E_RANGE if a crop is wider than bw. */
+CREC_API int crec_recognize(crec_handle* h, const int32_t* page_of, const crec_box* boxes, int n, int bw, crec_lines* out);
+/* Any number of lines, each at its own bucket width (bw[i]; null: crec_width_bucket of its crop
+ * width), in as few device runs as the configured columns allow; results as crec_recognize. */
+CREC_API int crec_recognize_lines(crec_handle* h, const int32_t* page_of, const crec_box* boxes, const int32_t* bw, int n,
+                         crec_lines* out);
+
+/* Crops given ready ([n][crop height][pitch] bytes, line i's first bw[i] columns already finished
+ * and padded, as crop_lines gives them; widths[i] its own crop width): the recognizer and CTC
+ * on them, as the reference's CPU device runs its session on crop_lines' output
+ * (carbon/src/pipeline.cpp:138-162).  At most max_lines; pitch at most max_width. */
+CREC_API int crec_recognize_crops(crec_handle* h, const uint8_t* crops, int pitch, const int32_t* widths, const int32_t* bw,
+                         int n, crec_lines* out);
+
+CREC_API int crec_width_bucket(int crop_width);
+/* carbon::crop_region: the page rectangle a box's crop resamples (region[4]: x0, y0, x1, y1) and
+ * the crop's width. */
+CREC_API int crec_crop_region(const crec_box* box, const crec_crop_rule* rule, double* region, int* width);
+
+/* The CUDA stream (a cudaStream_t) the handle's work runs on, for device-side timing. */
+CREC_API void* crec_stream(crec_handle* h);
+
+/* Test hooks: the last run's finished crops ([n][height][pitch] bytes, each line's first
+ * bucket-width columns), and a network tensor of the last run (value index of the model
+ * blob; each line's NHWC values without borders, lines one after another: uint8 for
+ * CREC_INT8, float16 for CREC_FP16). */
+CREC_API int crec_debug_crops(crec_handle* h, uint8_t* out, int pitch);
+CREC_API int crec_debug_value(crec_handle* h, int value, void* out, int64_t capacity_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CARBON_REC_H_ */
