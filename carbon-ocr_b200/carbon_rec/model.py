@@ -262,6 +262,32 @@ def synthetic_crops(rng: np.random.Generator, n: int, wmin: int = 96, wmax: int 
     return out
 
 
+MINI_BACKBONE = [
+    ("stem", 1, 8, 3, 3, 2, 2, (1, 1, 1, 1), True),
+    ("s1a", 8, 12, 3, 3, 2, 2, (1, 1, 1, 1), True),
+    ("s1b", 12, 12, 3, 3, 1, 1, (1, 1, 1, 1), True),
+    ("s2a", 12, 16, 3, 3, 2, 2, (1, 1, 1, 1), True),
+    ("s3a", 16, 20, 3, 3, 2, 1, (1, 1, 1, 1), True),
+    ("collapse", 20, 24, 2, 3, 1, 1, (0, 1, 0, 1), True),
+]
+
+
+def make_mini(seed: int = 4, calib_lines: int = 16):
+    """A miniature recognizer of the same family with channel counts that are not multiples of
+    16 (8, 12, 16, 20, 24; mixing 24 -> 48 -> 24; 11 classes): (weights, quant, fp32, int8)."""
+    global BACKBONE, MIX_C, MIX_HIDDEN
+    saved = BACKBONE, MIX_C, MIX_HIDDEN
+    BACKBONE, MIX_C, MIX_HIDDEN = MINI_BACKBONE, 24, 48
+    try:
+        w = make_weights(seed, classes=11)
+        rng = np.random.default_rng(2000 + seed)
+        crops = synthetic_crops(rng, calib_lines, 128, 128)
+        quant = calibrate(w, np.stack(crops))
+        return w, quant, build_onnx(w, None), build_onnx(w, quant)
+    finally:
+        BACKBONE, MIX_C, MIX_HIDDEN = saved
+
+
 def make_rec_latin(seed: int = 0, calib_lines: int = 24):
     """(weights, quant params, fp32 ONNX model, int8 ONNX model) of rec-latin at `seed`."""
     w = make_weights(seed)

@@ -25,7 +25,8 @@ _NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA
 # every entry point include/carbon_rec.h declares
 EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec_set_pages", "crec_prefetch_pages",
            "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_width_bucket", "crec_crop_region",
-           "crec_stream", "crec_debug_crops", "crec_debug_value"]
+           "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats",
+           "crec_profile"]
 
 
 class CrecError(RuntimeError):
@@ -64,6 +65,14 @@ class Box(C.Structure):
     _fields_ = [("x0", C.c_double), ("y0", C.c_double), ("x1", C.c_double), ("y1", C.c_double)]
 
 
+class Stats(C.Structure):
+    _fields_ = [("runs", C.c_int64), ("launches", C.c_int64), ("h2d_bytes", C.c_int64), ("d2h_bytes", C.c_int64)]
+
+
+class ProfileEntry(C.Structure):
+    _fields_ = [("kernel", C.c_char_p), ("launches", C.c_int64), ("ms", C.c_double), ("ops", C.c_double)]
+
+
 class Lines(C.Structure):
     _fields_ = [("counts", C.c_void_p), ("lengths", C.c_void_p), ("offsets", C.c_void_p), ("ids", C.c_void_p),
                 ("frames", C.c_void_p), ("probs", C.c_void_p), ("capacity", C.c_int64), ("total", C.c_int64)]
@@ -97,6 +106,9 @@ def lib() -> C.CDLL:
         L.crec_stream.restype = p
         L.crec_debug_crops.argtypes = [p, p, i]
         L.crec_debug_value.argtypes = [p, i, p, i64]
+        L.crec_debug_logits.argtypes = [p, p, i64]
+        L.crec_last_stats.argtypes = [p, C.POINTER(Stats)]
+        L.crec_profile.argtypes = [p, i, C.POINTER(ProfileEntry), i]
         _lib = L
     return _lib
 
@@ -112,6 +124,31 @@ def crop_region(box, rule: CropRule | None = None):
     w = C.c_int()
     lib().crec_crop_region(C.byref(b), C.byref(rule), reg.ctypes.data, C.byref(w))
     return reg, w.value
+
+
+def rows_read(boxes, height: int, rule: CropRule | None = None):
+    """The rows a page's crops read, as [first, last) runs (carbon/src/pipeline.cpp:489-510): each
+    line's crop region widened by twice the resampler's support and two rows, clipped to the
+    page, sorted, runs closer than 16 rows joined."""
+    import math
+    rule = rule or CropRule.default()
+    runs = []
+    for b in np.asarray(boxes, np.float64).reshape(-1, 4):
+        reg, _ = crop_region(b, rule)
+        scale = max(1.0, (reg[3] - reg[1]) / rule.height)
+        m = int(math.ceil(2 * scale)) + 2
+        y0 = max(0, int(math.floor(reg[1])) - m)
+        y1 = min(height, int(math.ceil(reg[3])) + m)
+        if y1 > y0:
+            runs.append((y0, y1))
+    runs.sort()
+    merged = []
+    for r in runs:
+        if merged and r[0] <= merged[-1][1] + 16:
+            merged[-1] = (merged[-1][0], max(merged[-1][1], r[1]))
+        else:
+            merged.append(r)
+    return merged
 
 
 @dataclass
@@ -251,6 +288,31 @@ class RecDevice:
         out = np.zeros((n, self.crop.height, pitch), np.uint8)
         self._check(lib().crec_debug_crops(self._h, out.ctypes.data, int(pitch)))
         return out
+
+    def last_stats(self) -> dict:
+        st = Stats()
+        self._check(lib().crec_last_stats(self._h, C.byref(st)))
+        return {"runs": st.runs, "launches": st.launches, "h2d_bytes": st.h2d_bytes, "d2h_bytes": st.d2h_bytes}
+
+    def profile(self, enable: int = -1) -> dict:
+        """Per-kernel totals {name: (launches, ms, ops)} since profiling was (re)started; enable 1 (re)starts."""
+        ent = (ProfileEntry * 8)()
+        n = lib().crec_profile(self._h, int(enable), ent, 8)
+        return {ent[i].kernel.decode(): (ent[i].launches, ent[i].ms, ent[i].ops) for i in range(max(n, 0))}
+
+    def arm_logits(self) -> None:
+        self._check(lib().crec_debug_logits(self._h, None, 0))
+
+    def logits(self, bws, classes: int) -> list:
+        """The last run's logits, a [classes, bw / frame_px] array per line (bucket widths bws)."""
+        t = [int(b) // self.crop.frame_px for b in bws]
+        out = np.zeros(sum(t) * classes, np.float32)
+        self._check(lib().crec_debug_logits(self._h, out.ctypes.data, out.size))
+        res, at = [], 0
+        for k in t:
+            res.append(out[at:at + classes * k].reshape(classes, k))
+            at += classes * k
+        return res
 
     def value(self, index: int, nbytes: int, dtype=np.uint8) -> np.ndarray:
         out = np.zeros(nbytes, np.uint8)

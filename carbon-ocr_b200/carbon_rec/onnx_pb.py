@@ -144,7 +144,9 @@ class Model:
 
 
 def _tensor_bytes(name: str, a: np.ndarray) -> bytes:
-    a = np.ascontiguousarray(a)
+    a = np.asarray(a)
+    if not a.flags.c_contiguous:
+        a = a.copy(order="C")  # (np.ascontiguousarray would make a 0-d scalar 1-d)
     out = b"".join(_int(1, int(d)) for d in a.shape)
     out += _int(2, CODE_OF[a.dtype])
     out += _str(8, name)

@@ -130,30 +130,42 @@ struct crec_handle {
   int max_pages = 0;
   // run buffers
   LineDesc* d_lines = nullptr;
-  LineDesc* h_lines = nullptr;  // pinned
   uint8_t* d_mask = nullptr;
-  uint8_t* h_mask = nullptr;  // pinned
   int* d_frame0 = nullptr;
   int* d_length = nullptr;
-  int* h_frame0 = nullptr;  // pinned [max_lines]
-  int* h_length = nullptr;
+  // a call's pinned staging (grown on demand): line descriptors, masks, frame starts, lengths, results
+  LineDesc* hs_lines = nullptr;
+  int* hs_frame0 = nullptr;
+  int* hs_length = nullptr;
+  int32_t* hs_count = nullptr;
+  uint8_t* hs_mask = nullptr;
+  int32_t* hs_ids = nullptr;
+  int32_t* hs_frames = nullptr;
+  float* hs_probs = nullptr;
+  size_t cap_lines = 0, cap_frame0 = 0, cap_length = 0, cap_count = 0, cap_mask = 0, cap_ids = 0, cap_frames = 0,
+         cap_probs = 0;
   int32_t* d_frame_id = nullptr;
   float* d_frame_prob = nullptr;
   int32_t* d_count = nullptr;
   int32_t* d_ids = nullptr;
   int32_t* d_frames = nullptr;
   float* d_probs = nullptr;
-  int32_t* h_count = nullptr;  // pinned
-  int32_t* h_ids = nullptr;
-  int32_t* h_frames = nullptr;
-  float* h_probs = nullptr;
   int* d_err = nullptr;
   int* h_err = nullptr;
   uint8_t* d_crops = nullptr;  // debug copy of the finished crops
   int crops_pitch = 0;
+  float* d_logits = nullptr;  // test hook: the last run's logits, [columns at the head's resolution][classes]
   uint8_t* d_crops_in = nullptr;  // ready crops given by crec_recognize_crops
   int crops_in_pitch = 0;
   const uint8_t* run_crops = nullptr;  // this run's ready crops on the device, or null
+  // the last call's statistics, and the optional per-launch profile (CUDA events on the stream)
+  long long st_runs = 0, st_launches = 0, st_h2d = 0, st_d2h = 0;
+  bool profile = false;
+  std::vector<cudaEvent_t> ev_pool;  // pairs
+  std::vector<int> ev_kind;          // a pair's kernel kind
+  size_t ev_used = 0;
+  double prof_ms[8] = {0}, prof_ops[8] = {0};
+  long long prof_count[8] = {0};
   // the last run
   int last_n = 0;
   long long last_cols = 0;
@@ -438,7 +450,6 @@ int setup_layer(crec_handle* h, size_t li) {
     const uint32_t codes = h->int8 ? 128u * round16(l.cout) : 0u;
     l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + 128;
     if (l.smem > 232448) return set_error(h, CREC_E_MODEL, "the head does not fit in shared memory");
-    if (l.last_steps != 4) return set_error(h, CREC_E_MODEL, "the head's channels must fill 128-byte blocks");
   } else {
     l.nt = std::min(256, round16(l.cout));
     l.n_tiles = (y.cp + l.nt - 1) / l.nt;
@@ -478,6 +489,67 @@ int encode_map(crec_handle* h, CUtensorMap* m, const void* base, uint64_t d0, ui
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(h, CREC_E_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
   return CREC_OK;
+}
+
+// Kernel kinds of the profile: 0 crop+stem, 1 dense convolutions (tcgen05), 2 depthwise, 3 head+CTC, 4 collapse.
+enum ProfKind { kProfCrop = 0, kProfConv = 1, kProfDw = 2, kProfHead = 3, kProfCollapse = 4 };
+
+// Brackets one launch with a pair of events when profiling (the pair's times are read after the call's sync).
+struct ProfScope {
+  crec_handle* h;
+  int kind;
+  cudaEvent_t end = nullptr;
+  ProfScope(crec_handle* hh, int k) : h(hh), kind(k) {
+    ++h->st_launches;
+    if (!h->profile) return;
+    if (h->ev_used + 2 > h->ev_pool.size()) {
+      for (int i = 0; i < 64; ++i) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        h->ev_pool.push_back(e);
+      }
+      h->ev_kind.resize(h->ev_pool.size() / 2);
+    }
+    cudaEventRecord(h->ev_pool[h->ev_used], h->stream);
+    end = h->ev_pool[h->ev_used + 1];
+    h->ev_kind[h->ev_used / 2] = k;
+    h->ev_used += 2;
+  }
+  ~ProfScope() {
+    if (end) cudaEventRecord(end, h->stream);
+  }
+};
+
+void collect_profile(crec_handle* h) {
+  for (size_t i = 0; i + 1 < h->ev_used; i += 2) {
+    float ms = 0;
+    if (cudaEventElapsedTime(&ms, h->ev_pool[i], h->ev_pool[i + 1]) == cudaSuccess) {
+      h->prof_ms[h->ev_kind[i / 2]] += ms;
+      h->prof_count[h->ev_kind[i / 2]] += 1;
+    }
+  }
+  h->ev_used = 0;
+}
+
+// Algorithmic work of a run, by kernel kind: multiply-adds x 2 over the lines' own columns (gaps
+// excluded; padded channels and K excluded), as the roofline counts it.
+void add_run_ops(crec_handle* h, const int* bw, int a, int b) {
+  if (!h->profile) return;
+  long long width = 0;
+  for (int i = a; i < b; ++i) width += bw[i];
+  for (size_t li = 0; li < h->l.size(); ++li) {
+    const Layer& l = h->l[li];
+    if (l.kind == kKindResize) continue;
+    const Value& y = h->v[l.out];
+    const double pixels = static_cast<double>(y.h) * static_cast<double>(width >> y.shift);
+    const double taps = l.kh * l.kw;
+    if (l.kind == kKindDw) {
+      h->prof_ops[kProfDw] += 2.0 * pixels * taps * l.cout;
+    } else {
+      const int kind = li == 0 ? kProfCrop : li + 1 == h->l.size() ? kProfHead : kProfConv;
+      h->prof_ops[kind] += 2.0 * pixels * taps * l.cin * l.cout;
+    }
+  }
 }
 
 // Launches every layer for the lines laid out in h_lines (already on the device), `cols` input columns.
@@ -523,6 +595,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     const int maxbw = h->cfg.max_width;
     const size_t smem = ((h->height * maxbw + 15) & ~15) + kMaxSrcRows * kStripCols +
                         (h->height * kMaxTaps + 2 * h->height + 256 + 8) * 4;
+    ProfScope prof(h, kProfCrop);
     if (h->int8)
       crop_stem_kernel<true><<<n, kCropThreads, smem, s>>>(p);
     else
@@ -545,6 +618,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       if (rc) return rc;
       p.wimg = l.wimg;
       p.nkb = l.nkb;
+      p.last_steps = l.last_steps;
       p.classes = l.cout;
       p.nchunk = l.nchunk;
       p.chunks = l.chunks;
@@ -563,8 +637,10 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.out_shift = y.shift;
       p.frame_id = h->d_frame_id;
       p.frame_prob = h->d_frame_prob;
+      p.logits = h->d_logits;
       p.err = h->d_err;
       const int grid = std::min(p.num_tiles, h->sms);
+      ProfScope prof(h, kProfHead);
       if (h->int8) {
         CK(cudaFuncSetAttribute(head_ctc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
         head_ctc_kernel<true><<<grid, kHeadThreads, l.smem, s>>>(p);
@@ -605,6 +681,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.out_shift = y.shift;
       const long long total = static_cast<long long>(oh) * ow * (y.cp / 16);
       const int grid = static_cast<int>((total + 255) / 256);
+      ProfScope prof(h, kProfDw);
       if (h->int8)
         dw_kernel<true><<<grid, 256, 0, s>>>(p);
       else
@@ -664,6 +741,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.out_shift = y.shift;
     p.err = h->d_err;
     const int grid = std::min(p.num_tiles, h->sms);
+    ProfScope prof(h, kProfConv);
     if (h->int8) {
       CK(cudaFuncSetAttribute(conv_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
       conv_gemm_kernel<true><<<grid, kConvThreads, l.smem, s>>>(p);
@@ -683,109 +761,180 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
   c.ids = h->d_ids;
   c.frames = h->d_frames;
   c.probs = h->d_probs;
-  collapse_kernel<<<(n + 127) / 128, 128, 0, s>>>(c);
+  {
+    ProfScope prof(h, kProfCollapse);
+    collapse_kernel<<<(n + 127) / 128, 128, 0, s>>>(c);
+  }
   CK(cudaGetLastError());
   return CREC_OK;
 }
 
-// One device run over lines [0, n) with bucket widths bw[i]: lay out, launch, fetch, pack into out
-// starting at out->total.
-int run_lines(crec_handle* h, const int32_t* page_of, const crec_box* boxes, const int* bw, int n, crec_lines* out,
-              int line0, const uint8_t* crops = nullptr, int crops_pitch = 0, const int32_t* widths = nullptr) {
+// Host staging for one call (pinned, grown on demand, never shrunk): each run of a call has its
+// own slices, so every run's copies and launches are queued at once and the call syncs once.
+template <class T>
+int grow_pinned(crec_handle* h, T** p, size_t* cap, size_t need) {
+  if (need <= *cap) return CREC_OK;
+  const size_t n = std::max(need, *cap * 2);
+  cudaFreeHost(*p);
+  *p = nullptr;
+  *cap = 0;
+  CK(cudaHostAlloc(reinterpret_cast<void**>(p), n * sizeof(T), cudaHostAllocDefault));
+  *cap = n;
+  return CREC_OK;
+}
+
+struct Source {  // where a call's lines come from
+  const int32_t* page_of = nullptr;
+  const crec_box* boxes = nullptr;
+  const uint8_t* crops = nullptr;  // ready crops, [n][height][pitch]
+  int pitch = 0;
+  const int32_t* widths = nullptr;
+};
+
+// Lays out lines [a, b) of a call as one run (its LineDescs, mask, frame starts and lengths in
+// the call's staging at the given offsets); returns the run's input columns in *cols.
+int layout_run(crec_handle* h, const Source& src, const int* bw, int a, int b, size_t mask_off, long long* cols_out) {
   const crec_crop_rule& rule = h->cfg.crop;
   long long seg = h->gap;
-  h->last_seg.resize(n);
-  h->last_bw.resize(n);
-  h->run_crops = nullptr;
-  for (int i = 0; i < n; ++i) {
+  for (int i = a; i < b; ++i) {
+    LineDesc& d = h->hs_lines[i];
     double reg[4] = {0, 0, 1, 1};
     int width = 0;
-    if (crops) {
-      width = widths[i];
-      if (width <= 0 || width > bw[i] || bw[i] > crops_pitch)
-        return set_error(h, CREC_E_RANGE, "recognize_crops: line " + std::to_string(line0 + i) + " width " +
+    if (src.crops) {
+      width = src.widths[i];
+      if (width <= 0 || width > bw[i] || bw[i] > src.pitch)
+        return set_error(h, CREC_E_RANGE, "recognize_crops: line " + std::to_string(i) + " width " +
                                               std::to_string(width) + ", bucket " + std::to_string(bw[i]));
-      LineDesc& d = h->h_lines[i];
-      d.x0 = d.y0 = 0;
-      d.x1 = d.y1 = 1;
       d.page = 0;
-      d.width = width;
-      d.bw = bw[i];
-      d.seg = static_cast<int>(seg);
-      h->last_seg[i] = static_cast<int>(seg);
-      h->last_bw[i] = bw[i];
-      h->h_frame0[i] = static_cast<int>(seg >> h->head_shift);
-      h->h_length[i] = std::min(bw[i] >> h->head_shift, width / rule.frame_px);
-      seg += bw[i] + h->gap;
-      continue;
+    } else {
+      crec_crop_region(&src.boxes[i], &rule, reg, &width);
+      const int pg = src.page_of[i];
+      if (pg < 0 || pg >= static_cast<int>(h->pages.size()))
+        return set_error(h, CREC_E_INVALID, "line " + std::to_string(i) + ": page " + std::to_string(pg) + " not set");
+      if (width > bw[i])
+        return set_error(h, CREC_E_RANGE, "crop_lines: line " + std::to_string(i) + " is " + std::to_string(width) +
+                                              " px wide, the batch " + std::to_string(bw[i]));
+      const double scale_x = (reg[2] - reg[0]) / width, scale_y = (reg[3] - reg[1]) / rule.height;
+      if (!(scale_x <= 7.0) || !(scale_y <= 7.0) || (reg[3] - reg[1]) + 2 * std::max(1.0, scale_y) + 2 > kMaxSrcRows)
+        return set_error(h, CREC_E_RANGE, "line " + std::to_string(i) + ": a downscale beyond this build's filter reach");
+      d.page = pg;
     }
-    crec_crop_region(&boxes[i], &rule, reg, &width);
-    if (page_of[i] < 0 || page_of[i] >= static_cast<int>(h->pages.size()))
-      return set_error(h, CREC_E_INVALID, "line " + std::to_string(line0 + i) + ": page " + std::to_string(page_of[i]) + " not set");
-    if (width > bw[i])
-      return set_error(h, CREC_E_RANGE, "crop_lines: line " + std::to_string(line0 + i) + " is " + std::to_string(width) +
-                                            " px wide, the batch " + std::to_string(bw[i]));
-    const double scale_x = (reg[2] - reg[0]) / width, scale_y = (reg[3] - reg[1]) / rule.height;
-    if (scale_x > 7.0 || scale_y > 7.0 || (reg[3] - reg[1]) + 2 * std::max(1.0, scale_y) + 2 > kMaxSrcRows)
-      return set_error(h, CREC_E_RANGE, "line " + std::to_string(line0 + i) + ": a downscale beyond this build's filter reach");
-    LineDesc& d = h->h_lines[i];
     d.x0 = reg[0];
     d.y0 = reg[1];
     d.x1 = reg[2];
     d.y1 = reg[3];
-    d.page = page_of[i];
     d.width = width;
     d.bw = bw[i];
     d.seg = static_cast<int>(seg);
-    h->last_seg[i] = static_cast<int>(seg);
-    h->last_bw[i] = bw[i];
-    h->h_frame0[i] = static_cast<int>(seg >> h->head_shift);
-    h->h_length[i] = std::min(bw[i] >> h->head_shift, width / rule.frame_px);
+    h->hs_frame0[i] = static_cast<int>(seg >> h->head_shift);
+    h->hs_length[i] = std::min(bw[i] >> h->head_shift, width / rule.frame_px);
     seg += bw[i] + h->gap;
   }
   const long long cols = round_up(seg, 128LL << h->max_shift);
   if (cols > h->max_cols) return set_error(h, CREC_E_RANGE, "a run wider than the configured columns");
-  for (int i = 0; i < n; ++i) h->h_lines[i].next_seg = i + 1 < n ? h->h_lines[i + 1].seg : static_cast<int>(cols);
-  std::memset(h->h_mask, 0, static_cast<size_t>(cols / 8));
-  for (int i = 0; i < n; ++i)
-    std::memset(h->h_mask + h->last_seg[i] / 8, 1, static_cast<size_t>(h->last_bw[i] / 8));
-  cudaStream_t s = h->stream;
-  CK(cudaMemcpyAsync(h->d_lines, h->h_lines, sizeof(LineDesc) * n, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(h->d_mask, h->h_mask, static_cast<size_t>(cols / 8), cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(h->d_frame0, h->h_frame0, sizeof(int) * n, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(h->d_length, h->h_length, sizeof(int) * n, cudaMemcpyHostToDevice, s));
-  CK(cudaMemsetAsync(h->d_err, 0, sizeof(int), s));
-  if (crops) {
-    CK(cudaMemcpyAsync(h->d_crops_in, crops, static_cast<size_t>(n) * h->height * crops_pitch, cudaMemcpyHostToDevice, s));
-    h->run_crops = h->d_crops_in;
-    h->crops_in_pitch = crops_pitch;
+  for (int i = a; i < b; ++i) h->hs_lines[i].next_seg = i + 1 < b ? h->hs_lines[i + 1].seg : static_cast<int>(cols);
+  uint8_t* mask = h->hs_mask + mask_off;
+  std::memset(mask, 0, static_cast<size_t>(cols / 8));
+  for (int i = a; i < b; ++i) std::memset(mask + h->hs_lines[i].seg / 8, 1, static_cast<size_t>(bw[i] / 8));
+  *cols_out = cols;
+  return CREC_OK;
+}
+
+// Lines [0, n) of a call, bucket widths bw[i]: cut into runs of at most max_lines lines and
+// max_columns columns, every run's copies and launches queued, one sync, the results packed.
+int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_lines* out) {
+  out->total = 0;
+  if (n == 0) return CREC_OK;
+  struct Run {
+    int a, b;
+    long long cols;
+    size_t mask_off, frame_off;
+  };
+  std::vector<Run> runs;
+  size_t mask_total = 0, frame_total = 0;
+  for (int a = 0; a < n;) {
+    long long cols = h->gap;
+    int b = a;
+    while (b < n && b - a < h->cfg.max_lines) {
+      const long long next = cols + bw[b] + h->gap;
+      if (round_up(next, 128LL << h->max_shift) > h->max_cols) break;
+      cols = next;
+      ++b;
+    }
+    if (b == a) return set_error(h, CREC_E_RANGE, "a line wider than the configured columns");
+    const long long rc = round_up(cols, 128LL << h->max_shift);
+    runs.push_back({a, b, rc, mask_total, frame_total});
+    mask_total += static_cast<size_t>(rc / 8);
+    frame_total += static_cast<size_t>(rc >> h->head_shift);
+    a = b;
   }
-  int rc = launch_run(h, n, cols, h->d_crops != nullptr);
-  if (rc) return rc;
-  const size_t frames = static_cast<size_t>(cols >> h->head_shift);
-  CK(cudaMemcpyAsync(h->h_count, h->d_count, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(h->h_ids, h->d_ids, sizeof(int32_t) * frames, cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(h->h_frames, h->d_frames, sizeof(int32_t) * frames, cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(h->h_probs, h->d_probs, sizeof(float) * frames, cudaMemcpyDeviceToHost, s));
+  int rc;
+  if ((rc = grow_pinned(h, &h->hs_lines, &h->cap_lines, n)) || (rc = grow_pinned(h, &h->hs_frame0, &h->cap_frame0, n)) ||
+      (rc = grow_pinned(h, &h->hs_length, &h->cap_length, n)) || (rc = grow_pinned(h, &h->hs_count, &h->cap_count, n)) ||
+      (rc = grow_pinned(h, &h->hs_mask, &h->cap_mask, mask_total)) ||
+      (rc = grow_pinned(h, &h->hs_ids, &h->cap_ids, frame_total)) ||
+      (rc = grow_pinned(h, &h->hs_frames, &h->cap_frames, frame_total)) ||
+      (rc = grow_pinned(h, &h->hs_probs, &h->cap_probs, frame_total)))
+    return rc;
+  cudaStream_t s = h->stream;
+  h->st_runs = static_cast<long long>(runs.size());
+  h->st_launches = 0;
+  h->st_h2d = 0;
+  h->st_d2h = 4;  // the error word
+  CK(cudaMemsetAsync(h->d_err, 0, sizeof(int), s));
+  for (const Run& r : runs) {
+    long long cols = 0;
+    if ((rc = layout_run(h, src, bw, r.a, r.b, r.mask_off, &cols))) return rc;
+    const int m = r.b - r.a;
+    CK(cudaMemcpyAsync(h->d_lines, h->hs_lines + r.a, sizeof(LineDesc) * m, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(h->d_mask, h->hs_mask + r.mask_off, static_cast<size_t>(cols / 8), cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(h->d_frame0, h->hs_frame0 + r.a, sizeof(int) * m, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(h->d_length, h->hs_length + r.a, sizeof(int) * m, cudaMemcpyHostToDevice, s));
+    h->run_crops = nullptr;
+    if (src.crops) {
+      CK(cudaMemcpyAsync(h->d_crops_in, src.crops + static_cast<size_t>(r.a) * h->height * src.pitch,
+                         static_cast<size_t>(m) * h->height * src.pitch, cudaMemcpyHostToDevice, s));
+      h->run_crops = h->d_crops_in;
+      h->crops_in_pitch = src.pitch;
+    }
+    h->st_h2d += static_cast<long long>(sizeof(LineDesc) * m + cols / 8 + 2 * sizeof(int) * m);
+    if (src.crops) h->st_h2d += static_cast<long long>(m) * h->height * src.pitch;
+    add_run_ops(h, bw, r.a, r.b);
+    if ((rc = launch_run(h, m, cols, h->d_crops != nullptr))) return rc;
+    const size_t frames = static_cast<size_t>(cols >> h->head_shift);
+    h->st_d2h += static_cast<long long>(sizeof(int32_t) * m + 12 * frames);
+    CK(cudaMemcpyAsync(h->hs_count + r.a, h->d_count, sizeof(int32_t) * m, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(h->hs_ids + r.frame_off, h->d_ids, sizeof(int32_t) * frames, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(h->hs_frames + r.frame_off, h->d_frames, sizeof(int32_t) * frames, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(h->hs_probs + r.frame_off, h->d_probs, sizeof(float) * frames, cudaMemcpyDeviceToHost, s));
+  }
   CK(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
-  if (*h->h_err) {
+  if (h->profile) collect_profile(h);
+  if (*h->h_err)
     return set_error(h, CREC_E_TIMEOUT, "a kernel's bounded wait ran out (device error " + std::to_string(*h->h_err) + ")");
+  const Run& last = runs.back();
+  h->last_n = last.b - last.a;
+  h->last_cols = last.cols;
+  h->last_seg.resize(h->last_n);
+  h->last_bw.resize(h->last_n);
+  for (int i = last.a; i < last.b; ++i) {
+    h->last_seg[i - last.a] = h->hs_lines[i].seg;
+    h->last_bw[i - last.a] = h->hs_lines[i].bw;
   }
-  h->last_n = n;
-  h->last_cols = cols;
-  for (int i = 0; i < n; ++i) {
-    const int k = h->h_count[i];
-    const int li = line0 + i;
-    out->counts[li] = k;
-    out->lengths[li] = h->h_length[i];
-    out->offsets[li] = static_cast<int32_t>(out->total);
-    if (out->total + k > out->capacity) return set_error(h, CREC_E_RANGE, "crec_lines: capacity too small");
-    const int f0 = h->h_frame0[i];
-    std::memcpy(out->ids + out->total, h->h_ids + f0, sizeof(int32_t) * k);
-    std::memcpy(out->frames + out->total, h->h_frames + f0, sizeof(int32_t) * k);
-    std::memcpy(out->probs + out->total, h->h_probs + f0, sizeof(float) * k);
-    out->total += k;
+  for (const Run& r : runs) {
+    for (int i = r.a; i < r.b; ++i) {
+      const int k = h->hs_count[i];
+      out->counts[i] = k;
+      out->lengths[i] = h->hs_length[i];
+      out->offsets[i] = static_cast<int32_t>(out->total);
+      if (out->total + k > out->capacity) return set_error(h, CREC_E_RANGE, "crec_lines: capacity too small");
+      const size_t f0 = r.frame_off + static_cast<size_t>(h->hs_frame0[i]);
+      std::memcpy(out->ids + out->total, h->hs_ids + f0, sizeof(int32_t) * k);
+      std::memcpy(out->frames + out->total, h->hs_frames + f0, sizeof(int32_t) * k);
+      std::memcpy(out->probs + out->total, h->hs_probs + f0, sizeof(float) * k);
+      out->total += k;
+    }
   }
   return CREC_OK;
 }
@@ -817,15 +966,17 @@ void free_all(crec_handle* h) {
   cudaFree(h->d_err);
   cudaFree(h->d_crops);
   cudaFree(h->d_crops_in);
-  cudaFreeHost(h->h_lines);
-  cudaFreeHost(h->h_mask);
-  cudaFreeHost(h->h_frame0);
-  cudaFreeHost(h->h_length);
-  cudaFreeHost(h->h_count);
-  cudaFreeHost(h->h_ids);
-  cudaFreeHost(h->h_frames);
-  cudaFreeHost(h->h_probs);
+  cudaFree(h->d_logits);
+  cudaFreeHost(h->hs_lines);
+  cudaFreeHost(h->hs_frame0);
+  cudaFreeHost(h->hs_length);
+  cudaFreeHost(h->hs_count);
+  cudaFreeHost(h->hs_mask);
+  cudaFreeHost(h->hs_ids);
+  cudaFreeHost(h->hs_frames);
+  cudaFreeHost(h->hs_probs);
   cudaFreeHost(h->h_err);
+  for (cudaEvent_t e : h->ev_pool) cudaEventDestroy(e);
   if (h->stream) cudaStreamDestroy(h->stream);
 }
 
@@ -884,12 +1035,7 @@ int open_impl(crec_handle* h, const crec_config* c) {
       (rc = dev_alloc(h, &h->d_ids, frames)) || (rc = dev_alloc(h, &h->d_frames, frames)) ||
       (rc = dev_alloc(h, &h->d_probs, frames)) || (rc = dev_alloc(h, &h->d_err, 1)))
     return rc;
-  if ((rc = host_alloc(h, &h->h_lines, ml)) || (rc = host_alloc(h, &h->h_mask, h->max_cols / 8)) ||
-      (rc = host_alloc(h, &h->h_frame0, ml)) || (rc = host_alloc(h, &h->h_length, ml)) ||
-      (rc = host_alloc(h, &h->h_count, ml)) || (rc = host_alloc(h, &h->h_ids, frames)) ||
-      (rc = host_alloc(h, &h->h_frames, frames)) || (rc = host_alloc(h, &h->h_probs, frames)) ||
-      (rc = host_alloc(h, &h->h_err, 1)))
-    return rc;
+  if ((rc = host_alloc(h, &h->h_err, 1))) return rc;
   const size_t crop_smem = ((h->height * c->max_width + 15) & ~15) + kMaxSrcRows * kStripCols +
                            (h->height * kMaxTaps + 2 * h->height + 256 + 8) * 4;
   CK(cudaFuncSetAttribute(crop_stem_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(crop_smem)));
@@ -983,6 +1129,10 @@ int crec_set_pages(crec_handle* h, const crec_page* pages, int n, const crec_row
     h->page_cap = need;
   }
   h->pages.resize(n);
+  h->st_h2d = 0;
+  h->st_d2h = 0;
+  h->st_launches = 0;
+  h->st_runs = 0;
   size_t at = 0;
   for (int i = 0; i < n; ++i) {
     const crec_page& pg = pages[i];
@@ -994,9 +1144,11 @@ int crec_set_pages(crec_handle* h, const crec_page* pages, int n, const crec_row
         if (y1 <= y0) continue;
         CK(cudaMemcpy2DAsync(d + static_cast<size_t>(y0) * pg.width, pg.width, pg.data + y0 * pg.stride, pg.stride,
                              pg.width, y1 - y0, cudaMemcpyHostToDevice, h->stream));
+        h->st_h2d += static_cast<long long>(y1 - y0) * pg.width;
       }
     } else {
       CK(cudaMemcpy2DAsync(d, pg.width, pg.data, pg.stride, pg.width, pg.height, cudaMemcpyHostToDevice, h->stream));
+      h->st_h2d += static_cast<long long>(pg.height) * pg.width;
     }
     at += (static_cast<size_t>(pg.height) * pg.width + 255) / 256 * 256;
   }
@@ -1034,14 +1186,18 @@ int crec_recognize(crec_handle* h, const int32_t* page_of, const crec_box* boxes
   if (n == 0) return CREC_OK;
   CK(cudaSetDevice(h->device));
   std::vector<int> bws(n, bw);
-  return run_lines(h, page_of, boxes, bws.data(), n, out, 0);
+  Source src;
+  src.page_of = page_of;
+  src.boxes = boxes;
+  return recognize_all(h, src, bws.data(), n, out);
 }
 
 int crec_recognize_lines(crec_handle* h, const int32_t* page_of, const crec_box* boxes, const int32_t* bw, int n,
                          crec_lines* out) {
   if (!h) return CREC_E_INVALID;
   if (h->broken) return set_error(h, CREC_E_STICKY, "the GPU is broken for this process");
-  if (n < 0 || !out || (n > 0 && (!page_of || !boxes)))
+  if (n < 0 || !out || (n > 0 && (!page_of || !boxes || !out->counts || !out->lengths || !out->offsets ||
+                                   !out->ids || !out->frames || !out->probs)))
     return set_error(h, CREC_E_INVALID, "recognize_lines: arguments");
   out->total = 0;
   if (n == 0) return CREC_OK;
@@ -1059,30 +1215,17 @@ int crec_recognize_lines(crec_handle* h, const int32_t* page_of, const crec_box*
     if (bws[i] <= 0 || bws[i] > h->cfg.max_width || bws[i] % h->cfg.crop.width_step || bws[i] % (1 << h->max_shift))
       return set_error(h, CREC_E_INVALID, "recognize_lines: line " + std::to_string(i) + " bucket width " + std::to_string(bws[i]));
   }
-  // runs: as many lines as fit the configured lines and columns
-  for (int a = 0; a < n;) {
-    long long cols = h->gap;
-    int b = a;
-    while (b < n && b - a < h->cfg.max_lines) {
-      const long long next = cols + bws[b] + h->gap;
-      if (round_up(next, 128LL << h->max_shift) > h->max_cols) break;
-      cols = next;
-      ++b;
-    }
-    if (b == a) return set_error(h, CREC_E_RANGE, "recognize_lines: a line wider than the configured columns");
-    const int rc = run_lines(h, page_of + a, boxes + a, bws.data() + a, b - a, out, a);
-    if (rc) return rc;
-    a = b;
-  }
-  return CREC_OK;
+  Source src;
+  src.page_of = page_of;
+  src.boxes = boxes;
+  return recognize_all(h, src, bws.data(), n, out);
 }
 
 int crec_recognize_crops(crec_handle* h, const uint8_t* crops, int pitch, const int32_t* widths, const int32_t* bw,
                          int n, crec_lines* out) {
   if (!h) return CREC_E_INVALID;
   if (h->broken) return set_error(h, CREC_E_STICKY, "the GPU is broken for this process");
-  if (n < 0 || n > h->cfg.max_lines || !out || (n > 0 && (!crops || !widths || !bw)) || pitch <= 0 ||
-      pitch > h->cfg.max_width)
+  if (n < 0 || !out || (n > 0 && (!crops || !widths || !bw)) || pitch <= 0 || pitch > h->cfg.max_width)
     return set_error(h, CREC_E_INVALID, "recognize_crops: arguments");
   out->total = 0;
   if (n == 0) return CREC_OK;
@@ -1092,7 +1235,11 @@ int crec_recognize_crops(crec_handle* h, const uint8_t* crops, int pitch, const 
       return set_error(h, CREC_E_INVALID, "recognize_crops: line " + std::to_string(i) + " bucket width " + std::to_string(bw[i]));
   if (!h->d_crops_in) CK(cudaMalloc(&h->d_crops_in, static_cast<size_t>(h->cfg.max_lines) * h->height * h->cfg.max_width));
   std::vector<int> bws(bw, bw + n);
-  return run_lines(h, nullptr, nullptr, bws.data(), n, out, 0, crops, pitch, widths);
+  Source src;
+  src.crops = crops;
+  src.pitch = pitch;
+  src.widths = widths;
+  return recognize_all(h, src, bws.data(), n, out);
 }
 
 int crec_debug_crops(crec_handle* h, uint8_t* out, int pitch) {
@@ -1108,6 +1255,63 @@ int crec_debug_crops(crec_handle* h, uint8_t* out, int pitch) {
   }
   if (!h->d_crops || h->crops_pitch != pitch) return set_error(h, CREC_E_INVALID, "debug crops not armed at this pitch");
   CK(cudaMemcpy(out, h->d_crops, static_cast<size_t>(h->last_n) * h->height * pitch, cudaMemcpyDeviceToHost));
+  return CREC_OK;
+}
+
+int crec_last_stats(const crec_handle* h, crec_stats* out) {
+  if (!h || !out) return CREC_E_INVALID;
+  out->runs = h->st_runs;
+  out->launches = h->st_launches;
+  out->h2d_bytes = h->st_h2d;
+  out->d2h_bytes = h->st_d2h;
+  return CREC_OK;
+}
+
+int crec_profile(crec_handle* h, int enable, crec_profile_entry* out, int capacity) {
+  if (!h) return CREC_E_INVALID;
+  static const char* names[5] = {"crop_stem", "conv_gemm_tcgen05", "depthwise", "head_ctc_tcgen05", "collapse"};
+  int n = 0;
+  if (out) {
+    for (int k = 0; k < 5 && n < capacity; ++k, ++n) {
+      out[n].kernel = names[k];
+      out[n].launches = h->prof_count[k];
+      out[n].ms = h->prof_ms[k];
+      out[n].ops = h->prof_ops[k];
+    }
+  }
+  if (enable >= 0) {  // (re)start: clear the totals
+    h->profile = enable != 0;
+    for (int k = 0; k < 8; ++k) {
+      h->prof_ms[k] = 0;
+      h->prof_ops[k] = 0;
+      h->prof_count[k] = 0;
+    }
+  }
+  return n;
+}
+
+int crec_debug_logits(crec_handle* h, float* out, int64_t capacity) {
+  if (!h) return CREC_E_INVALID;
+  CK(cudaSetDevice(h->device));
+  const int classes = h->v[h->outv].c;
+  if (!out) {  // arm: the runs from now on write their logits
+    if (!h->d_logits) CK(cudaMalloc(&h->d_logits, static_cast<size_t>(h->max_cols >> h->head_shift) * classes * sizeof(float)));
+    return CREC_OK;
+  }
+  if (!h->d_logits) return set_error(h, CREC_E_INVALID, "debug logits not armed");
+  CK(cudaStreamSynchronize(h->stream));
+  size_t need = 0;
+  for (int i = 0; i < h->last_n; ++i) need += static_cast<size_t>(h->last_bw[i] >> h->head_shift) * classes;
+  if (static_cast<int64_t>(need) > capacity) return set_error(h, CREC_E_RANGE, "debug_logits: capacity");
+  float* o = out;
+  for (int i = 0; i < h->last_n; ++i) {  // line i: [classes][frames], as the reference's output
+    const long long f0 = h->last_seg[i] >> h->head_shift, t = h->last_bw[i] >> h->head_shift;
+    std::vector<float> buf(static_cast<size_t>(t) * classes);
+    CK(cudaMemcpy(buf.data(), h->d_logits + f0 * classes, buf.size() * sizeof(float), cudaMemcpyDeviceToHost));
+    for (long long f = 0; f < t; ++f)
+      for (int c = 0; c < classes; ++c) o[static_cast<size_t>(c) * t + f] = buf[static_cast<size_t>(f) * classes + c];
+    o += buf.size();
+  }
   return CREC_OK;
 }
 

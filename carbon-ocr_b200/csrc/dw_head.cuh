@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(256) dw_kernel(const __grid_constant__ DwParam
 struct HeadParams {
   CUtensorMap tmap;     // the head's input: (K byte, frame column, row)
   const uint8_t* wimg;  // [chunk][kb][nchunk rows][128 bytes], swizzled
-  int nkb, classes, nchunk, chunks;
+  int nkb, last_steps, classes, nchunk, chunks;  // last_steps: 32-byte K steps in the last K block
   int ow, num_tiles;
   uint32_t a_bytes, b_bytes;  // A: nkb x 16 KB; B: one chunk (nkb blocks)
   const int32_t* colsum;
@@ -136,6 +136,7 @@ struct HeadParams {
   int out_shift;
   int32_t* frame_id;   // [ow]
   float* frame_prob;   // [ow]
+  float* logits;       // optional (tests): [ow][classes] each frame's logits as the reference stores them
   int* err;
 };
 
@@ -241,7 +242,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
           const uint32_t a0 = smem_u32(sa), b0 = smem_u32(sb + bi * p.b_bytes);
           uint32_t accumulate = 0;
           for (int kb = 0; kb < p.nkb; ++kb) {
-            for (int s = 0; s < 4; ++s) {
+            const int steps = kb == p.nkb - 1 ? p.last_steps : 4;
+            for (int s = 0; s < steps; ++s) {
               umma<kInt8>(d, umma_desc_sw128(a0 + kb * 16384 + s * 32),
                           umma_desc_sw128(b0 + kb * p.nchunk * 128 + s * 32), idesc, accumulate);
               accumulate = 1;
@@ -293,6 +295,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
               q = q < hi ? q : hi;
               const int code = __float2int_rn(q) + p.out_zero;
               o[i] = static_cast<uint8_t>(code);
+              if (p.logits && j < p.classes && ox < p.ow) p.logits[static_cast<long long>(ox) * p.classes + j] = tab[code];
               if (j < p.classes && code > bestq) {
                 bestq = code;
                 best = j;
@@ -305,6 +308,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
               const int j = j0 + i;
               if (j >= p.classes) continue;
               const float v = __fadd_rn(__uint_as_float(r[i]), p.bias[j]);
+              if (p.logits && ox < p.ow) p.logits[static_cast<long long>(ox) * p.classes + j] = v;
               if (v > bestv) {
                 sum = bestv == -INFINITY ? 1.0f : __fadd_rn(__fmul_rn(sum, exp_neg_d(__fsub_rn(bestv, v))), 1.0f);
                 bestv = v;

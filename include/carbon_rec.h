@@ -143,6 +143,25 @@ CREC_API int crec_width_bucket(int crop_width);
  * the crop's width. */
 CREC_API int crec_crop_region(const crec_box* box, const crec_crop_rule* rule, double* region, int* width);
 
+/* What the last call did: device runs, kernel launches, bytes copied host -> device and back. */
+typedef struct crec_stats {
+  int64_t runs, launches, h2d_bytes, d2h_bytes;
+} crec_stats;
+CREC_API int crec_last_stats(const crec_handle* h, crec_stats* out);
+
+/* Per-kernel device times, measured with CUDA events around each launch on the handle's stream:
+ * one entry per kernel kind (its name, launches, milliseconds summed, and algorithmic operations --
+ * 2 x multiply-adds over the lines' own columns -- summed), totals since profiling was last
+ * (re)started.  enable 1 starts (or restarts) profiling, 0 stops it, -1 leaves it as it is; out
+ * (null: not read) gets up to `capacity` entries; returns the entries written. */
+typedef struct crec_profile_entry {
+  const char* kernel;
+  int64_t launches;
+  double ms;
+  double ops;
+} crec_profile_entry;
+CREC_API int crec_profile(crec_handle* h, int enable, crec_profile_entry* out, int capacity);
+
 /* The CUDA stream (a cudaStream_t) the handle's work runs on, for device-side timing. */
 CREC_API void* crec_stream(crec_handle* h);
 
@@ -152,6 +171,10 @@ CREC_API void* crec_stream(crec_handle* h);
  * CREC_INT8, float16 for CREC_FP16). */
 CREC_API int crec_debug_crops(crec_handle* h, uint8_t* out, int pitch);
 CREC_API int crec_debug_value(crec_handle* h, int value, void* out, int64_t capacity_bytes);
+/* Test hook: the last run's logits, each line's [classes][bw / frame_px] floats one after another
+ * (INT8: the uint8 logits' values, (q - zero) * scale, as the reference's output table gives them;
+ * FP16: the FP32 sums).  out null arms it: the runs from then on write them (slower). */
+CREC_API int crec_debug_logits(crec_handle* h, float* out, int64_t capacity);
 
 #ifdef __cplusplus
 }

@@ -233,6 +233,9 @@ class Reference(_Common):
         L.ref_free.restype = None
         L.ref_bench_batches.argtypes = [C.c_char_p, C.c_char_p, _i, _i, _i, _p, _p, _p, _p, _p, _i, _i]
         L.ref_bench_batches.restype = _d
+        L.ref_bench_pages.argtypes = [C.c_char_p, C.c_char_p, _i, _i, _i, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _i,
+                                      C.POINTER(C.c_int64)]
+        L.ref_bench_pages.restype = _d
         self._crop_lines = L.ref_crop_lines
 
     def error(self) -> str:
@@ -279,6 +282,38 @@ class Reference(_Common):
                                    _ptr(fr), _ptr(pr)) != 0:
             raise ValueError(self.error())
         return [(ids[i, :counts[i]].copy(), fr[i, :counts[i]].copy(), pr[i, :counts[i]].copy()) for i in range(n)]
+
+    def bench_pages(self, model_path, pages, page_of, boxes, bws, threads: int, rounds: int = 1, first_cpu: int = 0,
+                    isa: str = "", batch: int = 256):
+        """The reference's CPU device on pages (crop_lines, ink, int8 session, ctc_greedy), `threads`
+        pinned workers: (seconds of `rounds` timed passes, lines recognized in them)."""
+        order = np.lexsort((np.arange(len(bws)), np.asarray(bws)))  # stable by bucket, as the pipeline sorts
+        po = np.ascontiguousarray(np.asarray(page_of, np.int32)[order])
+        bx = np.ascontiguousarray(np.asarray(boxes, np.float64).reshape(-1, 4)[order])
+        bwo = np.asarray(bws, np.int32)[order]
+        starts, counts, widths = [], [], []
+        a = 0
+        while a < len(bwo):
+            b = a
+            while b < len(bwo) and bwo[b] == bwo[a] and b - a < batch:
+                b += 1
+            starts.append(a)
+            counts.append(b - a)
+            widths.append(int(bwo[a]))
+            a = b
+        arr = [np.ascontiguousarray(p, np.uint8) for p in pages]
+        data = (C.c_void_p * len(arr))(*[p.ctypes.data for p in arr])
+        pw = np.array([p.shape[1] for p in arr], np.int32)
+        ph = np.array([p.shape[0] for p in arr], np.int32)
+        ps = np.array([p.strides[0] for p in arr], np.int64)
+        st, ct, wd = (np.array(v, np.int32) for v in (starts, counts, widths))
+        done = C.c_int64()
+        secs = self.lib.ref_bench_pages(str(model_path).encode(), isa.encode(), threads, first_cpu, len(arr), data,
+                                        _ptr(pw), _ptr(ph), _ptr(ps), len(st), _ptr(st), _ptr(ct), _ptr(wd), _ptr(po),
+                                        _ptr(bx), rounds, C.byref(done))
+        if secs < 0:
+            raise ValueError(self.error())
+        return secs, done.value
 
     def session(self, path, isa: str = "", model_bytes: bytes | None = None) -> "RefSession":
         return RefSession(self, path, isa, model_bytes)

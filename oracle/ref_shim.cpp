@@ -301,4 +301,91 @@ double ref_bench_batches(const char* model, const char* isa, int threads, int fi
   }
 }
 
+// The CPU baseline on pages, as the reference's CPU device recognizes a run
+// (CpuModels::recognize, carbon/src/pipeline.cpp:138-162): per batch (lines of one bucket width,
+// at most 256, contiguous in the arrays), crop_lines per run of lines of one page, the ink map
+// 1 - p / 255, the native session, ctc_greedy with lengths min(frames, width / 4).  `threads`
+// pinned workers (cores first_cpu...), each with its own single-threaded session, take batches
+// round-robin.  One untimed pass, then `rounds` timed passes; returns their wall seconds.
+double ref_bench_pages(const char* model, const char* isa, int threads, int first_cpu, int npages,
+                       const uint8_t* const* page_data, const int32_t* page_w, const int32_t* page_h,
+                       const int64_t* page_stride, int batches, const int32_t* batch_start,
+                       const int32_t* batch_count, const int32_t* batch_bw, const int32_t* page_of,
+                       const double* boxes, int rounds, int64_t* lines_done) {
+  try {
+    std::vector<std::unique_ptr<carbon::Session>> sessions(static_cast<size_t>(threads));
+    for (int t = 0; t < threads; ++t) {
+      carbon::SessionOptions o;
+      o.threads = 1;
+      if (isa) o.isa = isa;
+      sessions[t] = carbon::open_session(carbon::Backend::kNative, model, o);
+    }
+    std::atomic<int> errors{0};
+    std::atomic<int64_t> done{0};
+    const carbon::CropRule rule;
+    auto work = [&](int t, int passes) {
+      cpu_set_t set;
+      CPU_ZERO(&set);
+      CPU_SET(first_cpu + t, &set);
+      pthread_setaffinity_np(pthread_self(), sizeof set, &set);
+      try {
+        std::vector<uint8_t> crops;
+        std::vector<int32_t> widths;
+        for (int r = 0; r < passes; ++r) {
+          for (int b = t; b < batches; b += threads) {
+            const int a0 = batch_start[b], m = batch_count[b], bw = batch_bw[b], h = rule.height;
+            crops.assign(static_cast<size_t>(m) * h * bw, 0);
+            widths.assign(m, 0);
+            for (int i = 0; i < m;) {
+              int e = i + 1;
+              while (e < m && page_of[a0 + e] == page_of[a0 + i]) ++e;
+              const int pg = page_of[a0 + i];
+              const carbon::GrayView v{page_data[pg], page_w[pg], page_h[pg], page_stride[pg]};
+              std::vector<carbon::LineBox> bx;
+              for (int k = i; k < e; ++k) {
+                const double* q = boxes + 4 * static_cast<size_t>(a0 + k);
+                bx.push_back({q[0], q[1], q[2], q[3]});
+              }
+              carbon::crop_lines(v, bx, bw, crops.data() + static_cast<size_t>(i) * h * bw,
+                                 std::span<int32_t>(widths.data() + i, static_cast<size_t>(e - i)), rule);
+              i = e;
+            }
+            carbon::Tensor x = carbon::Tensor::empty(carbon::DType::kFloat32, {m, 1, h, bw});
+            float* px = x.data<float>().data();
+            for (size_t i = 0; i < crops.size(); ++i) px[i] = 1.0f - crops[i] / 255.0f;
+            std::vector<carbon::Tensor> in;
+            in.push_back(std::move(x));
+            const std::vector<carbon::Tensor> o = sessions[t]->run(in);
+            const carbon::Shape& s = o[0].shape();
+            std::vector<int32_t> lengths(m);
+            for (int i = 0; i < m; ++i) lengths[i] = std::min<int32_t>(static_cast<int32_t>(s[2]), widths[i] / rule.frame_px);
+            const auto lines = carbon::ctc_greedy(o[0].data<float>().data(), m, static_cast<int>(s[1]),
+                                                  static_cast<int>(s[2]), lengths);
+            if (lines.size() != static_cast<size_t>(m)) errors++;
+            done += m;
+          }
+        }
+      } catch (...) {
+        errors++;
+      }
+    };
+    auto run_all = [&](int passes) {
+      std::vector<std::thread> pool;
+      for (int t = 0; t < threads; ++t) pool.emplace_back(work, t, passes);
+      for (auto& th : pool) th.join();
+    };
+    run_all(1);
+    done = 0;
+    const auto t0 = std::chrono::steady_clock::now();
+    run_all(rounds);
+    const double secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (errors) throw carbon::Error("ref_bench_pages: a worker failed");
+    if (lines_done) *lines_done = done;
+    return secs;
+  } catch (const std::exception& e) {
+    fail(e);
+    return -1.0;
+  }
+}
+
 }  // extern "C"

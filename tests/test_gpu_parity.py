@@ -1,0 +1,288 @@
+"""The CUDA path against the oracle, through the C ABI.
+
+INT8: crops, every intermediate tensor, the logits' values, ids, frames and probabilities
+bit for bit (the reference's int8 executor, restated in oracle/rec_oracle.c and pinned to
+the reference's own code by tests/test_oracle_*.py).  FP16: logits within max-abs 2e-2 of
+the FP32 recognizer and at least 99.9% of frame ids agreeing."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from carbon_rec import native, synth
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+FP16_LOGIT_TOL = 2e-2   # max |logit_fp16 - logit_fp32|
+FP16_ID_AGREEMENT = 0.999
+
+
+@pytest.fixture(scope="module")
+def dev8(rec_latin):
+    d = native.RecDevice(rec_latin[0].to_blob(), native.INT8, max_lines=512, max_width=2048, max_pages=8)
+    yield d
+    d.close()
+
+
+@pytest.fixture(scope="module")
+def dev16(rec_latin):
+    d = native.RecDevice(rec_latin[1].to_blob(), native.FP16, max_lines=512, max_width=2048, max_pages=8)
+    yield d
+    d.close()
+
+
+def oracle_lines(orc, m, crops, widths, bws):
+    """Per line at its own bucket width: (logits, (ids, frames, probs), length)."""
+    out = []
+    for i in range(len(crops)):
+        logits = m.run(crops[i:i + 1, :, :int(bws[i])])
+        t = logits.shape[2]
+        length = min(t, int(widths[i]) // 4)
+        lines, _, _ = orc.ctc_greedy(logits, [length])
+        out.append((logits[0], lines[0], length))
+    return out
+
+
+def assert_same_lines(got, lengths, want):
+    for i, (g, (_, (ids, fr, pr), length)) in enumerate(zip(got, want)):
+        assert lengths[i] == length, i
+        assert np.array_equal(g.ids, ids), (i, g.ids[:12], ids[:12])
+        assert np.array_equal(g.frames, fr), i
+        assert np.array_equal(g.probs.view(np.int32), pr.view(np.int32)), i
+
+
+def test_config1_int8_bit_exact(dev8, orc, rec_latin):
+    crops, widths, bws = synth.crops(1, 64, 96, 640)
+    dev8.arm_logits()
+    got, lengths = dev8.recognize_crops(crops, widths, bws)
+    want = oracle_lines(orc, orc.model(rec_latin[0].to_blob()), crops, widths, bws)
+    assert_same_lines(got, lengths, want)
+    logits = dev8.logits(bws, 800)
+    for i, (l, _, _) in enumerate(want):
+        assert np.array_equal(logits[i], l), i
+
+
+def test_every_layer_int8_bit_exact(dev8, orc, rec_latin):
+    net = rec_latin[0]
+    crops, widths, bws = synth.crops(2, 5, 32, 700, bucket_step=8)
+    dev8.recognize_crops(crops, widths, bws)
+    m = orc.model(net.to_blob())
+    for vi, v in enumerate(net.values):
+        if vi in (net.inp, net.out):
+            continue
+        shapes = [net.shapes_for(int(b))[vi] for b in bws]
+        sizes = [h * w * v.c for h, w in shapes]
+        got = dev8.value(vi, sum(sizes))
+        at = 0
+        for i in range(len(bws)):
+            _, keep = m.run(crops[i:i + 1, :, :int(bws[i])], keep_value=vi, keep_shape=(sizes[i],))
+            assert np.array_equal(got[at:at + sizes[i]], keep), (vi, v.name, i)
+            at += sizes[i]
+
+
+def test_config1_fp16_within_tolerance(dev16, orc, rec_latin):
+    crops, widths, bws = synth.crops(1, 64, 96, 640)
+    dev16.arm_logits()
+    got, lengths = dev16.recognize_crops(crops, widths, bws)
+    logits = dev16.logits(bws, 800)
+    m32 = orc.model(rec_latin[1].to_blob())
+    agree = total = 0
+    worst = 0.0
+    for i in range(len(crops)):
+        ref = m32.run(crops[i:i + 1, :, :int(bws[i])])[0]
+        worst = max(worst, float(np.abs(logits[i] - ref).max()))
+        agree += int((logits[i].argmax(0) == ref.argmax(0)).sum())
+        total += ref.shape[1]
+    assert worst <= FP16_LOGIT_TOL, worst
+    assert agree / total >= FP16_ID_AGREEMENT, (agree, total)
+    assert all(lengths[i] == min(int(bws[i]) // 4, int(widths[i]) // 4) for i in range(len(crops)))
+
+
+def two_pages(seed=7):
+    """tests/cpp/cuda_lines_test.cpp:47-109 of the reference: 1700 x 2200 and 900 x 640, one inverted."""
+    rng = np.random.default_rng(seed)
+    pages, boxes, page_of = [], [], []
+    for p, (w, h, invert) in enumerate(((1700, 2200, False), (900, 640, True))):
+        page = np.clip(rng.normal(235, 8, (h, w)), 0, 255).astype(np.uint8)
+        for _ in range(400):
+            x, y = int(rng.integers(0, w - 20)), int(rng.integers(0, h - 10))
+            page[y:y + int(rng.integers(3, 20)), x:x + int(rng.integers(2, 8))] = int(rng.integers(0, 80))
+        pages.append(255 - page if invert else page)
+        k = 0
+        while k < 150:
+            bh = rng.uniform(8, 60)
+            x0, y0 = rng.uniform(-30, w - 10), rng.uniform(-20, h - 5)
+            bw = rng.uniform(5, 900)
+            if (bw + 0.6 * bh) * 32 / (1.4 * bh) > 1000:
+                continue
+            boxes.append([x0, y0, x0 + bw, y0 + bh])
+            page_of.append(p)
+            k += 1
+    return pages, np.asarray(boxes), np.asarray(page_of, np.int32)
+
+
+@pytest.mark.parametrize("rule", [{}, {"flip_margin": 0}])
+def test_pages_crops_and_ctc_bit_exact(rec_latin, orc, rule):
+    pages, boxes, page_of = two_pages()
+    crop_rule = native.CropRule.default(**rule)
+    dev = native.RecDevice(rec_latin[0].to_blob(), native.INT8, max_lines=512, max_width=1024, max_pages=4,
+                           crop=crop_rule)
+    try:
+        dev.set_pages(pages)
+        dev.arm_crops(1024)
+        got, lengths = dev.recognize(page_of, boxes, 1024)
+        crops = dev.crops(len(boxes), 1024)
+    finally:
+        dev.close()
+    ocr = O.CropRule.default(**rule)
+    want_crops = np.zeros_like(crops)
+    widths = np.zeros(len(boxes), np.int32)
+    for p in range(2):
+        sel = np.nonzero(page_of == p)[0]
+        c, w = orc.crop_lines(pages[p], boxes[sel], 1024, ocr)
+        want_crops[sel] = c
+        widths[sel] = w
+    assert np.array_equal(crops, want_crops)
+    # the recognizer on a sample of the crops, at the run's bucket width
+    m = orc.model(rec_latin[0].to_blob())
+    sample = np.arange(0, len(boxes), 15)
+    logits = m.run(want_crops[sample])
+    lines, _, _ = orc.ctc_greedy(logits, np.minimum(256, widths[sample] // 4))
+    for j, i in enumerate(sample):
+        assert lengths[i] == min(256, widths[i] // 4)
+        ids, fr, pr = lines[j]
+        assert np.array_equal(got[i].ids, ids) and np.array_equal(got[i].frames, fr)
+        assert np.array_equal(got[i].probs.view(np.int32), pr.view(np.int32))
+
+
+def test_scheduler_runs_are_independent_of_grouping(rec_latin):
+    """Lines of several pages at their ladder buckets, cut into many runs (a small column budget) or
+    one: the same decodings, each line's also the same as when it is read alone."""
+    pages, boxes = synth.pages(11, 3, 1200, 900, 20)
+    page_of = np.repeat(np.arange(3), 20).astype(np.int32)
+    allb = np.concatenate(boxes)
+    blob = rec_latin[0].to_blob()
+    big = native.RecDevice(blob, native.INT8, max_lines=256, max_width=2048, max_pages=4)
+    small = native.RecDevice(blob, native.INT8, max_lines=7, max_width=2048, max_columns=4096, max_pages=4)
+    try:
+        big.set_pages(pages)
+        small.set_pages(pages)
+        a, la = big.recognize_lines(page_of, allb)
+        b, lb = small.recognize_lines(page_of, allb)
+        assert np.array_equal(la, lb)
+        for x, y in zip(a, b):
+            assert np.array_equal(x.ids, y.ids) and np.array_equal(x.frames, y.frames)
+            assert np.array_equal(x.probs.view(np.int32), y.probs.view(np.int32))
+        bws = [native.width_bucket(native.crop_region(bx)[1]) for bx in allb]
+        for i in (0, 17, 33, 59):
+            one, l1 = big.recognize([page_of[i]], allb[i:i + 1], bws[i])
+            assert l1[0] == la[i] and np.array_equal(one[0].ids, a[i].ids)
+            assert np.array_equal(one[0].probs.view(np.int32), a[i].probs.view(np.int32))
+        # permuted order: each line's result is its own
+        perm = np.random.default_rng(0).permutation(len(allb))
+        c, lc = big.recognize_lines(page_of[perm], allb[perm])
+        for j, i in enumerate(perm):
+            assert np.array_equal(c[j].ids, a[i].ids) and lc[j] == la[i]
+    finally:
+        big.close()
+        small.close()
+
+
+def test_mini_model_odd_channels_bit_exact(mini, orc, golden):
+    """A recognizer whose channel counts are not multiples of 16 (padded on the device)."""
+    import hashlib
+    n8 = mini[0]
+    crops, widths, bws = synth.crops(21, 6, 40, 200, bucket_step=8)
+    dev = native.RecDevice(n8.to_blob(), native.INT8, max_lines=16, max_width=256, max_pages=1)
+    try:
+        dev.arm_logits()
+        got, lengths = dev.recognize_crops(crops, widths, bws)
+        logits = dev.logits(bws, n8.classes)
+    finally:
+        dev.close()
+    want = oracle_lines(orc, orc.model(n8.to_blob()), crops, widths, bws)
+    assert_same_lines(got, lengths, want)
+    for i, g in enumerate(golden["mini_int8"]["lines"]):
+        assert hashlib.sha256(logits[i][None].tobytes()).hexdigest() == g["logits_sha256"], i
+
+
+def test_config3_scale_int8(dev8, orc, rec_latin):
+    """Config 3: 4096 crops, widths log-uniform in [64, 1024], 32-px buckets.  Properties at full
+    size (a second run is identical; each line is its own), the oracle on a sample, and the
+    reference's own executor on all of them where its build travelled here."""
+    crops, widths, bws = synth.crops(3000, 4096, 64, 1024, log_uniform=True)
+    got, lengths = dev8.recognize_crops(crops, widths, bws)
+    again, lengths2 = dev8.recognize_crops(crops, widths, bws)
+    assert np.array_equal(lengths, lengths2)
+    for x, y in zip(got, again):
+        assert np.array_equal(x.ids, y.ids) and np.array_equal(x.probs.view(np.int32), y.probs.view(np.int32))
+    m = orc.model(rec_latin[0].to_blob())
+    sample = np.random.default_rng(5).choice(4096, 24, replace=False)
+    want = oracle_lines(orc, m, crops[sample], widths[sample], bws[sample])
+    assert_same_lines([got[i] for i in sample], lengths[sample], want)
+    if O.Reference.available():
+        import tempfile
+        from pathlib import Path
+        from carbon_rec import onnx_pb
+        ref = O.Reference()
+        with tempfile.TemporaryDirectory() as d:
+            path = Path(d) / "rec.int8.onnx"
+            onnx_pb.save(rec_latin[2], path)
+            s = ref.session(path)
+            for bw in np.unique(bws):
+                sel = np.nonzero(bws == bw)[0]
+                x = (np.float32(1.0) - crops[sel, :, :bw].astype(np.float32) / np.float32(255.0))[:, None]
+                logits = s.run(x)
+                lines = ref.ctc_greedy(logits, np.minimum(bw // 4, widths[sel] // 4))
+                for j, i in enumerate(sel):
+                    assert np.array_equal(got[i].ids, lines[j][0]) and np.array_equal(got[i].frames, lines[j][1])
+                    assert np.array_equal(got[i].probs.view(np.int32), lines[j][2].view(np.int32))
+
+
+def test_fp16_pages_agree_with_fp32(dev16, orc, rec_latin):
+    pages, boxes = synth.pages(2, 2, 2480, 3508, 32)
+    page_of = np.repeat(np.arange(2), 32).astype(np.int32)
+    allb = np.concatenate(boxes)
+    dev16.set_pages(pages)
+    dev16.arm_logits()
+    widths = np.array([native.crop_region(b)[1] for b in allb])
+    bws = ((widths + 31) // 32 * 32).astype(np.int32)
+    got, lengths = dev16.recognize_lines(page_of, allb, bws)
+    logits = dev16.logits(bws, 800)
+    m32 = orc.model(rec_latin[1].to_blob())
+    agree = total = 0
+    worst = 0.0
+    for i in range(0, len(allb), 4):
+        crop, _ = orc.crop_lines(pages[page_of[i]], allb[i:i + 1], int(bws[i]))
+        ref = m32.run(crop)[0]
+        worst = max(worst, float(np.abs(logits[i] - ref).max()))
+        agree += int((logits[i].argmax(0) == ref.argmax(0)).sum())
+        total += ref.shape[1]
+    assert worst <= FP16_LOGIT_TOL and agree / total >= FP16_ID_AGREEMENT, (worst, agree, total)
+
+
+def test_errors_are_reported_and_the_device_goes_on(dev8, rec_latin):
+    pages, boxes = synth.pages(3, 1, 800, 600, 4)
+    dev8.set_pages(pages)
+    wide = np.array([[10.0, 100.0, 790.0, 120.0]])
+    with pytest.raises(native.CrecError) as e:
+        dev8.recognize([0], wide, 64)  # crop_lines: wider than its batch
+    assert e.value.code == native.E_RANGE and "px wide, the batch 64" in str(e.value)
+    with pytest.raises(native.CrecError) as e:
+        dev8.recognize([5], boxes[0][:1], 2048)  # a page not set
+    assert e.value.code == native.E_INVALID
+    with pytest.raises(native.CrecError) as e:
+        dev8.recognize([0], boxes[0][:1], 100)  # not a multiple of the width step
+    assert e.value.code == native.E_INVALID
+    with pytest.raises(native.CrecError) as e:
+        native.RecDevice(b"CRECMDL1" + b"\0" * 64, native.INT8)
+    assert e.value.code == native.E_MODEL
+    with pytest.raises(native.CrecError) as e:
+        native.RecDevice(rec_latin[1].to_blob(), native.INT8)  # the float blob at INT8
+    assert e.value.code == native.E_MODEL
+    assert not dev8.broken
+    got, lengths = dev8.recognize([0, 0], boxes[0][:2], 2048)
+    assert len(got) == 2 and lengths.shape == (2,)
+    empty, el = dev8.recognize([], np.zeros((0, 4)), 256)
+    assert empty == [] and el.shape == (0,)
