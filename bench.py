@@ -66,11 +66,10 @@ def workload(rank: int, world: int):
     slots = range(rank * PAGES_TOTAL // world, (rank + 1) * PAGES_TOTAL // world)
     page_of = np.concatenate([np.full(LINES_PER_PAGE, s % DISTINCT, np.int32) for s in slots])
     allb = np.concatenate([boxes[s % DISTINCT] for s in slots])
-    widths = np.array([native.crop_region(b)[1] for b in allb[:LINES_PER_PAGE * DISTINCT]], np.int32)
-    wof = {int(i): widths[i] for i in range(len(widths))}
+    flat = np.concatenate(boxes)
+    widths = np.array([native.crop_region(b)[1] for b in flat], np.int32)
     per_page = [widths[p * LINES_PER_PAGE:(p + 1) * LINES_PER_PAGE] for p in range(DISTINCT)]
     bws = np.concatenate([(per_page[s % DISTINCT] + 31) // 32 * 32 for s in slots]).astype(np.int32)
-    del wof
     return pages, boxes, page_of, allb, bws
 
 

@@ -37,7 +37,7 @@ BACKBONE = [
     ("collapse", 160, 256, 2, 3, 1, 1, (0, 1, 0, 1), True),
 ]
 MIX_C, MIX_HIDDEN, CLASSES, HEIGHT = 256, 512, 800, 32
-BLANK_BIAS = 4.0  # class 0's bias: most frames of a line are blank, as in a trained CTC recognizer
+BLANK_BIAS = 4.75  # class 0's bias: about four frames in five blank, as a trained CTC recognizer gives them
 
 
 def make_weights(seed: int = 0, classes: int = CLASSES) -> dict[str, np.ndarray]:

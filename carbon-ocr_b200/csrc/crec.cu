@@ -1120,7 +1120,8 @@ int crec_set_pages(crec_handle* h, const crec_page* pages, int n, const crec_row
   if (need > h->page_cap) {
     const size_t limit = h->cfg.max_page_bytes > 0 ? static_cast<size_t>(h->cfg.max_page_bytes)
                                                    : static_cast<size_t>(h->max_pages) * 1700 * 2200;
-    if (need > std::max(limit, h->page_cap)) return set_error(h, CREC_E_RANGE, "set_pages: more page bytes than configured");
+    if (need > std::max(limit + static_cast<size_t>(n) * 256, h->page_cap))
+      return set_error(h, CREC_E_RANGE, "set_pages: more page bytes than configured");
     CK(cudaStreamSynchronize(h->stream));
     cudaFree(h->page_mem);
     h->page_mem = nullptr;
