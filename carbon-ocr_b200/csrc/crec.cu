@@ -491,6 +491,13 @@ int encode_map(crec_handle* h, CUtensorMap* m, const void* base, uint64_t d0, ui
   return CREC_OK;
 }
 
+// The crop kernel's shared memory: a crop at the widest bucket, the strip intermediate, the
+// vertical coefficients, the histogram and counters.
+size_t crop_smem_bytes(const crec_handle* h) {
+  return ((static_cast<size_t>(h->height) * h->cfg.max_width + 15) & ~size_t(15)) + kStripBytes +
+         (static_cast<size_t>(h->height) * kMaxTaps + 2 * h->height + 256 + 8) * 4;
+}
+
 // Kernel kinds of the profile: 0 crop+stem, 1 dense convolutions (tcgen05), 2 depthwise, 3 head+CTC, 4 collapse.
 enum ProfKind { kProfCrop = 0, kProfConv = 1, kProfDw = 2, kProfHead = 3, kProfCollapse = 4 };
 
@@ -592,14 +599,16 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.out_pitch = s0.pitch;
     p.out_shift = s0.shift;
     p.err = h->d_err;
-    const int maxbw = h->cfg.max_width;
-    const size_t smem = ((h->height * maxbw + 15) & ~15) + kMaxSrcRows * kStripCols +
-                        (h->height * kMaxTaps + 2 * h->height + 256 + 8) * 4;
+    const size_t smem = crop_smem_bytes(h);
     ProfScope prof(h, kProfCrop);
-    if (h->int8)
+    // the attribute is the function's, for every handle in the process: set it for this one's size
+    if (h->int8) {
+      CK(cudaFuncSetAttribute(crop_stem_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
       crop_stem_kernel<true><<<n, kCropThreads, smem, s>>>(p);
-    else
+    } else {
+      CK(cudaFuncSetAttribute(crop_stem_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
       crop_stem_kernel<false><<<n, kCropThreads, smem, s>>>(p);
+    }
     CK(cudaGetLastError());
   }
   for (size_t li = 1; li < h->l.size(); ++li) {
@@ -815,7 +824,8 @@ int layout_run(crec_handle* h, const Source& src, const int* bw, int a, int b, s
         return set_error(h, CREC_E_RANGE, "crop_lines: line " + std::to_string(i) + " is " + std::to_string(width) +
                                               " px wide, the batch " + std::to_string(bw[i]));
       const double scale_x = (reg[2] - reg[0]) / width, scale_y = (reg[3] - reg[1]) / rule.height;
-      if (!(scale_x <= 7.0) || !(scale_y <= 7.0) || (reg[3] - reg[1]) + 2 * std::max(1.0, scale_y) + 2 > kMaxSrcRows)
+      // the kernel's reach: at most kMaxTaps taps a sample (support up to 15), kMaxSrcRows source rows
+      if (!(scale_x <= 15.0) || !(scale_y <= 15.0) || (reg[3] - reg[1]) + 2 * std::max(1.0, scale_y) + 2 > kMaxSrcRows)
         return set_error(h, CREC_E_RANGE, "line " + std::to_string(i) + ": a downscale beyond this build's filter reach");
       d.page = pg;
     }
@@ -1036,10 +1046,7 @@ int open_impl(crec_handle* h, const crec_config* c) {
       (rc = dev_alloc(h, &h->d_probs, frames)) || (rc = dev_alloc(h, &h->d_err, 1)))
     return rc;
   if ((rc = host_alloc(h, &h->h_err, 1))) return rc;
-  const size_t crop_smem = ((h->height * c->max_width + 15) & ~15) + kMaxSrcRows * kStripCols +
-                           (h->height * kMaxTaps + 2 * h->height + 256 + 8) * 4;
-  CK(cudaFuncSetAttribute(crop_stem_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(crop_smem)));
-  CK(cudaFuncSetAttribute(crop_stem_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(crop_smem)));
+  if (crop_smem_bytes(h) > 232448) return set_error(h, CREC_E_INVALID, "max_width: the crop kernel's shared memory");
   return CREC_OK;
 }
 

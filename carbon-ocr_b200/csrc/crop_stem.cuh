@@ -26,9 +26,10 @@
 namespace crec {
 
 constexpr int kCropThreads = 256;
-constexpr int kMaxTaps = 16;        // taps a sample may have (downscales up to 7.5x)
-constexpr int kStripCols = 256;     // output columns a horizontal strip
-constexpr int kMaxSrcRows = 160;    // source rows a crop's vertical windows may span
+constexpr int kMaxTaps = 32;        // taps a sample may have: downscales up to 15x (the host checks)
+constexpr int kStripBytes = 48 << 10;  // the horizontal pass's intermediate: source rows x strip columns
+constexpr int kMaxStripCols = 256;  // output columns a horizontal strip at most
+constexpr int kMaxSrcRows = 1024;   // source rows a crop's vertical windows may span (the host checks)
 constexpr int kStemOut = 32;        // the stem's output channels this kernel supports (padded)
 
 struct PageDesc {
@@ -111,7 +112,7 @@ __device__ __forceinline__ uint8_t clip8d(int32_t v) {
   return static_cast<uint8_t>(v < 0 ? 0 : v > 255 ? 255 : v);
 }
 
-// Shared memory: crop [height][bw] | strip intermediate [kMaxSrcRows][kStripCols] |
+// Shared memory: crop [height][bw] | strip intermediate (kStripBytes: source rows x strip columns) |
 // vertical coefficients | histogram and counters.
 template <bool kInt8>
 __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_constant__ CropParams p) {
@@ -121,8 +122,8 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
   const PageDesc P = p.pages[L.page];
   const int H = p.height, bw = L.bw, cw = L.width;
   uint8_t* crop = sm;                                    // [H][bw]
-  uint8_t* tmp = crop + ((H * bw + 15) & ~15);           // [kMaxSrcRows][kStripCols]
-  int32_t* vk = reinterpret_cast<int32_t*>(tmp + kMaxSrcRows * kStripCols);  // [H][kMaxTaps]
+  uint8_t* tmp = crop + ((H * bw + 15) & ~15);           // [rows][strip columns], kStripBytes
+  int32_t* vk = reinterpret_cast<int32_t*>(tmp + kStripBytes);  // [H][kMaxTaps]
   int32_t* vfirst = vk + H * kMaxTaps;                   // [H]
   int32_t* vcount = vfirst + H;                          // [H]
   int32_t* hist = vcount + H;                            // [256]
@@ -152,9 +153,10 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
       return;
     }
 
-    // resample, a strip of columns at a time
-    for (int x0 = 0; x0 < cw; x0 += kStripCols) {
-      const int sc = min(kStripCols, cw - x0);
+    // resample, a strip of columns at a time (as wide as the intermediate holds for these rows)
+    const int strip = max(16, min(kMaxStripCols, (kStripBytes / max(rows, 1)) & ~15));
+    for (int x0 = 0; x0 < cw; x0 += strip) {
+      const int sc = min(strip, cw - x0);
       for (int xx = tid; xx < sc; xx += blockDim.x) {
         int32_t k[kMaxTaps];
         int n;
@@ -172,7 +174,7 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
               ss += v * k[i];
             }
           }
-          tmp[r * kStripCols + xx] = clip8d(ss);
+          tmp[r * strip + xx] = clip8d(ss);
         }
       }
       __syncthreads();
@@ -180,7 +182,7 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
         const int yy = i / sc, xx = i % sc;
         const int f = vfirst[yy] - top, n = vcount[yy];
         int32_t ss = 1 << 21;
-        for (int t = 0; t < n; ++t) ss += tmp[(f + t) * kStripCols + xx] * vk[yy * kMaxTaps + t];
+        for (int t = 0; t < n; ++t) ss += tmp[(f + t) * strip + xx] * vk[yy * kMaxTaps + t];
         crop[yy * bw + x0 + xx] = clip8d(ss);
       }
       __syncthreads();
