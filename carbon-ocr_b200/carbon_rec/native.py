@@ -24,7 +24,7 @@ _NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA
 
 # every entry point include/carbon_rec.h declares
 EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec_set_pages", "crec_prefetch_pages",
-           "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_width_bucket", "crec_crop_region",
+           "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_ctc_greedy", "crec_width_bucket", "crec_crop_region",
            "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats",
            "crec_profile"]
 
@@ -100,6 +100,7 @@ def lib() -> C.CDLL:
         L.crec_recognize.argtypes = [p, p, p, i, i, C.POINTER(Lines)]
         L.crec_recognize_lines.argtypes = [p, p, p, p, i, C.POINTER(Lines)]
         L.crec_recognize_crops.argtypes = [p, p, i, p, p, i, C.POINTER(Lines)]
+        L.crec_ctc_greedy.argtypes = [p, i, i, i, p, C.POINTER(Lines), p, C.c_char_p, C.c_size_t]
         L.crec_width_bucket.argtypes = [i]
         L.crec_crop_region.argtypes = [C.POINTER(Box), C.POINTER(CropRule), p, C.POINTER(i)]
         L.crec_stream.argtypes = [p]
@@ -111,6 +112,21 @@ def lib() -> C.CDLL:
         L.crec_profile.argtypes = [p, i, C.POINTER(ProfileEntry), i]
         _lib = L
     return _lib
+
+
+def ctc_greedy(logits_ptr: int, n: int, classes: int, frames: int, lengths, stream: int = 0):
+    """carbon::cuda::ctc_greedy on device logits [n][classes][frames] at logits_ptr: (list of CtcLine, lengths)."""
+    lens = np.ascontiguousarray(lengths, np.int32)
+    cap = max(1, n * frames)
+    bufs = dict(counts=np.zeros(n, np.int32), lengths=np.zeros(n, np.int32), offsets=np.zeros(n, np.int32),
+                ids=np.zeros(cap, np.int32), frames=np.zeros(cap, np.int32), probs=np.zeros(cap, np.float32))
+    s = Lines(*[bufs[k].ctypes.data for k in ("counts", "lengths", "offsets", "ids", "frames", "probs")], cap, 0)
+    err = C.create_string_buffer(512)
+    rc = lib().crec_ctc_greedy(int(logits_ptr), n, classes, frames, lens.ctypes.data, C.byref(s), stream or None,
+                               err, 512)
+    if rc != OK:
+        raise CrecError(rc, err.value.decode())
+    return RecDevice._unpack(bufs, n)
 
 
 def width_bucket(crop_width: int) -> int:

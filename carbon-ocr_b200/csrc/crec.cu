@@ -15,6 +15,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -23,6 +24,7 @@
 #include "../../include/carbon_rec.h"
 #include "conv_gemm.cuh"
 #include "crop_stem.cuh"
+#include "ctc.cuh"
 #include "dw_head.cuh"
 #include "sm100.cuh"
 
@@ -1263,6 +1265,79 @@ int crec_debug_crops(crec_handle* h, uint8_t* out, int pitch) {
   }
   if (!h->d_crops || h->crops_pitch != pitch) return set_error(h, CREC_E_INVALID, "debug crops not armed at this pitch");
   CK(cudaMemcpy(out, h->d_crops, static_cast<size_t>(h->last_n) * h->height * pitch, cudaMemcpyDeviceToHost));
+  return CREC_OK;
+}
+
+int crec_ctc_greedy(const float* logits, int n, int classes, int frames, const int32_t* lengths, crec_lines* out,
+                    void* stream, char* error, size_t error_size) {
+  auto fail = [&](int code, const std::string& msg) {
+    if (error && error_size) {
+      std::snprintf(error, error_size, "%s", msg.c_str());
+    }
+    return code;
+  };
+  if (n < 0 || classes <= 0 || frames < 0 || (n > 0 && (!logits || !lengths || !out)))
+    return fail(CREC_E_INVALID, "ctc_greedy: arguments");
+  if (!out) return fail(CREC_E_INVALID, "ctc_greedy: no output");
+  out->total = 0;
+  if (n == 0 || frames == 0) {
+    for (int i = 0; i < n; ++i) out->counts[i] = out->lengths[i] = out->offsets[i] = 0;
+    return CREC_OK;
+  }
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t cells = static_cast<size_t>(n) * frames;
+  // per-call scratch (stream-ordered): lengths, each frame's best class and probability, the slots, counts
+  int32_t *d_len = nullptr, *d_arg = nullptr, *d_ids = nullptr, *d_starts = nullptr, *d_count = nullptr;
+  float *d_prob = nullptr, *d_probs = nullptr;
+  auto release = [&]() {
+    cudaFreeAsync(d_len, s);
+    cudaFreeAsync(d_arg, s);
+    cudaFreeAsync(d_ids, s);
+    cudaFreeAsync(d_starts, s);
+    cudaFreeAsync(d_count, s);
+    cudaFreeAsync(d_prob, s);
+    cudaFreeAsync(d_probs, s);
+  };
+  cudaError_t e = cudaSuccess;
+  if ((e = cudaMallocAsync(&d_len, sizeof(int32_t) * n, s)) != cudaSuccess ||
+      (e = cudaMallocAsync(&d_arg, sizeof(int32_t) * cells, s)) != cudaSuccess ||
+      (e = cudaMallocAsync(&d_ids, sizeof(int32_t) * cells, s)) != cudaSuccess ||
+      (e = cudaMallocAsync(&d_starts, sizeof(int32_t) * cells, s)) != cudaSuccess ||
+      (e = cudaMallocAsync(&d_count, sizeof(int32_t) * n, s)) != cudaSuccess ||
+      (e = cudaMallocAsync(&d_prob, sizeof(float) * cells, s)) != cudaSuccess ||
+      (e = cudaMallocAsync(&d_probs, sizeof(float) * cells, s)) != cudaSuccess) {
+    release();
+    return fail(e == cudaErrorMemoryAllocation ? CREC_E_NOMEM : CREC_E_CUDA,
+                std::string("ctc_greedy: ") + cudaGetErrorString(e));
+  }
+  std::vector<int32_t> count(n), ids(cells), starts(cells);
+  std::vector<float> probs(cells);
+  e = cudaMemcpyAsync(d_len, lengths, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) {
+    ctc_argmax_kernel<<<n, 256, 0, s>>>(logits, classes, frames, d_len, d_arg, d_prob);
+    ctc_collapse_lines_kernel<<<(n + 127) / 128, 128, 0, s>>>(n, frames, d_len, d_arg, d_prob, d_ids, d_starts,
+                                                               d_probs, d_count);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(count.data(), d_count, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(ids.data(), d_ids, sizeof(int32_t) * cells, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(starts.data(), d_starts, sizeof(int32_t) * cells, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(probs.data(), d_probs, sizeof(float) * cells, cudaMemcpyDeviceToHost, s);
+  release();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail(CREC_E_CUDA, std::string("ctc_greedy: ") + cudaGetErrorString(e));
+  for (int i = 0; i < n; ++i) {
+    const int k = count[i];
+    out->counts[i] = k;
+    out->lengths[i] = std::min(std::max(lengths[i], 0), frames);
+    out->offsets[i] = static_cast<int32_t>(out->total);
+    if (out->total + k > out->capacity) return fail(CREC_E_RANGE, "ctc_greedy: crec_lines capacity too small");
+    const size_t b = static_cast<size_t>(i) * frames;
+    std::memcpy(out->ids + out->total, ids.data() + b, sizeof(int32_t) * k);
+    std::memcpy(out->frames + out->total, starts.data() + b, sizeof(int32_t) * k);
+    std::memcpy(out->probs + out->total, probs.data() + b, sizeof(float) * k);
+    out->total += k;
+  }
   return CREC_OK;
 }
 

@@ -138,6 +138,15 @@ CREC_API int crec_recognize_lines(crec_handle* h, const int32_t* page_of, const 
 CREC_API int crec_recognize_crops(crec_handle* h, const uint8_t* crops, int pitch, const int32_t* widths, const int32_t* bw,
                          int n, crec_lines* out);
 
+/* carbon::cuda::ctc_greedy (carbon/include/carbon/cuda.h:58-62 of the reference): greedy CTC
+ * decoding of device logits [n][classes][frames] (float32), each line's first lengths[i] frames
+ * (a host array), queued on `stream` (a cudaStream_t; null the default stream) and waited for.
+ * Ids, frames and probabilities are carbon::ctc_greedy's, bit for bit.  Its scratch is allocated
+ * and freed on the stream by the call.  No handle: a message for an error goes to error[0,
+ * error_size) (may be null).  out->lengths gets min(lengths[i], frames). */
+CREC_API int crec_ctc_greedy(const float* logits, int n, int classes, int frames, const int32_t* lengths,
+                             crec_lines* out, void* stream, char* error, size_t error_size);
+
 CREC_API int crec_width_bucket(int crop_width);
 /* carbon::crop_region: the page rectangle a box's crop resamples (region[4]: x0, y0, x1, y1) and
  * the crop's width. */
