@@ -24,7 +24,7 @@ _NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA
 
 # every entry point include/carbon_rec.h declares
 EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec_set_pages", "crec_prefetch_pages",
-           "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_ctc_greedy", "crec_width_bucket", "crec_crop_region",
+           "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_ctc_greedy", "crec_ctc_greedy_noalloc", "crec_width_bucket", "crec_crop_region",
            "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats",
            "crec_profile"]
 
@@ -101,6 +101,7 @@ def lib() -> C.CDLL:
         L.crec_recognize_lines.argtypes = [p, p, p, p, i, C.POINTER(Lines)]
         L.crec_recognize_crops.argtypes = [p, p, i, p, p, i, C.POINTER(Lines)]
         L.crec_ctc_greedy.argtypes = [p, i, i, i, p, C.POINTER(Lines), p, C.c_char_p, C.c_size_t]
+        L.crec_ctc_greedy_noalloc.argtypes = [p, i, i, i, p, p, p, p, p, p, C.c_char_p, C.c_size_t]
         L.crec_width_bucket.argtypes = [i]
         L.crec_crop_region.argtypes = [C.POINTER(Box), C.POINTER(CropRule), p, C.POINTER(i)]
         L.crec_stream.argtypes = [p]
@@ -127,6 +128,16 @@ def ctc_greedy(logits_ptr: int, n: int, classes: int, frames: int, lengths, stre
     if rc != OK:
         raise CrecError(rc, err.value.decode())
     return RecDevice._unpack(bufs, n)
+
+
+def ctc_greedy_noalloc(logits_ptr: int, n: int, classes: int, frames: int, lengths_ptr: int, counts_ptr: int,
+                       ids_ptr: int, starts_ptr: int, probs_ptr: int, stream: int = 0) -> None:
+    """crec_ctc_greedy_noalloc: every pointer a device address; queued on `stream`, not waited for."""
+    err = C.create_string_buffer(256)
+    rc = lib().crec_ctc_greedy_noalloc(int(logits_ptr), n, classes, frames, int(lengths_ptr), int(counts_ptr),
+                                       int(ids_ptr), int(starts_ptr), int(probs_ptr), stream or None, err, 256)
+    if rc != OK:
+        raise CrecError(rc, err.value.decode())
 
 
 def width_bucket(crop_width: int) -> int:

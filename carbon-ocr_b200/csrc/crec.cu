@@ -18,6 +18,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1064,6 +1065,40 @@ int pages_common(crec_handle* h, const crec_page* pages, int n) {
 
 }  // namespace
 
+// ---------------------------------------------------------------- greedy CTC without allocating
+//
+// crec_ctc_greedy_noalloc's scratch: each frame's best class (int32) and probability (float), for
+// at most kNoAllocFrames frames.  A file-scope device array: every GPU that loads this library
+// holds these 4 MiB until the process exits, and every call on a device shares them.
+constexpr size_t kNoAllocFrames = size_t{1} << 19;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocFrames * 8];
+
+namespace {
+
+constexpr int kNoAllocDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[kNoAllocDevices] = {};
+
+// The scratch's device address on the current device, taken once per device (the host-side name
+// g_noalloc_scratch is only a stand-in for it, not a device address).
+cudaError_t noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kNoAllocDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_addr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_addr[dev] = ptr;
+  }
+  *out = g_noalloc_addr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
 extern "C" {
 
 int crec_width_bucket(int w) {
@@ -1338,6 +1373,38 @@ int crec_ctc_greedy(const float* logits, int n, int classes, int frames, const i
     std::memcpy(out->probs + out->total, probs.data() + b, sizeof(float) * k);
     out->total += k;
   }
+  return CREC_OK;
+}
+
+int crec_ctc_greedy_noalloc(const float* logits, int n, int classes, int frames, const int32_t* lengths,
+                            int32_t* counts, int32_t* ids, int32_t* starts, float* probs, void* stream, char* error,
+                            size_t error_size) {
+  auto fail = [&](int code, const char* msg) {
+    if (error && error_size) std::snprintf(error, error_size, "%s", msg);
+    return code;
+  };
+  if (n < 0 || classes <= 0 || frames < 0 ||
+      (n > 0 && frames > 0 && (!logits || !lengths || !counts || !ids || !starts || !probs)))
+    return fail(CREC_E_INVALID, "ctc_greedy_noalloc: arguments");
+  const size_t cells = static_cast<size_t>(n) * static_cast<size_t>(frames);
+  if (cells > kNoAllocFrames) {
+    char msg[160];
+    std::snprintf(msg, sizeof msg, "ctc_greedy_noalloc: n x frames = %zu frames, more than its scratch's %zu",
+                  cells, kNoAllocFrames);
+    return fail(CREC_E_RANGE, msg);
+  }
+  if (n == 0) return CREC_OK;
+  void* scratch = nullptr;
+  cudaError_t e = noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return fail(CREC_E_CUDA, cudaGetErrorString(e));
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* arg = static_cast<int32_t*>(scratch);
+  float* prob = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kNoAllocFrames * 4);
+  // nothing in the scratch needs to start at zero: the argmax writes every frame the collapse reads
+  if (frames > 0) ctc_argmax_kernel<<<n, 256, 0, s>>>(logits, classes, frames, lengths, arg, prob);
+  ctc_collapse_lines_kernel<<<(n + 127) / 128, 128, 0, s>>>(n, frames, lengths, arg, prob, ids, starts, probs, counts);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CREC_E_CUDA, cudaGetErrorString(e));
   return CREC_OK;
 }
 

@@ -147,6 +147,22 @@ CREC_API int crec_recognize_crops(crec_handle* h, const uint8_t* crops, int pitc
 CREC_API int crec_ctc_greedy(const float* logits, int n, int classes, int frames, const int32_t* lengths,
                              crec_lines* out, void* stream, char* error, size_t error_size);
 
+/* crec_ctc_greedy without allocating: for callers that cannot have a library call cudaMalloc or
+ * cudaMallocAsync -- a process whose device memory all belongs to its own allocator (a framework's
+ * caching allocator, an arena reserved at start-up) or a serving path that fixed its memory before
+ * it started.  No counterpart in the reference.  Everything is in device memory and queued on
+ * `stream` without waiting: logits [n][classes][frames] (float32), lengths [n], and the outputs
+ * counts [n] and ids, starts, probs [n][frames] (line i's characters at [i * frames, i * frames +
+ * counts[i])), the same values as crec_ctc_greedy's.  The per-frame scratch is a 4 MiB device
+ * array inside this library: n x frames may be at most 524,288 (CREC_E_RANGE beyond, nothing
+ * queued).  Each call on a device uses the same array, so calls whose work overlaps on the GPU
+ * (two streams, two threads) race: order them on one stream.  The first call on each device looks
+ * the array's address up (cudaGetSymbolAddress, with that device current): make it before any
+ * stream capture. */
+CREC_API int crec_ctc_greedy_noalloc(const float* logits, int n, int classes, int frames, const int32_t* lengths,
+                                     int32_t* counts, int32_t* ids, int32_t* starts, float* probs, void* stream,
+                                     char* error, size_t error_size);
+
 CREC_API int crec_width_bucket(int crop_width);
 /* carbon::crop_region: the page rectangle a box's crop resamples (region[4]: x0, y0, x1, y1) and
  * the crop's width. */
