@@ -53,17 +53,18 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--max-columns", type=int, default=1 << 21)
     ap.add_argument("--max-lines", type=int, default=8192)
+    ap.add_argument("--pages", type=int, default=PAGES_TOTAL, help="page slots of the whole job (1024: config 5)")
     ap.add_argument("--no-fp16", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
 
-def workload(rank: int, world: int):
+def workload(rank: int, world: int, pages_total: int = PAGES_TOTAL):
     """The rank's shard: distinct pages, and per line its page index (into the distinct pages),
     box and bucket width."""
     from carbon_rec import native, synth
     pages, boxes = synth.pages(SEED, DISTINCT, PAGE_W, PAGE_H, LINES_PER_PAGE)
-    slots = range(rank * PAGES_TOTAL // world, (rank + 1) * PAGES_TOTAL // world)
+    slots = range(rank * pages_total // world, (rank + 1) * pages_total // world)
     page_of = np.concatenate([np.full(LINES_PER_PAGE, s % DISTINCT, np.int32) for s in slots])
     allb = np.concatenate([boxes[s % DISTINCT] for s in slots])
     flat = np.concatenate(boxes)
@@ -218,8 +219,7 @@ def main() -> int:
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
-    pages, boxes, page_of, allb, bws = workload(rank, world)
-    n_lines = len(page_of)
+    pages, boxes, page_of, allb, bws = workload(rank, world, args.pages)
     _, _, fp, i8 = model.make_rec_latin(0)
     blobs = {"int8": netdef.compile_model(i8).to_blob(), "fp16": netdef.compile_model(fp).to_blob()}
     # pinned host pages (the e2e leg uploads from them) and their row runs
@@ -264,7 +264,7 @@ def main() -> int:
                                max_lines=args.max_lines, max_width=1024, max_columns=args.max_columns,
                                max_pages=DISTINCT, max_page_bytes=DISTINCT * PAGE_W * PAGE_H)
         dev.set_pages(host_pages)  # resident for the device-time leg
-        step = lambda: dev.recognize_lines(page_of, allb, bws)  # noqa: E731
+        step = lambda: dev.recognize_lines(page_of, allb, bws, flat=True)  # noqa: E731
         for _ in range(args.warmup):
             step()
         if prec == "int8":
@@ -280,16 +280,16 @@ def main() -> int:
 
         def e2e_step():
             dev.set_pages(host_pages, rows)
-            dev.recognize_lines(page_of, allb, bws)
+            dev.recognize_lines(page_of, allb, bws, flat=True)
 
         for _ in range(max(1, args.warmup // 2)):
             e2e_step()
         esecs = max_over_ranks(timed(dev, e2e_step, args.steps))
         dev.set_pages(host_pages, rows)
         h2d_pages = dev.last_stats()["h2d_bytes"]
-        dev.recognize_lines(page_of, allb, bws)
+        dev.recognize_lines(page_of, allb, bws, flat=True)
         st = dev.last_stats()
-        total_lines = PAGES_TOTAL * LINES_PER_PAGE
+        total_lines = args.pages * LINES_PER_PAGE
         results[prec] = {"value": total_lines * args.steps / secs, "ms_per_step": 1000 * secs / args.steps,
                          "e2e": {"value": total_lines * args.steps / esecs, "unit": "lines/s",
                                  "h2d_bytes_per_step": int(h2d_pages + st["h2d_bytes"]),
@@ -320,7 +320,9 @@ def main() -> int:
             "warmup": args.warmup, "ms_per_step": r8["ms_per_step"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "u8xs8->s32 (INT8 engine)", "data": "synthetic (seeded pages, random-init "
             "rec-latin weights, seed 0)",
-            "config": {"workload": WORKLOAD, "lines": PAGES_TOTAL * LINES_PER_PAGE, "parallelism": f"pages/{world}",
+            "config": {"workload": WORKLOAD if args.pages == PAGES_TOTAL else
+                       f"{args.pages} of config 5's pages ({args.pages * LINES_PER_PAGE} lines)",
+                       "lines": args.pages * LINES_PER_PAGE, "parallelism": f"pages/{world}",
                        "l2": "inputs larger than L2 (278 MB of pages; GB-scale activations)",
                        "max_columns_per_run": args.max_columns},
             "e2e": r8["e2e"],

@@ -262,10 +262,15 @@ class RecDevice:
         self._check(lib().crec_prefetch_pages(self._h, descs, len(arr), None))
 
     def _lines(self, n: int, cap: int):
-        bufs = dict(counts=np.zeros(n, np.int32), lengths=np.zeros(n, np.int32), offsets=np.zeros(n, np.int32),
-                    ids=np.zeros(cap, np.int32), frames=np.zeros(cap, np.int32), probs=np.zeros(cap, np.float32))
+        bufs = dict(counts=np.empty(n, np.int32), lengths=np.empty(n, np.int32), offsets=np.empty(n, np.int32),
+                    ids=np.empty(cap, np.int32), frames=np.empty(cap, np.int32), probs=np.empty(cap, np.float32))
         s = Lines(*[bufs[k].ctypes.data for k in ("counts", "lengths", "offsets", "ids", "frames", "probs")], cap, 0)
         return bufs, s
+
+    @staticmethod
+    def _flat(bufs, total: int) -> dict:
+        """The decodings as flat arrays: counts, lengths, offsets per line; ids, frames, probs packed."""
+        return {k: (v[:total] if k in ("ids", "frames", "probs") else v) for k, v in bufs.items()}
 
     @staticmethod
     def _unpack(bufs, n: int):
@@ -284,17 +289,18 @@ class RecDevice:
         self._check(lib().crec_recognize(self._h, po.ctypes.data, b.ctypes.data, n, int(bw), C.byref(s)))
         return self._unpack(bufs, n)
 
-    def recognize_lines(self, page_of, boxes, bw=None):
-        """Any number of lines, each at its own bucket width (bw[i], or the width ladder's bucket)."""
+    def recognize_lines(self, page_of, boxes, bw=None, flat: bool = False):
+        """Any number of lines, each at its own bucket width (bw[i], or the width ladder's bucket):
+        (list of CtcLine, lengths), or with flat the arrays as the C ABI fills them."""
         po = np.ascontiguousarray(page_of, np.int32)
         b = _boxes(boxes)
         n = len(po)
         bwa = None if bw is None else np.ascontiguousarray(bw, np.int32)
-        cap = max(1, n * (self.max_width // self.crop.frame_px))
+        cap = max(1, (int(bwa.sum()) if bwa is not None else n * self.max_width) // self.crop.frame_px)
         bufs, s = self._lines(n, cap)
         self._check(lib().crec_recognize_lines(self._h, po.ctypes.data, b.ctypes.data,
                                                None if bwa is None else bwa.ctypes.data, n, C.byref(s)))
-        return self._unpack(bufs, n)
+        return self._flat(bufs, s.total) if flat else self._unpack(bufs, n)
 
     def recognize_crops(self, crops, widths, bw):
         """Ready crops [n, height, pitch] uint8 (line i's first bw[i] columns finished and padded), their crop

@@ -183,12 +183,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
         res = p.res + (oy + p.res_ph) * p.res_pitch + static_cast<long long>(ox >> p.res_shift) * p.res_cp * p.ebytes;
       const int c0 = n * p.nt;
       const int cend = min(c0 + p.nt, p.cp_out);
-      for (int cb = c0; cb < c0 + p.nt; cb += 16) {
-        uint32_t r[16];
-        tmem_ld16(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * 256 + cb - c0),
-                  r);
-        tmem_wait_ld();
-        if (!inside || cb >= cend) continue;
+      // 16 channels from r[0..16) to the output at channel cb
+      auto store16 = [&](const uint32_t* r, int cb) {
+        if (!inside || cb >= cend) return;
         if constexpr (kInt8) {
           alignas(16) uint8_t o[16];
           if (!valid) {
@@ -201,8 +198,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int j = cb + i;
-              const int32_t s = static_cast<int32_t>(r[i]) - p.in_zero * p.colsum[j];
-              float v = __fmul_rn(static_cast<float>(s), p.scale[j]);
+              const int32_t sum = static_cast<int32_t>(r[i]) - p.in_zero * p.colsum[j];
+              float v = __fmul_rn(static_cast<float>(sum), p.scale[j]);
               v = __fadd_rn(v, p.bias[j]);
               if (res) v = __fadd_rn(v, __fmul_rn(static_cast<float>(static_cast<int32_t>(rb[i]) - p.res_zero), p.res_scale));
               if (p.relu) v = v > 0.0f ? v : 0.0f;
@@ -237,6 +234,29 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
           *reinterpret_cast<uint4*>(dst + cb * 2) = *reinterpret_cast<const uint4*>(o);
           *reinterpret_cast<uint4*>(dst + cb * 2 + 16) = *reinterpret_cast<const uint4*>(o + 8);
         }
+      };
+      // TMEM read 32 columns at a time, the next load in flight while the current is stored
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * 256);
+      const int groups = p.nt / 16;
+      uint32_t ra[32], rb[32];
+      if (groups >= 2) tmem_ld32(taddr, ra); else tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(ra));
+      tmem_wait_ld();
+      tmem_pin(ra);
+      for (int g = 0; g < groups;) {
+        const int w = g + 1 < groups ? 2 : 1;
+        const int gn = g + w;
+        if (gn + 1 < groups) {
+          tmem_ld32(taddr + gn * 16, rb);
+        } else if (gn < groups) {
+          tmem_ld16(taddr + gn * 16, *reinterpret_cast<uint32_t(*)[16]>(rb));
+        }
+        store16(ra, c0 + g * 16);
+        if (w == 2) store16(ra + 16, c0 + g * 16 + 16);
+        tmem_wait_ld();
+        tmem_pin(rb);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ra[i] = rb[i];
+        g = gn;
       }
       tc_fence_before();
       __syncwarp();

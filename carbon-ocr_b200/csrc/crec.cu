@@ -140,13 +140,18 @@ struct crec_handle {
   LineDesc* hs_lines = nullptr;
   int* hs_frame0 = nullptr;
   int* hs_length = nullptr;
-  int32_t* hs_count = nullptr;
   uint8_t* hs_mask = nullptr;
-  int32_t* hs_ids = nullptr;
-  int32_t* hs_frames = nullptr;
-  float* hs_probs = nullptr;
-  size_t cap_lines = 0, cap_frame0 = 0, cap_length = 0, cap_count = 0, cap_mask = 0, cap_ids = 0, cap_frames = 0,
-         cap_probs = 0;
+  size_t cap_lines = 0, cap_frame0 = 0, cap_length = 0, cap_mask = 0;
+  // a call's packed decodings on the device (grown on demand): every line's count and offset, the
+  // characters end to end, the running total
+  int32_t* dp_counts = nullptr;
+  int32_t* dp_offsets = nullptr;
+  int32_t* dp_ids = nullptr;
+  int32_t* dp_frames = nullptr;
+  float* dp_probs = nullptr;
+  long long* d_total = nullptr;
+  long long* h_total = nullptr;  // pinned
+  size_t cap_dp_lines = 0, cap_dp_chars = 0;
   int32_t* d_frame_id = nullptr;
   float* d_frame_prob = nullptr;
   int32_t* d_count = nullptr;
@@ -161,6 +166,7 @@ struct crec_handle {
   uint8_t* d_crops_in = nullptr;  // ready crops given by crec_recognize_crops
   int crops_in_pitch = 0;
   const uint8_t* run_crops = nullptr;  // this run's ready crops on the device, or null
+  const int* run_bw = nullptr;         // this run's bucket widths (host)
   // the last call's statistics, and the optional per-launch profile (CUDA events on the stream)
   long long st_runs = 0, st_launches = 0, st_h2d = 0, st_d2h = 0;
   bool profile = false;
@@ -326,7 +332,7 @@ int plan_model(crec_handle* h) {
     y.extra = 0;
     y.real = true;
     if (i == 0) {
-      if (l.in != h->inp || l.kind != kKindConv || l.cin != 1 || l.kh * l.kw > 9 || l.residual >= 0 || l.cout > 256 ||
+      if (l.in != h->inp || l.kind != kKindConv || l.cin != 1 || l.kh * l.kw > 9 || l.residual >= 0 || l.cout > kStemMaxOut ||
           l.pt != l.pb || l.pl != l.pr)
         return set_error(h, CREC_E_MODEL, "the first layer must be a 1-channel convolution of at most 3x3");
     } else if (static_cast<int>(i) == static_cast<int>(L.size()) - 1) {
@@ -496,9 +502,10 @@ int encode_map(crec_handle* h, CUtensorMap* m, const void* base, uint64_t d0, ui
 
 // The crop kernel's shared memory: a crop at the widest bucket, the strip intermediate, the
 // vertical coefficients, the histogram and counters.
-size_t crop_smem_bytes(const crec_handle* h) {
-  return ((static_cast<size_t>(h->height) * h->cfg.max_width + 15) & ~size_t(15)) + kStripBytes +
-         (static_cast<size_t>(h->height) * kMaxTaps + 2 * h->height + 256 + 8) * 4;
+size_t crop_smem_bytes(const crec_handle* h, int max_bw) {
+  return ((static_cast<size_t>(h->height) * max_bw + 15) & ~size_t(15)) + kStripBytes + kCoefBytes +
+         (static_cast<size_t>(h->height) * kMaxTaps + 2 * h->height + 256 + 8) * 4 +
+         (kStemMaxOut * 9 + 2 * kStemMaxOut) * 4 + 256;
 }
 
 // Kernel kinds of the profile: 0 crop+stem, 1 dense convolutions (tcgen05), 2 depthwise, 3 head+CTC, 4 collapse.
@@ -602,7 +609,10 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.out_pitch = s0.pitch;
     p.out_shift = s0.shift;
     p.err = h->d_err;
-    const size_t smem = crop_smem_bytes(h);
+    int max_bw = 8;
+    for (int i = 0; i < n; ++i) max_bw = std::max(max_bw, h->run_bw[i]);
+    p.max_bw = max_bw;
+    const size_t smem = crop_smem_bytes(h, max_bw);
     ProfScope prof(h, kProfCrop);
     // the attribute is the function's, for every handle in the process: set it for this one's size
     if (h->int8) {
@@ -795,6 +805,19 @@ int grow_pinned(crec_handle* h, T** p, size_t* cap, size_t need) {
   return CREC_OK;
 }
 
+template <class T>
+int grow_device(crec_handle* h, T** p, size_t* cap, size_t need) {
+  if (need <= *cap) return CREC_OK;
+  const size_t n = std::max(need, *cap * 2);
+  CK(cudaStreamSynchronize(h->stream));  // nothing queued may still use the old buffer
+  cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  CK(cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T)));
+  *cap = n;
+  return CREC_OK;
+}
+
 struct Source {  // where a call's lines come from
   const int32_t* page_of = nullptr;
   const crec_box* boxes = nullptr;
@@ -882,19 +905,25 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
     a = b;
   }
   int rc;
+  size_t cap_dp_lines = h->cap_dp_lines, cap_dp_chars = h->cap_dp_chars, cap_dp_a = cap_dp_lines,
+         cap_dp_c = cap_dp_chars, cap_dp_d = cap_dp_chars;
   if ((rc = grow_pinned(h, &h->hs_lines, &h->cap_lines, n)) || (rc = grow_pinned(h, &h->hs_frame0, &h->cap_frame0, n)) ||
-      (rc = grow_pinned(h, &h->hs_length, &h->cap_length, n)) || (rc = grow_pinned(h, &h->hs_count, &h->cap_count, n)) ||
+      (rc = grow_pinned(h, &h->hs_length, &h->cap_length, n)) ||
       (rc = grow_pinned(h, &h->hs_mask, &h->cap_mask, mask_total)) ||
-      (rc = grow_pinned(h, &h->hs_ids, &h->cap_ids, frame_total)) ||
-      (rc = grow_pinned(h, &h->hs_frames, &h->cap_frames, frame_total)) ||
-      (rc = grow_pinned(h, &h->hs_probs, &h->cap_probs, frame_total)))
+      (rc = grow_device(h, &h->dp_counts, &cap_dp_lines, n)) || (rc = grow_device(h, &h->dp_offsets, &cap_dp_a, n)) ||
+      (rc = grow_device(h, &h->dp_ids, &cap_dp_chars, frame_total)) ||
+      (rc = grow_device(h, &h->dp_frames, &cap_dp_c, frame_total)) ||
+      (rc = grow_device(h, &h->dp_probs, &cap_dp_d, frame_total)))
     return rc;
+  h->cap_dp_lines = std::min(cap_dp_lines, cap_dp_a);
+  h->cap_dp_chars = std::min({cap_dp_chars, cap_dp_c, cap_dp_d});
   cudaStream_t s = h->stream;
   h->st_runs = static_cast<long long>(runs.size());
   h->st_launches = 0;
   h->st_h2d = 0;
-  h->st_d2h = 4;  // the error word
+  h->st_d2h = 4 + 8;  // the error word, the total
   CK(cudaMemsetAsync(h->d_err, 0, sizeof(int), s));
+  CK(cudaMemsetAsync(h->d_total, 0, sizeof(long long), s));
   for (const Run& r : runs) {
     long long cols = 0;
     if ((rc = layout_run(h, src, bw, r.a, r.b, r.mask_off, &cols))) return rc;
@@ -913,19 +942,37 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
     h->st_h2d += static_cast<long long>(sizeof(LineDesc) * m + cols / 8 + 2 * sizeof(int) * m);
     if (src.crops) h->st_h2d += static_cast<long long>(m) * h->height * src.pitch;
     add_run_ops(h, bw, r.a, r.b);
+    h->run_bw = bw + r.a;
     if ((rc = launch_run(h, m, cols, h->d_crops != nullptr))) return rc;
-    const size_t frames = static_cast<size_t>(cols >> h->head_shift);
-    h->st_d2h += static_cast<long long>(sizeof(int32_t) * m + 12 * frames);
-    CK(cudaMemcpyAsync(h->hs_count + r.a, h->d_count, sizeof(int32_t) * m, cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(h->hs_ids + r.frame_off, h->d_ids, sizeof(int32_t) * frames, cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(h->hs_frames + r.frame_off, h->d_frames, sizeof(int32_t) * frames, cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(h->hs_probs + r.frame_off, h->d_probs, sizeof(float) * frames, cudaMemcpyDeviceToHost, s));
+    {  // this run's characters packed after the previous runs'
+      ProfScope prof(h, kProfCollapse);
+      scan_counts_kernel<<<1, 1024, 0, s>>>(h->d_count, m, h->dp_counts + r.a, h->dp_offsets + r.a, h->d_total);
+      pack_kernel<<<(m * 32 + 255) / 256, 256, 0, s>>>(h->d_ids, h->d_frames, h->d_probs, h->d_frame0,
+                                                      h->dp_counts + r.a, h->dp_offsets + r.a, m, h->dp_ids,
+                                                      h->dp_frames, h->dp_probs);
+      ++h->st_launches;
+    }
+    CK(cudaGetLastError());
   }
   CK(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(h->h_total, h->d_total, sizeof(long long), cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(out->counts, h->dp_counts, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(out->offsets, h->dp_offsets, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
   if (h->profile) collect_profile(h);
   if (*h->h_err)
     return set_error(h, CREC_E_TIMEOUT, "a kernel's bounded wait ran out (device error " + std::to_string(*h->h_err) + ")");
+  const long long total = *h->h_total;
+  if (total > out->capacity) return set_error(h, CREC_E_RANGE, "crec_lines: capacity too small");
+  if (total > 0) {  // the characters themselves, and nothing else
+    CK(cudaMemcpyAsync(out->ids, h->dp_ids, sizeof(int32_t) * total, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(out->frames, h->dp_frames, sizeof(int32_t) * total, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(out->probs, h->dp_probs, sizeof(float) * total, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+  }
+  h->st_d2h += static_cast<long long>(8 * n + 12 * total);
+  std::memcpy(out->lengths, h->hs_length, sizeof(int32_t) * n);
+  out->total = total;
   const Run& last = runs.back();
   h->last_n = last.b - last.a;
   h->last_cols = last.cols;
@@ -934,20 +981,6 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
   for (int i = last.a; i < last.b; ++i) {
     h->last_seg[i - last.a] = h->hs_lines[i].seg;
     h->last_bw[i - last.a] = h->hs_lines[i].bw;
-  }
-  for (const Run& r : runs) {
-    for (int i = r.a; i < r.b; ++i) {
-      const int k = h->hs_count[i];
-      out->counts[i] = k;
-      out->lengths[i] = h->hs_length[i];
-      out->offsets[i] = static_cast<int32_t>(out->total);
-      if (out->total + k > out->capacity) return set_error(h, CREC_E_RANGE, "crec_lines: capacity too small");
-      const size_t f0 = r.frame_off + static_cast<size_t>(h->hs_frame0[i]);
-      std::memcpy(out->ids + out->total, h->hs_ids + f0, sizeof(int32_t) * k);
-      std::memcpy(out->frames + out->total, h->hs_frames + f0, sizeof(int32_t) * k);
-      std::memcpy(out->probs + out->total, h->hs_probs + f0, sizeof(float) * k);
-      out->total += k;
-    }
   }
   return CREC_OK;
 }
@@ -983,11 +1016,14 @@ void free_all(crec_handle* h) {
   cudaFreeHost(h->hs_lines);
   cudaFreeHost(h->hs_frame0);
   cudaFreeHost(h->hs_length);
-  cudaFreeHost(h->hs_count);
   cudaFreeHost(h->hs_mask);
-  cudaFreeHost(h->hs_ids);
-  cudaFreeHost(h->hs_frames);
-  cudaFreeHost(h->hs_probs);
+  cudaFreeHost(h->h_total);
+  cudaFree(h->dp_counts);
+  cudaFree(h->dp_offsets);
+  cudaFree(h->dp_ids);
+  cudaFree(h->dp_frames);
+  cudaFree(h->dp_probs);
+  cudaFree(h->d_total);
   cudaFreeHost(h->h_err);
   for (cudaEvent_t e : h->ev_pool) cudaEventDestroy(e);
   if (h->stream) cudaStreamDestroy(h->stream);
@@ -1048,8 +1084,10 @@ int open_impl(crec_handle* h, const crec_config* c) {
       (rc = dev_alloc(h, &h->d_ids, frames)) || (rc = dev_alloc(h, &h->d_frames, frames)) ||
       (rc = dev_alloc(h, &h->d_probs, frames)) || (rc = dev_alloc(h, &h->d_err, 1)))
     return rc;
-  if ((rc = host_alloc(h, &h->h_err, 1))) return rc;
-  if (crop_smem_bytes(h) > 232448) return set_error(h, CREC_E_INVALID, "max_width: the crop kernel's shared memory");
+  if ((rc = host_alloc(h, &h->h_err, 1)) || (rc = host_alloc(h, &h->h_total, 1)) ||
+      (rc = dev_alloc(h, &h->d_total, 1)))
+    return rc;
+  if (crop_smem_bytes(h, c->max_width) > 232448) return set_error(h, CREC_E_INVALID, "max_width: the crop kernel's shared memory");
   return CREC_OK;
 }
 

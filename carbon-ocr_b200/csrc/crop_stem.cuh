@@ -25,12 +25,13 @@
 
 namespace crec {
 
-constexpr int kCropThreads = 256;
-constexpr int kMaxTaps = 32;        // taps a sample may have: downscales up to 15x (the host checks)
-constexpr int kStripBytes = 48 << 10;  // the horizontal pass's intermediate: source rows x strip columns
-constexpr int kMaxStripCols = 256;  // output columns a horizontal strip at most
-constexpr int kMaxSrcRows = 1024;   // source rows a crop's vertical windows may span (the host checks)
-constexpr int kStemOut = 32;        // the stem's output channels this kernel supports (padded)
+constexpr int kCropThreads = 512;
+constexpr int kMaxTaps = 32;          // taps a sample may have: downscales up to 15x (the host checks)
+constexpr int kStripBytes = 32 << 10;  // the horizontal pass's intermediate: source rows x strip columns
+constexpr int kCoefBytes = 16 << 10;   // a strip's horizontal coefficients: columns x taps x 4 bytes
+constexpr int kMaxStripCols = 512;    // output columns a strip at most
+constexpr int kMaxSrcRows = 1024;     // source rows a crop's vertical windows may span (the host checks)
+constexpr int kStemMaxOut = 64;       // the stem's output channels at most (padded)
 
 struct PageDesc {
   const uint8_t* data;
@@ -53,6 +54,7 @@ struct CropParams {
   int crops_pitch;     // bytes per crop row in crops_out
   const uint8_t* crops_in;  // optional: crops given ready, [n][height][crops_in_pitch]: no resampling, no finish
   int crops_in_pitch;
+  int max_bw;  // the widest bucket of the run (the crop buffer's size in shared memory)
   // stem: 3x3 (kh x kw), stride (sh, sw), pads (pt, pl), one input channel
   int kh, kw, sh, sw, pt, pl;
   int cout, cp_out;
@@ -80,28 +82,24 @@ __device__ __forceinline__ int floor_i(double v) {
 }
 
 // The coefficients of output sample xx of a filter over [in0, in1) to `out` samples:
-// returns the first source index, the count in *n, the fixed-point weights in k.
-__device__ __forceinline__ int coeffs(double in0, double in1, int out, int xx, int32_t (&k)[kMaxTaps], int* n) {
+// returns the first source index, the count in *n (at most kMaxTaps: the host checks the
+// scale), the fixed-point weights in k[0 .. n) (shared memory).
+__device__ __forceinline__ int coeffs(double in0, double in1, int out, int xx, int32_t* k, int* n) {
   const double scale = __ddiv_rn(__dsub_rn(in1, in0), static_cast<double>(out));
   const double fs = scale < 1.0 ? 1.0 : scale;
   const double support = __dmul_rn(1.0, fs), ss = __ddiv_rn(1.0, fs);
   const double center = __dadd_rn(in0, __dmul_rn(__dadd_rn(static_cast<double>(xx), 0.5), scale));
   const int xmin = floor_i(__dadd_rn(__dsub_rn(center, support), 0.5));
   int cnt = floor_i(__dadd_rn(__dadd_rn(center, support), 0.5)) - xmin;
-  if (cnt > kMaxTaps) cnt = kMaxTaps;  // never at the supported scales (checked by the host)
+  if (cnt > kMaxTaps) cnt = kMaxTaps;
   double ww = 0.0;
   for (int x = 0; x < cnt; ++x)
     ww = __dadd_rn(ww, tri(__dmul_rn(__dadd_rn(__dsub_rn(static_cast<double>(x + xmin), center), 0.5), ss)));
-#pragma unroll
-  for (int x = 0; x < kMaxTaps; ++x) {
-    if (x < cnt) {
-      double w = tri(__dmul_rn(__dadd_rn(__dsub_rn(static_cast<double>(x + xmin), center), 0.5), ss));
-      if (ww != 0.0) w = __ddiv_rn(w, ww);
-      const double f = static_cast<double>(1 << 22);
-      k[x] = static_cast<int32_t>(w < 0 ? __dadd_rn(-0.5, __dmul_rn(w, f)) : __dadd_rn(0.5, __dmul_rn(w, f)));
-    } else {
-      k[x] = 0;
-    }
+  const double f = static_cast<double>(1 << 22);
+  for (int x = 0; x < cnt; ++x) {
+    double w = tri(__dmul_rn(__dadd_rn(__dsub_rn(static_cast<double>(x + xmin), center), 0.5), ss));
+    if (ww != 0.0) w = __ddiv_rn(w, ww);
+    k[x] = static_cast<int32_t>(w < 0 ? __dadd_rn(-0.5, __dmul_rn(w, f)) : __dadd_rn(0.5, __dmul_rn(w, f)));
   }
   *n = cnt;
   return xmin;
@@ -112,8 +110,9 @@ __device__ __forceinline__ uint8_t clip8d(int32_t v) {
   return static_cast<uint8_t>(v < 0 ? 0 : v > 255 ? 255 : v);
 }
 
-// Shared memory: crop [height][bw] | strip intermediate (kStripBytes: source rows x strip columns) |
-// vertical coefficients | histogram and counters.
+// Shared memory: crop [height][bw] | strip intermediate (kStripBytes) | a strip's horizontal
+// coefficients (kCoefBytes: first and count a column, then taps) | vertical coefficients |
+// the stem's weights and per-channel constants | histogram and counters.
 template <bool kInt8>
 __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_constant__ CropParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
@@ -121,14 +120,30 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
   const LineDesc L = p.lines[line];
   const PageDesc P = p.pages[L.page];
   const int H = p.height, bw = L.bw, cw = L.width;
-  uint8_t* crop = sm;                                    // [H][bw]
-  uint8_t* tmp = crop + ((H * bw + 15) & ~15);           // [rows][strip columns], kStripBytes
-  int32_t* vk = reinterpret_cast<int32_t*>(tmp + kStripBytes);  // [H][kMaxTaps]
-  int32_t* vfirst = vk + H * kMaxTaps;                   // [H]
-  int32_t* vcount = vfirst + H;                          // [H]
-  int32_t* hist = vcount + H;                            // [256]
-  int32_t* red = hist + 256;                             // reductions
+  uint8_t* crop = sm;                                                   // [H][bw]
+  uint8_t* tmp = crop + ((H * p.max_bw + 15) & ~15);                    // [rows][strip]
+  int32_t* hk = reinterpret_cast<int32_t*>(tmp + kStripBytes);         // [strip][2 + T]
+  int32_t* vk = hk + kCoefBytes / 4;                                   // [H][kMaxTaps]
+  int32_t* vfirst = vk + H * kMaxTaps;                                 // [H]
+  int32_t* vcount = vfirst + H;                                        // [H]
+  int32_t* hist = vcount + H;                                          // [256]
+  int32_t* red = hist + 256;                                           // [8] reductions
+  float* sw_ = reinterpret_cast<float*>(red + 8);                      // stem weights [cout][taps]
+  float* sscale = sw_ + kStemMaxOut * 9;                               // [cout]
+  float* sbias = sscale + kStemMaxOut;                                 // [cout]
+  uint8_t* stab = reinterpret_cast<uint8_t*>(sbias + kStemMaxOut);     // [256] input table
   const int tid = threadIdx.x;
+  const int taps_stem = p.kh * p.kw;
+
+  for (int i = tid; i < p.cout * taps_stem; i += blockDim.x) sw_[i] = kInt8 ? static_cast<float>(p.w8[i]) : p.wf[i];
+  for (int i = tid; i < p.cout; i += blockDim.x) {
+    sscale[i] = kInt8 ? p.scale[i] : 1.0f;
+    sbias[i] = p.bias[i];
+  }
+  if (kInt8)
+    for (int i = tid; i < 256; i += blockDim.x) stab[i] = p.in_table[i];
+  for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+  if (tid < 8) red[tid] = 0;
 
   if (p.crops_in) {  // a ready crop (already finished and padded to its bucket width)
     const uint8_t* src = p.crops_in + static_cast<long long>(line) * H * p.crops_in_pitch;
@@ -137,14 +152,10 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
   } else {
     // vertical coefficients, one thread a row
     for (int yy = tid; yy < H; yy += blockDim.x) {
-      int32_t k[kMaxTaps];
       int n;
-      vfirst[yy] = coeffs(L.y0, L.y1, H, yy, k, &n);
+      vfirst[yy] = coeffs(L.y0, L.y1, H, yy, vk + yy * kMaxTaps, &n);
       vcount[yy] = n;
-      for (int i = 0; i < kMaxTaps; ++i) vk[yy * kMaxTaps + i] = k[i];
     }
-    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
-    if (tid < 8) red[tid] = 0;
     __syncthreads();
     const int top = vfirst[0];
     const int rows = vfirst[H - 1] + vcount[H - 1] - top;
@@ -152,34 +163,46 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
       if (tid == 0) atomicCAS(p.err, 0, kErrBadShape);
       return;
     }
-
-    // resample, a strip of columns at a time (as wide as the intermediate holds for these rows)
-    const int strip = max(16, min(kMaxStripCols, (kStripBytes / max(rows, 1)) & ~15));
+    // this line's tap stride: the filter's most taps (PIL's ksize)
+    const double hscale = (L.x1 - L.x0) / cw;
+    const int T = min(kMaxTaps, static_cast<int>(ceil(hscale < 1.0 ? 1.0 : hscale)) * 2 + 1);
+    const int strip = max(16, min(kMaxStripCols, min(kStripBytes / max(rows, 1), kCoefBytes / (4 * (T + 2)))));
     for (int x0 = 0; x0 < cw; x0 += strip) {
       const int sc = min(strip, cw - x0);
+      // the strip's horizontal coefficients, a thread a column
       for (int xx = tid; xx < sc; xx += blockDim.x) {
-        int32_t k[kMaxTaps];
+        int32_t* c = hk + xx * (T + 2);
         int n;
-        const int xmin = coeffs(L.x0, L.x1, cw, x0 + xx, k, &n);
-        for (int r = 0; r < rows; ++r) {
-          const int y = top + r;
-          const bool row_in = y >= 0 && y < P.height;
-          const uint8_t* src = P.data + static_cast<long long>(y) * P.stride;
-          int32_t ss = 1 << 21;
-  #pragma unroll
-          for (int i = 0; i < kMaxTaps; ++i) {
-            if (i < n) {
-              const int x = xmin + i;
-              const int v = (row_in && x >= 0 && x < P.width) ? src[x] : 255;
-              ss += v * k[i];
-            }
-          }
-          tmp[r * strip + xx] = clip8d(ss);
-        }
+        c[0] = coeffs(L.x0, L.x1, cw, x0 + xx, c + 2, &n);
+        c[1] = n;
       }
       __syncthreads();
+      // horizontal pass: a thread an (intermediate row, column)
+      for (int i = tid; i < rows * sc; i += blockDim.x) {
+        const int r = i / sc, xx = i - r * sc;
+        const int32_t* c = hk + xx * (T + 2);
+        const int xmin = c[0], n = c[1];
+        const int y = top + r;
+        int32_t ss = 1 << 21;
+        if (y >= 0 && y < P.height) {
+          const uint8_t* src = P.data + static_cast<long long>(y) * P.stride;
+          if (xmin >= 0 && xmin + n <= P.width) {
+            for (int t = 0; t < n; ++t) ss += static_cast<int32_t>(__ldg(src + xmin + t)) * c[2 + t];
+          } else {
+            for (int t = 0; t < n; ++t) {
+              const int x = xmin + t;
+              ss += ((x >= 0 && x < P.width) ? static_cast<int32_t>(__ldg(src + x)) : 255) * c[2 + t];
+            }
+          }
+        } else {
+          for (int t = 0; t < n; ++t) ss += 255 * c[2 + t];
+        }
+        tmp[r * strip + xx] = clip8d(ss);
+      }
+      __syncthreads();
+      // vertical pass: a thread an output pixel
       for (int i = tid; i < H * sc; i += blockDim.x) {
-        const int yy = i / sc, xx = i % sc;
+        const int yy = i / sc, xx = i - yy * sc;
         const int f = vfirst[yy] - top, n = vcount[yy];
         int32_t ss = 1 << 21;
         for (int t = 0; t < n; ++t) ss += tmp[(f + t) * strip + xx] * vk[yy * kMaxTaps + t];
@@ -187,8 +210,7 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
       }
       __syncthreads();
     }
-
-    // finish: the ground's histogram (first row, last row, last column)
+  // finish: the ground's histogram (first row, last row, last column)
     for (int x = tid; x < cw; x += blockDim.x) {
       atomicAdd(&hist[crop[x]], 1);
       atomicAdd(&hist[crop[(H - 1) * bw + x]], 1);
@@ -255,24 +277,24 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
 
   }
   // the stem on the quantized crop (its border the input's zero point: real zero), into the
-  // line's segment of the stem tensor; then the gap after it
+  // line's segment of the stem tensor; a thread an output pixel and all its channels
   const int oh = (H + 2 * p.pt - p.kh) / p.sh + 1, ow = (bw + 2 * p.pl - p.kw) / p.sw + 1;
-  const int taps = p.kh * p.kw;
   const long long col0 = static_cast<long long>(L.seg) >> p.out_shift;
   const int eb = kInt8 ? 1 : 2;
   for (int i = tid; i < oh * ow; i += blockDim.x) {
-    const int oy = i / ow, ox = i % ow;
+    const int oy = i / ow, ox = i - oy * ow;
     float in[9];
-    int32_t qin[9];
-    for (int t = 0; t < taps && t < 9; ++t) {
+    for (int t = 0; t < 9; ++t) {
+      in[t] = 0.0f;
+      if (t >= taps_stem) continue;
       const int y = oy * p.sh - p.pt + t / p.kw, x = ox * p.sw - p.pl + t % p.kw;
-      const bool inside = y >= 0 && y < H && x >= 0 && x < bw;
-      const uint8_t px = inside ? crop[y * bw + x] : 0;
+      if (y < 0 || y >= H || x < 0 || x >= bw) continue;  // the border: real zero
+      const uint8_t px = crop[y * bw + x];
       if constexpr (kInt8) {
-        qin[t] = (inside ? static_cast<int32_t>(p.in_table[px]) : p.in_zero) - p.in_zero;
+        in[t] = static_cast<float>(static_cast<int32_t>(stab[px]) - p.in_zero);  // exact small integers
       } else {
         // the FP16 engine's input: the ink 1 - p / 255 rounded to float16
-        in[t] = inside ? __half2float(__float2half_rn(__fsub_rn(1.0f, __fdiv_rn(static_cast<float>(px), 255.0f)))) : 0.0f;
+        in[t] = __half2float(__float2half_rn(__fsub_rn(1.0f, __fdiv_rn(static_cast<float>(px), 255.0f))));
       }
     }
     uint8_t* dst = p.out + (oy + p.out_ph) * p.out_pitch + (col0 + ox) * p.cp_out * eb;
@@ -280,16 +302,18 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
       if constexpr (kInt8) {
         alignas(16) uint8_t o[16];
         const float lo = static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
+#pragma unroll
         for (int u = 0; u < 16; ++u) {
           const int j = c0 + u;
           if (j >= p.cout) {
             o[u] = static_cast<uint8_t>(p.out_zero);
             continue;
           }
+          // an exact int32 sum (|terms| < 2^15, 9 of them), as the reference's int8 GEMM
           int32_t s = 0;
-          for (int t = 0; t < taps; ++t) s += qin[t] * p.w8[j * taps + t];
-          float v = __fmul_rn(static_cast<float>(s), p.scale[j]);
-          v = __fadd_rn(v, p.bias[j]);
+          for (int t = 0; t < taps_stem; ++t) s += static_cast<int32_t>(in[t]) * static_cast<int32_t>(sw_[j * taps_stem + t]);
+          float v = __fmul_rn(static_cast<float>(s), sscale[j]);
+          v = __fadd_rn(v, sbias[j]);
           if (p.relu) v = v > 0.0f ? v : 0.0f;
           float q = __fmul_rn(v, p.out_inv_scale);
           q = q > lo ? q : lo;
@@ -299,12 +323,13 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
         *reinterpret_cast<uint4*>(dst + c0) = *reinterpret_cast<const uint4*>(o);
       } else {
         alignas(16) __half o[16];
+#pragma unroll
         for (int u = 0; u < 16; ++u) {
           const int j = c0 + u;
           float v = 0.0f;
           if (j < p.cout) {
-            for (int t = 0; t < taps; ++t) v = __fmaf_rn(in[t], p.wf[j * taps + t], v);
-            v = __fadd_rn(v, p.bias[j]);
+            for (int t = 0; t < taps_stem; ++t) v = __fmaf_rn(in[t], sw_[j * taps_stem + t], v);
+            v = __fadd_rn(v, sbias[j]);
             if (p.relu) v = v > 0.0f ? v : 0.0f;
           }
           o[u] = __float2half_rn(v);

@@ -277,10 +277,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
         }
         t_phase[ti] ^= 1;
         tc_fence_after();
-        for (int cb = 0; cb < p.nchunk; cb += 16) {
-          uint32_t r[16];
-          tmem_ld16(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(ti * 256 + cb), r);
-          tmem_wait_ld();
+        // 16 classes of this chunk, from r[0..16), starting at chunk column cb
+        auto take16 = [&](const uint32_t* r, int cb) {
           const int j0 = c * p.nchunk + cb;
           if constexpr (kInt8) {
             alignas(16) uint8_t o[16];
@@ -318,6 +316,29 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
               }
             }
           }
+        };
+        // TMEM read 32 columns at a time, the next load in flight while the current is taken
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(ti * 256);
+        const int groups = p.nchunk / 16;
+        uint32_t ra[32], rb[32];
+        if (groups >= 2) tmem_ld32(taddr, ra); else tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(ra));
+        tmem_wait_ld();
+        tmem_pin(ra);
+        for (int g = 0; g < groups;) {
+          const int w = g + 1 < groups ? 2 : 1;
+          const int gn = g + w;
+          if (gn + 1 < groups) {
+            tmem_ld32(taddr + gn * 16, rb);
+          } else if (gn < groups) {
+            tmem_ld16(taddr + gn * 16, *reinterpret_cast<uint32_t(*)[16]>(rb));
+          }
+          take16(ra, g * 16);
+          if (w == 2) take16(ra + 16, g * 16 + 16);
+          tmem_wait_ld();
+          tmem_pin(rb);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ra[i] = rb[i];
+          g = gn;
         }
         tc_fence_before();
         __syncwarp();
@@ -387,4 +408,64 @@ __global__ void collapse_kernel(const __grid_constant__ CollapseParams p) {
   p.count[i] = k;
 }
 
+// ---------------------------------------------------------------- packing the decodings
+//
+// A call's runs each collapse into per-line slots; these pack every line's characters end to
+// end, in line order across the runs, so only the characters themselves cross to the host.
+// scan_counts_kernel: one CTA; the run's lines' exclusive prefix sum of counts, from the call's
+// running total (*total, then advanced by the run's characters).
+__global__ void __launch_bounds__(1024) scan_counts_kernel(const int32_t* count, int m, int32_t* counts_out,
+                                                           int32_t* offsets_out, long long* total) {
+  __shared__ int32_t warp_sums[32];
+  __shared__ long long carry;
+  if (threadIdx.x == 0) carry = *total;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int base = 0; base < m; base += 1024) {
+    const int i = base + static_cast<int>(threadIdx.x);
+    const int32_t v = i < m ? count[i] : 0;
+    int32_t x = v;  // inclusive scan within the warp
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int32_t w = warp_sums[lane];
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_sums[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int32_t before = (warp ? warp_sums[warp - 1] : 0) + x - v;
+    if (i < m) {
+      counts_out[i] = v;
+      offsets_out[i] = static_cast<int32_t>(carry + before);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) carry += warp_sums[31];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total = carry;
+}
+
+// A warp a line: its characters from its slots to the packed arrays at its offset.
+__global__ void pack_kernel(const int32_t* ids, const int32_t* frames, const float* probs, const int* line_frame0,
+                            const int32_t* counts, const int32_t* offsets, int m, int32_t* out_ids,
+                            int32_t* out_frames, float* out_probs) {
+  const int warp = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (warp >= m) return;
+  const int f0 = line_frame0[warp], k = counts[warp];
+  const long long o = offsets[warp];
+  for (int j = lane; j < k; j += 32) {
+    out_ids[o + j] = ids[f0 + j];
+    out_frames[o + j] = frames[f0 + j];
+    out_probs[o + j] = probs[f0 + j];
+  }
+}
+
 }  // namespace crec
+

@@ -186,6 +186,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Pins registers a tcgen05.ld wrote after the tcgen05.wait::ld that made them valid: the compiler
+// sees the load's outputs as ready at the load, so without this it could move their uses above
+// the wait.
+template <int N>
+__device__ __forceinline__ void tmem_pin(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i])::"memory");
+}
+
 __device__ __forceinline__ uint32_t elect_one_sync() {
   uint32_t pred = 0;
   asm volatile(
