@@ -21,8 +21,13 @@
 // ReLU, * inv_scale, clamped to [-zero, 255 - zero], rounded half to even, + zero.
 // FP16: A and B float16, FP32 sums; bias, residual and ReLU in FP32, stored as float16.
 //
-// Warp roles (6 warps): 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-5 epilogue (each
-// reading the TMEM lane quarter of its warp index mod 4).
+// Warp roles (10 warps): 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-9 epilogue: two warps
+// for each TMEM lane quarter (the quarter of its warp index mod 4), each taking half of a tile's
+// channel groups.  The epilogue is where an INT8 layer's time goes (requantizing 128 x N outputs
+// costs more CUDA-core cycles than the tensor cores' MMAs for K below ~700), hence 8 warps, the
+// per-channel constants in shared memory, and for layers with both zero points 0 and a ReLU
+// (most of the backbone) one saturating convert: cvt.rni.sat.u8 rounds half to even and clamps
+// to [0, 255], which is the reference's ReLU, clamp and round for a zero point of 0.
 #pragma once
 
 #include <cuda.h>
@@ -30,6 +35,7 @@
 
 #include <cstdint>
 
+#include "crop_stem.cuh"  // cvt_rni_sat_u8
 #include "sm100.cuh"
 
 namespace crec {
@@ -61,7 +67,8 @@ struct ConvParams {
   int* err;
 };
 
-constexpr int kConvThreads = 192;
+constexpr int kConvThreads = 320;
+constexpr int kConvEpiWarps = 8;
 constexpr uint32_t kTmemCols = 512;
 
 template <bool kInt8>
@@ -74,6 +81,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
   uint64_t* tmem_full = empty + p.stages;
   uint64_t* tmem_empty = tmem_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  int32_t* s_colsum = reinterpret_cast<int32_t*>(tmem_slot + 4);  // [cp_out] per-channel constants
+  float* s_scale = reinterpret_cast<float*>(s_colsum + p.cp_out);
+  float* s_bias = s_scale + p.cp_out;
+  for (int j = threadIdx.x; j < p.cp_out; j += blockDim.x) {
+    s_colsum[j] = p.colsum[j];
+    s_scale[j] = p.scale[j];
+    s_bias[j] = p.bias[j];
+  }
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
@@ -83,7 +98,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 4);
+      mbar_init(&tmem_empty[a], kConvEpiWarps);
     }
     fence_mbar_init();
   }
@@ -166,7 +181,11 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
   } else {
     // ---------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // the TMEM lanes this warp may read
+    const int half = (warp - 2) >> 2;  // which half of the tile's channel groups
     const int row = quarter * 32 + lane;
+    const bool fast = kInt8 && p.in_zero == 0 && p.out_zero == 0 && p.relu && !p.res && p.c_out == p.cp_out;
+    const int groups_all = p.nt / 16, g_lo = half ? (groups_all + 1) / 2 : 0,
+              g_hi = half ? groups_all : (groups_all + 1) / 2;
     int iter = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++iter) {
       const int acc = iter & 1;
@@ -191,6 +210,23 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
           if (!valid) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) o[i] = static_cast<uint8_t>(p.out_zero);
+          } else if (fast) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i4 = 0; i4 < 4; ++i4) {
+              const float4 sc = *reinterpret_cast<const float4*>(s_scale + cb + 4 * i4);
+              const float4 bi = *reinterpret_cast<const float4*>(s_bias + cb + 4 * i4);
+              const float scs[4] = {sc.x, sc.y, sc.z, sc.w}, bis[4] = {bi.x, bi.y, bi.z, bi.w};
+              uint32_t packed = 0;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float v = __fadd_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[4 * i4 + k])), scs[k]), bis[k]);
+                packed |= cvt_rni_sat_u8(__fmul_rn(v, p.out_inv_scale)) << (8 * k);
+              }
+              w[i4] = packed;
+            }
+            *reinterpret_cast<uint4*>(dst + cb) = make_uint4(w[0], w[1], w[2], w[3]);
+            return;
           } else {
             alignas(16) uint8_t rb[16];
             if (res) *reinterpret_cast<uint4*>(rb) = *reinterpret_cast<const uint4*>(res + cb);
@@ -198,9 +234,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int j = cb + i;
-              const int32_t sum = static_cast<int32_t>(r[i]) - p.in_zero * p.colsum[j];
-              float v = __fmul_rn(static_cast<float>(sum), p.scale[j]);
-              v = __fadd_rn(v, p.bias[j]);
+              const int32_t sum = static_cast<int32_t>(r[i]) - p.in_zero * s_colsum[j];
+              float v = __fmul_rn(static_cast<float>(sum), s_scale[j]);
+              v = __fadd_rn(v, s_bias[j]);
               if (res) v = __fadd_rn(v, __fmul_rn(static_cast<float>(static_cast<int32_t>(rb[i]) - p.res_zero), p.res_scale));
               if (p.relu) v = v > 0.0f ? v : 0.0f;
               float q = __fmul_rn(v, p.out_inv_scale);
@@ -225,7 +261,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int j = cb + i;
-              float v = __fadd_rn(__uint_as_float(r[i]), p.bias[j]);
+              float v = __fadd_rn(__uint_as_float(r[i]), s_bias[j]);
               if (res) v = __fadd_rn(v, __half2float(rh[i]));
               if (p.relu) v = v > 0.0f ? v : 0.0f;
               o[i] = __float2half_rn(j < p.c_out ? v : 0.0f);
@@ -237,26 +273,27 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       };
       // TMEM read 32 columns at a time, the next load in flight while the current is stored
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * 256);
-      const int groups = p.nt / 16;
-      uint32_t ra[32], rb[32];
-      if (groups >= 2) tmem_ld32(taddr, ra); else tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(ra));
-      tmem_wait_ld();
-      tmem_pin(ra);
-      for (int g = 0; g < groups;) {
-        const int w = g + 1 < groups ? 2 : 1;
-        const int gn = g + w;
-        if (gn + 1 < groups) {
-          tmem_ld32(taddr + gn * 16, rb);
-        } else if (gn < groups) {
-          tmem_ld16(taddr + gn * 16, *reinterpret_cast<uint32_t(*)[16]>(rb));
-        }
-        store16(ra, c0 + g * 16);
-        if (w == 2) store16(ra + 16, c0 + g * 16 + 16);
+      if (g_lo < g_hi) {
+        uint32_t ra[32], rb[32];
+        if (g_lo + 1 < g_hi) tmem_ld32(taddr + g_lo * 16, ra); else tmem_ld16(taddr + g_lo * 16, *reinterpret_cast<uint32_t(*)[16]>(ra));
         tmem_wait_ld();
-        tmem_pin(rb);
+        tmem_pin(ra);
+        for (int g = g_lo; g < g_hi;) {
+          const int w = g + 1 < g_hi ? 2 : 1;
+          const int gn = g + w;
+          if (gn + 1 < g_hi) {
+            tmem_ld32(taddr + gn * 16, rb);
+          } else if (gn < g_hi) {
+            tmem_ld16(taddr + gn * 16, *reinterpret_cast<uint32_t(*)[16]>(rb));
+          }
+          store16(ra, c0 + g * 16);
+          if (w == 2) store16(ra + 16, c0 + g * 16 + 16);
+          tmem_wait_ld();
+          tmem_pin(rb);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) ra[i] = rb[i];
-        g = gn;
+          for (int i = 0; i < 32; ++i) ra[i] = rb[i];
+          g = gn;
+        }
       }
       tc_fence_before();
       __syncwarp();

@@ -457,7 +457,7 @@ int setup_layer(crec_handle* h, size_t li) {
     l.a_bytes = static_cast<uint32_t>(l.nkb) * 16384;
     l.b_bytes = static_cast<uint32_t>(l.nkb) * l.nchunk * 128;
     const uint32_t codes = h->int8 ? 128u * round16(l.cout) : 0u;
-    l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + 128;
+    l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + 128 + 12u * l.chunks * l.nchunk + 3u * 512 + 64;
     if (l.smem > 232448) return set_error(h, CREC_E_MODEL, "the head does not fit in shared memory");
   } else {
     l.nt = std::min(256, round16(l.cout));
@@ -466,7 +466,7 @@ int setup_layer(crec_handle* h, size_t li) {
     l.b_bytes = static_cast<uint32_t>(l.nt) * 128;
     l.stage_bytes = l.a_bytes + l.b_bytes;
     l.stages = std::min<int>(8, (200 * 1024) / l.stage_bytes);
-    l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 4) * 8 + 16;
+    l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 4) * 8 + 16 + 12 * y.cp + 64;
   }
   const std::vector<uint8_t> img = weight_image(h, l, x.cp, l.nt, l.n_tiles, l.nkb);
   if ((rc = upload(h, &l.wimg, img))) return rc;
@@ -505,7 +505,7 @@ int encode_map(crec_handle* h, CUtensorMap* m, const void* base, uint64_t d0, ui
 size_t crop_smem_bytes(const crec_handle* h, int max_bw) {
   return ((static_cast<size_t>(h->height) * max_bw + 15) & ~size_t(15)) + kStripBytes + kCoefBytes +
          (static_cast<size_t>(h->height) * kMaxTaps + 2 * h->height + 256 + 8) * 4 +
-         (kStemMaxOut * 9 + 2 * kStemMaxOut) * 4 + 256;
+         (kStemMaxOut * 9 + 2 * kStemMaxOut + 4 * kStemMaxOut) * 4 + 256;
 }
 
 // Kernel kinds of the profile: 0 crop+stem, 1 dense convolutions (tcgen05), 2 depthwise, 3 head+CTC, 4 collapse.
@@ -599,6 +599,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.wf = stem.dwf;
     p.scale = stem.scale;
     p.bias = stem.dbias;
+    p.colsum = stem.colsum;
     p.in_table = h->in_table;
     p.in_zero = x0.zero;
     p.out_zero = s0.zero;

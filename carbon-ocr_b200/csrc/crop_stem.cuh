@@ -62,6 +62,7 @@ struct CropParams {
   const float* wf;      // [cout][kh*kw] (FP16 engine: the weights' float16 values widened)
   const float* scale;   // [cout]
   const float* bias;    // [cout]
+  const int32_t* colsum;  // [cout] sum of each output channel's int8 weights
   const uint8_t* in_table;  // [256] the INT8 input table
   int in_zero, out_zero, relu;
   float out_inv_scale;
@@ -105,6 +106,20 @@ __device__ __forceinline__ int coeffs(double in0, double in1, int out, int xx, i
   return xmin;
 }
 
+// Round half to even and saturate to [0, 255] (the output stage for a zero point of 0 after a ReLU).
+__device__ __forceinline__ uint32_t cvt_rni_sat_u8(float q) {
+  uint32_t r;
+  asm("cvt.rni.sat.u8.f32 %0, %1;" : "=r"(r) : "f"(q));
+  return r;
+}
+
+// Four unsigned bytes of a times four signed bytes of b, summed into c.
+__device__ __forceinline__ int32_t dp4a_us(uint32_t a, uint32_t b, int32_t c) {
+  int32_t d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint8_t clip8d(int32_t v) {
   v >>= 22;
   return static_cast<uint8_t>(v < 0 ? 0 : v > 255 ? 255 : v);
@@ -128,17 +143,31 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
   int32_t* vcount = vfirst + H;                                        // [H]
   int32_t* hist = vcount + H;                                          // [256]
   int32_t* red = hist + 256;                                           // [8] reductions
-  float* sw_ = reinterpret_cast<float*>(red + 8);                      // stem weights [cout][taps]
+  float* sw_ = reinterpret_cast<float*>(red + 8);                      // stem weights [cout][taps] (FP16 engine)
   float* sscale = sw_ + kStemMaxOut * 9;                               // [cout]
   float* sbias = sscale + kStemMaxOut;                                 // [cout]
-  uint8_t* stab = reinterpret_cast<uint8_t*>(sbias + kStemMaxOut);     // [256] input table
+  uint32_t* sw4 = reinterpret_cast<uint32_t*>(sbias + kStemMaxOut);    // INT8: [cout][3] taps packed 4 a word
+  int32_t* scol = reinterpret_cast<int32_t*>(sw4 + kStemMaxOut * 3);   // [cout] weight sums
+  uint8_t* stab = reinterpret_cast<uint8_t*>(scol + kStemMaxOut);      // [256] input table
   const int tid = threadIdx.x;
   const int taps_stem = p.kh * p.kw;
 
-  for (int i = tid; i < p.cout * taps_stem; i += blockDim.x) sw_[i] = kInt8 ? static_cast<float>(p.w8[i]) : p.wf[i];
+  if (!kInt8)
+    for (int i = tid; i < p.cout * taps_stem; i += blockDim.x) sw_[i] = p.wf[i];
+  if (kInt8)
+    for (int i = tid; i < p.cout * 3; i += blockDim.x) {  // taps 4k .. 4k+3 of channel i / 3, zeros past the last
+      const int j = i / 3, k = i % 3;
+      uint32_t w = 0;
+      for (int b = 0; b < 4; ++b) {
+        const int t = 4 * k + b;
+        if (t < taps_stem) w |= static_cast<uint32_t>(static_cast<uint8_t>(p.w8[j * taps_stem + t])) << (8 * b);
+      }
+      sw4[i] = w;
+    }
   for (int i = tid; i < p.cout; i += blockDim.x) {
     sscale[i] = kInt8 ? p.scale[i] : 1.0f;
     sbias[i] = p.bias[i];
+    scol[i] = kInt8 ? p.colsum[i] : 0;
   }
   if (kInt8)
     for (int i = tid; i < 256; i += blockDim.x) stab[i] = p.in_table[i];
@@ -281,47 +310,62 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
   const int oh = (H + 2 * p.pt - p.kh) / p.sh + 1, ow = (bw + 2 * p.pl - p.kw) / p.sw + 1;
   const long long col0 = static_cast<long long>(L.seg) >> p.out_shift;
   const int eb = kInt8 ? 1 : 2;
+  const bool fast = p.in_zero == 0 && p.out_zero == 0 && p.relu && p.cout == p.cp_out;
   for (int i = tid; i < oh * ow; i += blockDim.x) {
     const int oy = i / ow, ox = i - oy * ow;
-    float in[9];
-    for (int t = 0; t < 9; ++t) {
-      in[t] = 0.0f;
-      if (t >= taps_stem) continue;
-      const int y = oy * p.sh - p.pt + t / p.kw, x = ox * p.sw - p.pl + t % p.kw;
-      if (y < 0 || y >= H || x < 0 || x >= bw) continue;  // the border: real zero
-      const uint8_t px = crop[y * bw + x];
-      if constexpr (kInt8) {
-        in[t] = static_cast<float>(static_cast<int32_t>(stab[px]) - p.in_zero);  // exact small integers
-      } else {
-        // the FP16 engine's input: the ink 1 - p / 255 rounded to float16
-        in[t] = __half2float(__float2half_rn(__fsub_rn(1.0f, __fdiv_rn(static_cast<float>(px), 255.0f))));
-      }
-    }
     uint8_t* dst = p.out + (oy + p.out_ph) * p.out_pitch + (col0 + ox) * p.cp_out * eb;
-    for (int c0 = 0; c0 < p.cp_out; c0 += 16) {
-      if constexpr (kInt8) {
-        alignas(16) uint8_t o[16];
-        const float lo = static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
+    if constexpr (kInt8) {
+      // the taps' quantized inputs packed 4 a word (the border reads the zero point: real zero);
+      // sum over taps of (a - zero) * w = dp4a(a, w) - zero * sum(w), exact in int32
+      uint32_t a4[3] = {0, 0, 0};
+      for (int t = 0; t < taps_stem; ++t) {
+        const int y = oy * p.sh - p.pt + t / p.kw, x = ox * p.sw - p.pl + t % p.kw;
+        const uint32_t q = (y >= 0 && y < H && x >= 0 && x < bw) ? stab[crop[y * bw + x]] : static_cast<uint32_t>(p.in_zero);
+        a4[t >> 2] |= q << (8 * (t & 3));
+      }
+      uint32_t words[kStemMaxOut / 4];
+      const float lo = static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
+      for (int c0 = 0; c0 < p.cp_out; c0 += 4) {
+        uint32_t wv = 0;
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
+        for (int u = 0; u < 4; ++u) {
           const int j = c0 + u;
-          if (j >= p.cout) {
-            o[u] = static_cast<uint8_t>(p.out_zero);
-            continue;
+          uint32_t code = static_cast<uint32_t>(p.out_zero);
+          if (j < p.cout) {
+            const uint32_t* w = sw4 + j * 3;
+            int32_t sum = dp4a_us(a4[0], w[0], 0);
+            sum = dp4a_us(a4[1], w[1], sum);
+            sum = dp4a_us(a4[2], w[2], sum);
+            sum -= p.in_zero * scol[j];
+            float v = __fadd_rn(__fmul_rn(static_cast<float>(sum), sscale[j]), sbias[j]);
+            if (fast) {
+              code = cvt_rni_sat_u8(__fmul_rn(v, p.out_inv_scale));
+            } else {
+              if (p.relu) v = v > 0.0f ? v : 0.0f;
+              float q = __fmul_rn(v, p.out_inv_scale);
+              q = q > lo ? q : lo;
+              q = q < hi ? q : hi;
+              code = static_cast<uint32_t>(__float2int_rn(q) + p.out_zero);
+            }
           }
-          // an exact int32 sum (|terms| < 2^15, 9 of them), as the reference's int8 GEMM
-          int32_t s = 0;
-          for (int t = 0; t < taps_stem; ++t) s += static_cast<int32_t>(in[t]) * static_cast<int32_t>(sw_[j * taps_stem + t]);
-          float v = __fmul_rn(static_cast<float>(s), sscale[j]);
-          v = __fadd_rn(v, sbias[j]);
-          if (p.relu) v = v > 0.0f ? v : 0.0f;
-          float q = __fmul_rn(v, p.out_inv_scale);
-          q = q > lo ? q : lo;
-          q = q < hi ? q : hi;
-          o[u] = static_cast<uint8_t>(__float2int_rn(q) + p.out_zero);
+          wv |= (code & 0xffu) << (8 * u);
         }
-        *reinterpret_cast<uint4*>(dst + c0) = *reinterpret_cast<const uint4*>(o);
-      } else {
+        words[c0 >> 2] = wv;
+      }
+      for (int c0 = 0; c0 < p.cp_out; c0 += 16)
+        *reinterpret_cast<uint4*>(dst + c0) =
+            make_uint4(words[c0 >> 2], words[(c0 >> 2) + 1], words[(c0 >> 2) + 2], words[(c0 >> 2) + 3]);
+    } else {
+      float in[9];
+      for (int t = 0; t < 9; ++t) {
+        in[t] = 0.0f;
+        if (t >= taps_stem) continue;
+        const int y = oy * p.sh - p.pt + t / p.kw, x = ox * p.sw - p.pl + t % p.kw;
+        if (y < 0 || y >= H || x < 0 || x >= bw) continue;  // the border: real zero
+        // the FP16 engine's input: the ink 1 - p / 255 rounded to float16
+        in[t] = __half2float(__float2half_rn(__fsub_rn(1.0f, __fdiv_rn(static_cast<float>(crop[y * bw + x]), 255.0f))));
+      }
+      for (int c0 = 0; c0 < p.cp_out; c0 += 16) {
         alignas(16) __half o[16];
 #pragma unroll
         for (int u = 0; u < 16; ++u) {

@@ -175,7 +175,22 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
   uint64_t* t_full = bars + 6;      // [2]
   uint64_t* t_empty = bars + 8;     // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  const int ncls = p.chunks * p.nchunk;
+  int32_t* s_colsum = reinterpret_cast<int32_t*>(bars + 16);  // [ncls] per-class constants
+  float* s_scale = reinterpret_cast<float*>(s_colsum + ncls);
+  float* s_bias = s_scale + ncls;
+  int32_t* nb_row = reinterpret_cast<int32_t*>(s_bias + ncls);  // the tile's non-blank frames: row
+  int32_t* nb_q = nb_row + 128;                                 // and best code
+  int32_t* s_best = nb_q + 128;                                 // each row's best class
+  int32_t* nb_count = s_best + 128;                             // [2]: by tile parity
+  int32_t* s_abort = nb_count + 2;
   __shared__ float tab[256];
+  for (int j = threadIdx.x; j < ncls; j += blockDim.x) {
+    s_colsum[j] = p.colsum[j];
+    s_scale[j] = p.scale[j];
+    s_bias[j] = p.bias[j];
+  }
+  if (threadIdx.x < 3) nb_count[threadIdx.x] = 0;  // both counters and the abort flag
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) tab[i] = p.table ? p.table[i] : 0.0f;
@@ -265,12 +280,13 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
     uint8_t* my = codes + row * ((p.classes + 15) & ~15);
     const float lo = static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
     bool ok = true;
-    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+    int tile_parity = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, tile_parity ^= 1) {
       const int ox = t * 128 + row;
       int best = 0;
       int bestq = -1;
       float bestv = -INFINITY, sum = 0.0f;
-      for (int c = 0; c < p.chunks; ++c) {
+      for (int c = 0; c < p.chunks && ok; ++c) {
         if (!mbar_wait(&t_full[ti], t_phase[ti], p.err, kErrTimeoutTmemFull)) {
           ok = false;
           break;
@@ -285,9 +301,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int j = j0 + i;
-              const int32_t s = static_cast<int32_t>(r[i]) - p.in_zero * p.colsum[j];
-              float v = __fmul_rn(static_cast<float>(s), p.scale[j]);
-              v = __fadd_rn(v, p.bias[j]);
+              const int32_t s = static_cast<int32_t>(r[i]) - p.in_zero * s_colsum[j];
+              float v = __fmul_rn(static_cast<float>(s), s_scale[j]);
+              v = __fadd_rn(v, s_bias[j]);
               float q = __fmul_rn(v, p.out_inv_scale);
               q = q > lo ? q : lo;
               q = q < hi ? q : hi;
@@ -305,7 +321,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
             for (int i = 0; i < 16; ++i) {
               const int j = j0 + i;
               if (j >= p.classes) continue;
-              const float v = __fadd_rn(__uint_as_float(r[i]), p.bias[j]);
+              const float v = __fadd_rn(__uint_as_float(r[i]), s_bias[j]);
               if (p.logits && ox < p.ow) p.logits[static_cast<long long>(ox) * p.classes + j] = v;
               if (v > bestv) {
                 sum = bestv == -INFINITY ? 1.0f : __fadd_rn(__fmul_rn(sum, exp_neg_d(__fsub_rn(bestv, v))), 1.0f);
@@ -345,22 +361,54 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
         if (lane == 0) mbar_arrive(&t_empty[ti]);
         ti ^= 1;
       }
-      if (!ok) break;
-      const bool valid = ox < p.ow && p.mask8[(static_cast<long long>(ox) << p.out_shift) >> 3] != 0;
-      if (!valid) continue;
-      float prob = 0.0f;
-      if (best != 0) {
-        if constexpr (kInt8) {
-          const float top = tab[bestq];
-          float s = 0.0f;
-          for (int j = 0; j < p.classes; ++j) s = __fadd_rn(s, exp_neg_d(__fsub_rn(tab[my[j]], top)));
-          prob = __fdiv_rn(1.0f, s);
-        } else {
-          prob = __fdiv_rn(1.0f, sum);
+      const bool valid = ok && ox < p.ow && p.mask8[(static_cast<long long>(ox) << p.out_shift) >> 3] != 0;
+      if constexpr (kInt8) {
+        // the class-order sums only for the tile's non-blank frames, gathered into a list so every
+        // lane of the warps that run them has one (most frames are blank)
+        if (!ok) atomicOr(s_abort, 1);
+        s_best[row] = best;
+        if (valid && best != 0) {
+          const int k = atomicAdd(&nb_count[tile_parity], 1);
+          nb_row[k] = row;
+          nb_q[k] = bestq;
+        } else if (valid) {
+          p.frame_id[ox] = 0;
+          p.frame_prob[ox] = 0.0f;
         }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int e = threadIdx.x - 64;  // 0..127: this thread's place among the epilogue's
+        if (e == 0) nb_count[tile_parity ^ 1] = 0;  // the next tile's counter (its adds follow the next barrier)
+        const int listed = nb_count[tile_parity];
+        const int stride = (p.classes + 15) & ~15;
+        if (!*s_abort) {
+          for (int k = e; k < listed; k += 128) {
+            const int r = nb_row[k];
+            const uint8_t* rowc = codes + r * stride;
+            const float top = tab[nb_q[k]];
+            float sum = 0.0f;
+            for (int j0 = 0; j0 < p.classes; j0 += 16) {
+              alignas(16) uint8_t q16[16];
+              *reinterpret_cast<uint4*>(q16) = *reinterpret_cast<const uint4*>(rowc + j0);
+              float term[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) term[i] = exp_neg_d(__fsub_rn(tab[q16[i]], top));
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (j0 + i < p.classes) sum = __fadd_rn(sum, term[i]);
+            }
+            const int fx = t * 128 + r;
+            p.frame_id[fx] = s_best[r];
+            p.frame_prob[fx] = __fdiv_rn(1.0f, sum);
+          }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (*s_abort) break;
+      } else {
+        if (!ok) break;
+        if (!valid) continue;
+        p.frame_id[ox] = best;
+        p.frame_prob[ox] = best != 0 ? __fdiv_rn(1.0f, sum) : 0.0f;
       }
-      p.frame_id[ox] = best;
-      p.frame_prob[ox] = prob;
     }
   }
   tc_fence_before();
