@@ -63,6 +63,8 @@ struct Layer {
   float* dbias = nullptr;
   int8_t* dw8 = nullptr;  // depthwise [taps][cp], stem [cout][taps]
   float* dwf = nullptr;
+  int32_t* hoff = nullptr;  // the INT8 head's per-class offsets (HeadParams::off)
+  bool fast = false;        // its sums fit the exact conversions without the conversion unit
   int nkb = 0, last_steps = 0, nt = 0, n_tiles = 0, stages = 0, nchunk = 0, chunks = 0;
   uint32_t stage_bytes = 0, a_bytes = 0, b_bytes = 0, smem = 0;
 };
@@ -124,6 +126,7 @@ struct crec_handle {
   long long max_cols = 0;  // input columns a run holds
   uint8_t* in_table = nullptr;
   float* head_table = nullptr;
+  float* ctc_terms = nullptr;  // INT8: [256][256] exp_neg(table[q] - table[best])
   // pages
   std::vector<PageDesc> pages;  // device pointers
   uint8_t* page_mem = nullptr;
@@ -450,15 +453,35 @@ int setup_layer(crec_handle* h, size_t li) {
   l.last_steps = (window - (l.nkb - 1) * 128 + 31) / 32;
   if (li + 1 == h->l.size()) {  // the head
     if (l.nkb * 16384 > 65536) return set_error(h, CREC_E_MODEL, "a head reading more than 512 bytes a frame");
-    l.nchunk = std::min(h->int8 ? 160 : 80, round16(l.cout));
+    l.nchunk = std::min(kHeadChunk, round16(l.cout));
     l.chunks = (l.cout + l.nchunk - 1) / l.nchunk;
     l.nt = l.nchunk;
     l.n_tiles = l.chunks;
     l.a_bytes = static_cast<uint32_t>(l.nkb) * 16384;
     l.b_bytes = static_cast<uint32_t>(l.nkb) * l.nchunk * 128;
-    const uint32_t codes = h->int8 ? 128u * round16(l.cout) : 0u;
-    l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + 128 + 12u * l.chunks * l.nchunk + 3u * 512 + 64;
-    if (l.smem > 232448) return set_error(h, CREC_E_MODEL, "the head does not fit in shared memory");
+    const uint32_t codes = h->int8 ? 128u * head_code_stride(l.cout) : 0u;
+    const int ncls = l.chunks * l.nchunk;
+    l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + head_tail_bytes(ncls);
+    if (l.smem + 1024 > 232448) return set_error(h, CREC_E_MODEL, "the head does not fit in shared memory");
+    if (h->int8) {
+      // |acc - zero * colsum| <= max(zero, 255 - zero) * sum |w| over a class's weights: below 2^22
+      // the kernel converts with kMagic (exact), otherwise with the conversion unit
+      const int z = x.zero;
+      const long long reach = std::max(z, 255 - z);
+      long long worst = 0;
+      for (int j = 0; j < l.cout; ++j) {
+        long long a = 0;
+        for (int k = 0; k < l.cin; ++k) a += std::abs(static_cast<int>(l.w8[static_cast<size_t>(j) * l.cin + k]));
+        worst = std::max(worst, a * reach);
+      }
+      l.fast = worst < (1LL << 22);
+      std::vector<int32_t> off(ncls, 0);
+      for (int j = 0; j < ncls; ++j) {
+        const int32_t zc = z * colsum[j];
+        off[j] = l.fast ? kMagicBits - zc : zc;
+      }
+      if ((rc = upload(h, &l.hoff, off))) return rc;
+    }
   } else {
     l.nt = std::min(256, round16(l.cout));
     l.n_tiles = (y.cp + l.nt - 1) / l.nt;
@@ -649,13 +672,13 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.num_tiles = static_cast<int>((ow + 127) / 128);
       p.a_bytes = l.a_bytes;
       p.b_bytes = l.b_bytes;
-      p.colsum = l.colsum;
+      p.off = l.hoff;
       p.scale = l.scale;
       p.bias = l.dbias;
-      p.in_zero = x.zero;
       p.out_zero = y.zero;
       p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
       p.table = h->head_table;
+      p.terms = h->ctc_terms;
       p.mask8 = h->d_mask;
       p.out_shift = y.shift;
       p.frame_id = h->d_frame_id;
@@ -664,12 +687,15 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.err = h->d_err;
       const int grid = std::min(p.num_tiles, h->sms);
       ProfScope prof(h, kProfHead);
-      if (h->int8) {
-        CK(cudaFuncSetAttribute(head_ctc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-        head_ctc_kernel<true><<<grid, kHeadThreads, l.smem, s>>>(p);
+      if (h->int8 && l.fast) {
+        CK(cudaFuncSetAttribute(head_ctc_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+        head_ctc_kernel<true, true><<<grid, kHeadThreads, l.smem, s>>>(p);
+      } else if (h->int8) {
+        CK(cudaFuncSetAttribute(head_ctc_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+        head_ctc_kernel<true, false><<<grid, kHeadThreads, l.smem, s>>>(p);
       } else {
-        CK(cudaFuncSetAttribute(head_ctc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-        head_ctc_kernel<false><<<grid, kHeadThreads, l.smem, s>>>(p);
+        CK(cudaFuncSetAttribute(head_ctc_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+        head_ctc_kernel<false, false><<<grid, kHeadThreads, l.smem, s>>>(p);
       }
       CK(cudaGetLastError());
       continue;
@@ -995,9 +1021,11 @@ void free_all(crec_handle* h) {
     cudaFree(l.dbias);
     cudaFree(l.dw8);
     cudaFree(l.dwf);
+    cudaFree(l.hoff);
   }
   cudaFree(h->in_table);
   cudaFree(h->head_table);
+  cudaFree(h->ctc_terms);
   if (h->pages_owned) cudaFree(h->page_mem);
   cudaFree(h->d_pages);
   cudaFree(h->d_lines);
@@ -1074,6 +1102,10 @@ int open_impl(crec_handle* h, const crec_config* c) {
     const Value& y = h->v[h->outv];
     for (int q = 0; q < 256; ++q) tab[q] = static_cast<float>(q - y.zero) * y.scale;
     if ((rc = upload(h, &h->head_table, tab))) return rc;
+    CK(cudaMalloc(&h->ctc_terms, 256 * 256 * sizeof(float)));
+    ctc_terms_kernel<<<256, 256, 0, h->stream>>>(h->head_table, h->ctc_terms);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(h->stream));
   }
   const int ml = c->max_lines;
   const size_t frames = static_cast<size_t>(h->max_cols >> h->head_shift);

@@ -110,15 +110,21 @@ __global__ void __launch_bounds__(256) dw_kernel(const __grid_constant__ DwParam
 // ---------------------------------------------------------------- the head fused with CTC's argmax
 //
 // A tile is 128 frames (columns of the head's input, one row); the 1x1 head runs over the
-// classes a chunk at a time (tcgen05.mma, the accumulators double-buffered in TMEM), A loaded
-// once a tile, the chunks' weights streamed.  Per frame: the best class, ties to the lower id
-// (strictly greater, classes in order), and for a non-blank best its softmax probability.
+// classes a chunk of up to 128 at a time (tcgen05.mma; A loaded once a tile, the chunks'
+// weights streamed by bulk copies), each chunk's accumulator in one of four TMEM buffers.
+// Eight epilogue warps, two for each TMEM lane quarter: the even chunks go to the first four,
+// the odd chunks to the other four, each half of the classes with two buffers of its own.
+// Per frame: the best class, ties to the lower id, and for a non-blank best its softmax
+// probability.
 // INT8: each class's logit requantized to uint8 exactly as the reference stores the head's
-// output (the dense epilogue), the codes kept in shared memory, then the probability as
+// output (the dense epilogue), the codes kept in shared memory; the probability as
 // carbon/src/cpu/kernels.cpp:799-828 computes it: 1 / (the sum in class order of
 // exp_neg(table[q_c] - table[q_best])), table[q] = (q - zero) * scale
-// (carbon/src/net/net.cpp:1101-1128) -- the same float operations in the same order.
-// FP16: the FP32 logits (sum + bias) and an online maximum and sum of exp_neg terms.
+// (carbon/src/net/net.cpp:1101-1128).  A term depends only on (q_c, q_best), so the 65,536
+// possible terms are computed once per model (ctc_terms_kernel, the same float operations) and
+// the sums only add them, in class order.
+// FP16: the FP32 logits (sum + bias); each half keeps an online maximum and sum of 2^x terms,
+// merged per frame.
 // Only each frame's id and probability leave the kernel; the logits are never written.
 struct HeadParams {
   CUtensorMap tmap;     // the head's input: (K byte, frame column, row)
@@ -126,12 +132,13 @@ struct HeadParams {
   int nkb, last_steps, classes, nchunk, chunks;  // last_steps: 32-byte K steps in the last K block
   int ow, num_tiles;
   uint32_t a_bytes, b_bytes;  // A: nkb x 16 KB; B: one chunk (nkb blocks)
-  const int32_t* colsum;
-  const float* scale;
+  const int32_t* off;   // INT8 [chunks * nchunk]: kMagicBits - in_zero * colsum (fast), else in_zero * colsum
+  const float* scale;   // INT8: in_scale * weight scale
   const float* bias;
-  int in_zero, out_zero;
+  int out_zero;
   float out_inv_scale;
-  const float* table;  // [256] the u8 logits' values
+  const float* table;  // INT8 [256]: the u8 logits' values
+  const float* terms;  // INT8 [256 best][256 q]: exp_neg(table[q] - table[best])
   const uint8_t* mask8;
   int out_shift;
   int32_t* frame_id;   // [ow]
@@ -140,8 +147,19 @@ struct HeadParams {
   int* err;
 };
 
-constexpr int kHeadThreads = 192;
+constexpr int kHeadThreads = 320;  // warp 0 TMA, warp 1 MMA and TMEM, warps 2..9 the epilogue
+constexpr int kHeadChunk = 128;    // classes a chunk (the MMA's N): four buffers in 512 TMEM columns
 constexpr uint32_t kTmemColsHead = 512;
+
+// The INT8 codes' row stride: 16-byte groups, an odd number of them, so that the 32 rows of a
+// warp storing the same 16 classes spread over the shared-memory banks.
+__host__ __device__ constexpr int head_code_stride(int classes) {
+  return ((classes + 15) / 16 | 1) * 16;
+}
+
+// Bytes of the head's shared memory after A, B and the codes: barriers, per-class constants,
+// the per-frame merge slots and the list of non-blank frames.
+__host__ __device__ constexpr int head_tail_bytes(int ncls) { return 128 + 12 * ncls + (3 * 256 + 3 * 128 + 2) * 4; }
 
 // carbon/src/cpu/kernels.h:216-250 (exp_neg), each multiply and add rounded on its own.
 __device__ __forceinline__ float exp_neg_d(float x) {
@@ -160,46 +178,65 @@ __device__ __forceinline__ float exp_neg_d(float x) {
   return __fmul_rn(y, s);
 }
 
-template <bool kInt8>
+// terms[b][q] = exp_neg(table[q] - table[b]): a CTC sum's term for class code q when the best
+// code is b.  256 blocks of 256 threads.
+__global__ void ctc_terms_kernel(const float* table, float* terms) {
+  const int b = blockIdx.x, q = threadIdx.x;
+  terms[b * 256 + q] = exp_neg_d(__fsub_rn(table[q], table[b]));
+}
+
+// The lowest byte of w equal to the byte in every byte of m4, as a bit mask whose lowest set bit
+// is that byte's top bit (bytes above it may be flagged too), or 0 if there is none.
+__device__ __forceinline__ uint32_t first_byte_eq(uint32_t w, uint32_t m4) {
+  const uint32_t v = w ^ m4;
+  return (v - 0x01010101u) & ~v & 0x80808080u;
+}
+
+template <bool kInt8, bool kFast>
 __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_constant__ HeadParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sa = smem;                         // A: nkb blocks of [128][128]
-  uint8_t* sb = sa + p.a_bytes;               // B: 2 chunk buffers
-  uint8_t* codes = sb + 2 * p.b_bytes;        // INT8: [128][classes]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(codes + (kInt8 ? 128 * ((p.classes + 15) & ~15) : 0));
+  const int cstride = head_code_stride(p.classes);
+  uint8_t* sa = smem;                // A: nkb blocks of [128][128]
+  uint8_t* sb = sa + p.a_bytes;      // B: 2 chunk buffers
+  uint8_t* codes = sb + 2 * p.b_bytes;  // INT8: [128][cstride]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(codes + (kInt8 ? 128 * cstride : 0));
   uint64_t* a_full = bars;
   uint64_t* a_empty = bars + 1;
-  uint64_t* b_full = bars + 2;      // [2]
-  uint64_t* b_empty = bars + 4;     // [2]
-  uint64_t* t_full = bars + 6;      // [2]
-  uint64_t* t_empty = bars + 8;     // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* b_full = bars + 2;    // [2]
+  uint64_t* b_empty = bars + 4;   // [2]
+  uint64_t* t_full = bars + 6;    // [4] TMEM buffers: 0, 1 the even chunks', 2, 3 the odd chunks'
+  uint64_t* t_empty = bars + 10;  // [4]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   const int ncls = p.chunks * p.nchunk;
-  int32_t* s_colsum = reinterpret_cast<int32_t*>(bars + 16);  // [ncls] per-class constants
-  float* s_scale = reinterpret_cast<float*>(s_colsum + ncls);
+  int32_t* s_off = reinterpret_cast<int32_t*>(bars + 16);  // [ncls] per-class constants
+  float* s_scale = reinterpret_cast<float*>(s_off + ncls);
   float* s_bias = s_scale + ncls;
-  int32_t* nb_row = reinterpret_cast<int32_t*>(s_bias + ncls);  // the tile's non-blank frames: row
-  int32_t* nb_q = nb_row + 128;                                 // and best code
+  int32_t* s_hmax = reinterpret_cast<int32_t*>(s_bias + ncls);  // [2][128] each half's highest code (FP16: logit)
+  int32_t* s_hbest = s_hmax + 256;                              // FP16 [2][128] each half's best class
+  float* s_hsum = reinterpret_cast<float*>(s_hbest + 256);     // FP16 [2][128] each half's sum
+  int32_t* nb_row = reinterpret_cast<int32_t*>(s_hsum + 256);  // INT8: the tile's non-blank frames' rows
+  int32_t* nb_q = nb_row + 128;                                 // and best codes
   int32_t* s_best = nb_q + 128;                                 // each row's best class
-  int32_t* nb_count = s_best + 128;                             // [2]: by tile parity
-  int32_t* s_abort = nb_count + 2;
+  volatile int32_t* s_count = s_best + 128;                     // [0] frames listed, [1] abort
   __shared__ float tab[256];
-  for (int j = threadIdx.x; j < ncls; j += blockDim.x) {
-    s_colsum[j] = p.colsum[j];
-    s_scale[j] = p.scale[j];
-    s_bias[j] = p.bias[j];
-  }
-  if (threadIdx.x < 3) nb_count[threadIdx.x] = 0;  // both counters and the abort flag
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) tab[i] = p.table ? p.table[i] : 0.0f;
+  for (int j = threadIdx.x; j < ncls; j += blockDim.x) {
+    s_off[j] = kInt8 ? p.off[j] : 0;
+    s_scale[j] = kInt8 ? p.scale[j] : 0.0f;
+    s_bias[j] = p.bias[j];
+  }
+  if (threadIdx.x < 2) s_count[threadIdx.x] = 0;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) tab[i] = kInt8 ? p.table[i] : 0.0f;
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
     mbar_init(a_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&b_full[i], 1);
       mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&t_full[i], 1);
       mbar_init(&t_empty[i], 4);
     }
@@ -214,7 +251,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
 
   if (warp == 0) {
     if (lane == 0) {
-      uint32_t a_phase = 0, b_phase[2] = {0, 0};
+      uint32_t a_phase = 0, b_phases = 0;  // bit i: B buffer i's phase
       int bi = 0;
       for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
         if (!mbar_wait(a_empty, a_phase ^ 1, p.err, kErrTimeoutEmpty)) break;
@@ -223,11 +260,11 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
         for (int kb = 0; kb < p.nkb; ++kb) tma_load_3d(sa + kb * 16384, &p.tmap, kb * 128, t * 128, 0, a_full);
         bool ok = true;
         for (int c = 0; c < p.chunks; ++c) {
-          if (!mbar_wait(&b_empty[bi], b_phase[bi] ^ 1, p.err, kErrTimeoutEmpty)) {
+          if (!mbar_wait(&b_empty[bi], ((b_phases >> bi) & 1) ^ 1, p.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
           }
-          b_phase[bi] ^= 1;
+          b_phases ^= 1u << bi;
           mbar_expect_tx(&b_full[bi], p.b_bytes);
           bulk_load(sb + bi * p.b_bytes, p.wimg + static_cast<size_t>(c) * p.b_bytes, p.b_bytes, &b_full[bi]);
           bi ^= 1;
@@ -238,22 +275,23 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = kInt8 ? idesc_i8(p.nchunk) : idesc_f16(p.nchunk);
-      uint32_t a_phase = 0, b_phase[2] = {0, 0}, t_phase[2] = {0, 0};
-      int bi = 0, ti = 0;
+      uint32_t a_phase = 0, b_phases = 0, t_phases = 0, tsel = 0;  // bit i: buffer i's phase; bit h: half h's buffer
+      int bi = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         if (!mbar_wait(a_full, a_phase, p.err, kErrTimeoutFull)) break;
         a_phase ^= 1;
         for (int c = 0; c < p.chunks; ++c) {
-          if (!mbar_wait(&t_empty[ti], t_phase[ti] ^ 1, p.err, kErrTimeoutTmemEmpty) ||
-              !mbar_wait(&b_full[bi], b_phase[bi], p.err, kErrTimeoutFull)) {
+          const int half = c & 1, tb = 2 * half + ((tsel >> half) & 1);
+          if (!mbar_wait(&t_empty[tb], ((t_phases >> tb) & 1) ^ 1, p.err, kErrTimeoutTmemEmpty) ||
+              !mbar_wait(&b_full[bi], (b_phases >> bi) & 1, p.err, kErrTimeoutFull)) {
             ok = false;
             break;
           }
-          t_phase[ti] ^= 1;
-          b_phase[bi] ^= 1;
+          t_phases ^= 1u << tb;
+          b_phases ^= 1u << bi;
           tc_fence_after();
-          const uint32_t d = tmem_base + static_cast<uint32_t>(ti * 256);
+          const uint32_t d = tmem_base + static_cast<uint32_t>(tb * kHeadChunk);
           const uint32_t a0 = smem_u32(sa), b0 = smem_u32(sb + bi * p.b_bytes);
           uint32_t accumulate = 0;
           for (int kb = 0; kb < p.nkb; ++kb) {
@@ -265,77 +303,123 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
             }
           }
           umma_commit(&b_empty[bi]);
-          umma_commit(&t_full[ti]);
+          umma_commit(&t_full[tb]);
           bi ^= 1;
-          ti ^= 1;
+          tsel ^= 1u << half;
         }
         umma_commit(a_empty);
       }
     }
   } else {
-    const int quarter = warp & 3;
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
-    uint32_t t_phase[2] = {0, 0};
-    int ti = 0;
-    uint8_t* my = codes + row * ((p.classes + 15) & ~15);
+    const int e = threadIdx.x - 64;  // 0..255: this thread's place among the epilogue's
+    uint32_t t_phases = 0;  // bit i: this half's buffer i's phase
+    int tsel = 0;
     const float lo = static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
+    const int32_t zc = p.out_zero - kMagicBits;
+    constexpr float kLog2e = 1.44269504088896341f;
+    uint8_t* my = codes + row * cstride;
     bool ok = true;
-    int tile_parity = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, tile_parity ^= 1) {
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       const int ox = t * 128 + row;
-      int best = 0;
-      int bestq = -1;
-      float bestv = -INFINITY, sum = 0.0f;
-      for (int c = 0; c < p.chunks && ok; ++c) {
-        if (!mbar_wait(&t_full[ti], t_phase[ti], p.err, kErrTimeoutTmemFull)) {
+      int32_t mx = 0;                                   // INT8: this half's highest code
+      float fm = -INFINITY, fsum = 0.0f;                // FP16: this half's highest logit and sum
+      int fbest = 0;
+      for (int c = half; c < p.chunks && ok; c += 2) {
+        const int tb = 2 * half + tsel;
+        if (!mbar_wait(&t_full[tb], (t_phases >> tsel) & 1, p.err, kErrTimeoutTmemFull)) {
           ok = false;
           break;
         }
-        t_phase[ti] ^= 1;
+        t_phases ^= 1u << tsel;
+        tsel ^= 1;
         tc_fence_after();
-        // 16 classes of this chunk, from r[0..16), starting at chunk column cb
-        auto take16 = [&](const uint32_t* r, int cb) {
-          const int j0 = c * p.nchunk + cb;
+        const int cbase = c * p.nchunk;
+        // 16 classes from r[0..16), the first j0
+        auto take16 = [&](const uint32_t* r, int j0) {
           if constexpr (kInt8) {
-            alignas(16) uint8_t o[16];
+            int32_t code[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int j = j0 + i;
-              const int32_t s = static_cast<int32_t>(r[i]) - p.in_zero * s_colsum[j];
-              float v = __fmul_rn(static_cast<float>(s), s_scale[j]);
-              v = __fadd_rn(v, s_bias[j]);
-              float q = __fmul_rn(v, p.out_inv_scale);
-              q = q > lo ? q : lo;
-              q = q < hi ? q : hi;
-              const int code = __float2int_rn(q) + p.out_zero;
-              o[i] = static_cast<uint8_t>(code);
-              if (p.logits && j < p.classes && ox < p.ow) p.logits[static_cast<long long>(ox) * p.classes + j] = tab[code];
-              if (j < p.classes && code > bestq) {
-                bestq = code;
-                best = j;
+            for (int k = 0; k < 4; ++k) {
+              const int4 o = *reinterpret_cast<const int4*>(s_off + j0 + 4 * k);
+              const float4 sc = *reinterpret_cast<const float4*>(s_scale + j0 + 4 * k);
+              const float4 bb = *reinterpret_cast<const float4*>(s_bias + j0 + 4 * k);
+              const int32_t oo[4] = {o.x, o.y, o.z, o.w};
+              const float ss[4] = {sc.x, sc.y, sc.z, sc.w}, bv[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int32_t acc = static_cast<int32_t>(r[4 * k + u]);
+                // carbon/src/net/net.cpp:703-720: (acc - zero * colsum) * scale + bias, requantized
+                const float f = kFast ? magic_to_float(acc + oo[u]) : static_cast<float>(acc - oo[u]);
+                const float v = __fadd_rn(__fmul_rn(f, ss[u]), bv[u]);
+                float q = __fmul_rn(v, p.out_inv_scale);
+                q = fminf(fmaxf(q, lo), hi);
+                code[4 * k + u] = magic_rint_bits(q) + zc;  // in [0, 255]
               }
             }
-            if (j0 < ((p.classes + 15) & ~15)) *reinterpret_cast<uint4*>(my + j0) = *reinterpret_cast<const uint4*>(o);
+            uint4 packed;
+            uint32_t* pw = reinterpret_cast<uint32_t*>(&packed);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              pw[k] = __byte_perm(__byte_perm(code[4 * k], code[4 * k + 1], 0x0040),
+                                  __byte_perm(code[4 * k + 2], code[4 * k + 3], 0x0040), 0x5410);
+            *reinterpret_cast<uint4*>(my + j0) = packed;
+            if (j0 + 16 > p.classes) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (j0 + i >= p.classes) code[i] = 0;
+            }
+            int32_t m8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) m8[i] = max(code[i], code[i + 8]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) m8[i] = max(m8[i], m8[i + 4]);
+            mx = max(mx, max(max(m8[0], m8[1]), max(m8[2], m8[3])));
           } else {
+            float v[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int j = j0 + i;
-              if (j >= p.classes) continue;
-              const float v = __fadd_rn(__uint_as_float(r[i]), s_bias[j]);
-              if (p.logits && ox < p.ow) p.logits[static_cast<long long>(ox) * p.classes + j] = v;
-              if (v > bestv) {
-                sum = bestv == -INFINITY ? 1.0f : __fadd_rn(__fmul_rn(sum, exp_neg_d(__fsub_rn(bestv, v))), 1.0f);
-                bestv = v;
-                best = j;
-              } else {
-                sum = __fadd_rn(sum, exp_neg_d(__fsub_rn(v, bestv)));
-              }
+            for (int k = 0; k < 4; ++k) {
+              const float4 bb = *reinterpret_cast<const float4*>(s_bias + j0 + 4 * k);
+              v[4 * k] = __fadd_rn(__uint_as_float(r[4 * k]), bb.x);
+              v[4 * k + 1] = __fadd_rn(__uint_as_float(r[4 * k + 1]), bb.y);
+              v[4 * k + 2] = __fadd_rn(__uint_as_float(r[4 * k + 2]), bb.z);
+              v[4 * k + 3] = __fadd_rn(__uint_as_float(r[4 * k + 3]), bb.w);
             }
+            if (j0 + 16 > p.classes) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (j0 + i >= p.classes) v[i] = -INFINITY;
+            }
+            if (p.logits && ox < p.ow) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (j0 + i < p.classes) p.logits[static_cast<long long>(ox) * p.classes + j0 + i] = v[i];
+            }
+            float m8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) m8[i] = fmaxf(v[i], v[i + 8]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) m8[i] = fmaxf(m8[i], m8[i + 4]);
+            const float mb = fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3]));
+            if (mb > fm) {  // a new best: the first class holding it; the sum so far rescaled
+              int idx = 15;
+#pragma unroll
+              for (int i = 14; i >= 0; --i) idx = v[i] == mb ? i : idx;
+              fsum = fm == -INFINITY ? 0.0f : fsum * ex2_approx((fm - mb) * kLog2e);
+              fm = mb;
+              fbest = j0 + idx;
+            }
+            const float fl = fm * kLog2e;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) fsum += ex2_approx(fmaf(v[i], kLog2e, -fl));
           }
         };
-        // TMEM read 32 columns at a time, the next load in flight while the current is taken
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(ti * 256);
-        const int groups = p.nchunk / 16;
+        // TMEM read 32 columns at a time, the next load in flight while the current is taken; the
+        // buffer goes back to the MMA as soon as its last load has completed
+        const int groups = min(p.nchunk, (p.classes - cbase + 15) & ~15) >> 4;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(tb * kHeadChunk);
         uint32_t ra[32], rb[32];
         if (groups >= 2) tmem_ld32(taddr, ra); else tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(ra));
         tmem_wait_ld();
@@ -347,67 +431,104 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
             tmem_ld32(taddr + gn * 16, rb);
           } else if (gn < groups) {
             tmem_ld16(taddr + gn * 16, *reinterpret_cast<uint32_t(*)[16]>(rb));
+          } else {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&t_empty[tb]);
           }
-          take16(ra, g * 16);
-          if (w == 2) take16(ra + 16, g * 16 + 16);
-          tmem_wait_ld();
-          tmem_pin(rb);
+          take16(ra, cbase + g * 16);
+          if (w == 2) take16(ra + 16, cbase + g * 16 + 16);
+          if (gn < groups) {
+            tmem_wait_ld();
+            tmem_pin(rb);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ra[i] = rb[i];
+            for (int i = 0; i < 32; ++i) ra[i] = rb[i];
+          }
           g = gn;
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&t_empty[ti]);
-        ti ^= 1;
       }
-      const bool valid = ok && ox < p.ow && p.mask8[(static_cast<long long>(ox) << p.out_shift) >> 3] != 0;
+      // the two halves of each frame meet
+      if (!ok) s_count[1] = 1;
       if constexpr (kInt8) {
-        // the class-order sums only for the tile's non-blank frames, gathered into a list so every
-        // lane of the warps that run them has one (most frames are blank)
-        if (!ok) atomicOr(s_abort, 1);
-        s_best[row] = best;
-        if (valid && best != 0) {
-          const int k = atomicAdd(&nb_count[tile_parity], 1);
-          nb_row[k] = row;
-          nb_q[k] = bestq;
-        } else if (valid) {
-          p.frame_id[ox] = 0;
-          p.frame_prob[ox] = 0.0f;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        const int e = threadIdx.x - 64;  // 0..127: this thread's place among the epilogue's
-        if (e == 0) nb_count[tile_parity ^ 1] = 0;  // the next tile's counter (its adds follow the next barrier)
-        const int listed = nb_count[tile_parity];
-        const int stride = (p.classes + 15) & ~15;
-        if (!*s_abort) {
-          for (int k = e; k < listed; k += 128) {
-            const int r = nb_row[k];
-            const uint8_t* rowc = codes + r * stride;
-            const float top = tab[nb_q[k]];
-            float sum = 0.0f;
-            for (int j0 = 0; j0 < p.classes; j0 += 16) {
-              alignas(16) uint8_t q16[16];
-              *reinterpret_cast<uint4*>(q16) = *reinterpret_cast<const uint4*>(rowc + j0);
-              float term[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) term[i] = exp_neg_d(__fsub_rn(tab[q16[i]], top));
-#pragma unroll
-              for (int i = 0; i < 16; ++i)
-                if (j0 + i < p.classes) sum = __fadd_rn(sum, term[i]);
+        s_hmax[half * 128 + row] = mx;
+      } else {
+        s_hmax[half * 128 + row] = __float_as_int(fm);
+        s_hbest[half * 128 + row] = fbest;
+        s_hsum[half * 128 + row] = fsum;
+      }
+      named_bar(1, 256);
+      if (s_count[1]) break;
+      const bool valid = ox < p.ow && p.mask8[(static_cast<long long>(ox) << p.out_shift) >> 3] != 0;
+      if (half == 0) {
+        if constexpr (kInt8) {
+          // the first class with the highest code: for a blank frame the first 16 bytes hold it
+          const int32_t m = max(s_hmax[row], s_hmax[128 + row]);
+          const uint32_t m4 = static_cast<uint32_t>(m) * 0x01010101u;
+          int best = 0;
+          for (int j0 = 0; j0 < p.classes; j0 += 16) {
+            const uint4 w = *reinterpret_cast<const uint4*>(my + j0);
+            const uint32_t f0 = first_byte_eq(w.x, m4), f1 = first_byte_eq(w.y, m4);
+            const uint32_t f2 = first_byte_eq(w.z, m4), f3 = first_byte_eq(w.w, m4);
+            if (f0 | f1 | f2 | f3) {
+              best = j0 + (f0   ? (__ffs(f0) - 1) >> 3
+                           : f1 ? 4 + ((__ffs(f1) - 1) >> 3)
+                           : f2 ? 8 + ((__ffs(f2) - 1) >> 3)
+                                : 12 + ((__ffs(f3) - 1) >> 3));
+              break;
             }
-            const int fx = t * 128 + r;
-            p.frame_id[fx] = s_best[r];
-            p.frame_prob[fx] = __fdiv_rn(1.0f, sum);
+          }
+          s_best[row] = best;
+          if (valid && best != 0) {
+            const int k = atomicAdd(const_cast<int32_t*>(&s_count[0]), 1);
+            nb_row[k] = row;
+            nb_q[k] = m;
+          } else if (valid) {
+            p.frame_id[ox] = 0;
+            p.frame_prob[ox] = 0.0f;
+          }
+        } else {
+          const float m0 = __int_as_float(s_hmax[row]), m1 = __int_as_float(s_hmax[128 + row]);
+          const int b0 = s_hbest[row], b1 = s_hbest[128 + row];
+          const bool second = m1 > m0 || (m1 == m0 && b1 < b0);
+          const float top = second ? m1 : m0, other = second ? m0 : m1;
+          float sum = second ? s_hsum[128 + row] : s_hsum[row];
+          const float rest = second ? s_hsum[row] : s_hsum[128 + row];
+          if (other != -INFINITY) sum += rest * ex2_approx((other - top) * kLog2e);
+          const int best = second ? b1 : b0;
+          if (valid) {
+            p.frame_id[ox] = best;
+            p.frame_prob[ox] = best != 0 ? __fdiv_rn(1.0f, sum) : 0.0f;
           }
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (*s_abort) break;
-      } else {
-        if (!ok) break;
-        if (!valid) continue;
-        p.frame_id[ox] = best;
-        p.frame_prob[ox] = best != 0 ? __fdiv_rn(1.0f, sum) : 0.0f;
+      } else if (kInt8 && p.logits && ox < p.ow) {  // test hook: the dequantized logits
+        for (int j = 0; j < p.classes; ++j) p.logits[static_cast<long long>(ox) * p.classes + j] = tab[my[j]];
+      }
+      named_bar(1, 256);
+      if constexpr (kInt8) {
+        // the class-order sums of the listed (non-blank) frames, a thread a frame
+        const int listed = s_count[0];
+        for (int k = e; k < listed; k += 256) {
+          const int r = nb_row[k];
+          const uint8_t* rowc = codes + r * cstride;
+          const float* trow = p.terms + nb_q[k] * 256;
+          float sum = 0.0f;
+          int j0 = 0;
+          for (; j0 + 16 <= p.classes; j0 += 16) {
+            const uint4 w = *reinterpret_cast<const uint4*>(rowc + j0);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+            float term[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) term[i] = __ldg(trow + ((ww[i >> 2] >> (8 * (i & 3))) & 0xff));
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, term[i]);
+          }
+          for (; j0 < p.classes; ++j0) sum = __fadd_rn(sum, __ldg(trow + rowc[j0]));
+          const int fx = t * 128 + r;
+          p.frame_id[fx] = s_best[r];
+          p.frame_prob[fx] = __fdiv_rn(1.0f, sum);
+        }
+        named_bar(1, 256);
+        if (e == 0) s_count[0] = 0;  // read by every thread before the barrier; the next adds follow the next one
       }
     }
   }

@@ -195,6 +195,30 @@ __device__ __forceinline__ void tmem_pin(uint32_t (&r)[N]) {
   for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i])::"memory");
 }
 
+// A barrier among `count` threads of the block (a multiple of 32), id 1..15; id 0 is __syncthreads.
+__device__ __forceinline__ void named_bar(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Exact integer <-> float conversions on the FMA and integer pipes instead of the conversion
+// unit.  The floats in [2^23, 2^24) are the integers, one apart, so for an integer |s| < 2^22 the
+// float with bits kMagicBits + s is kMagic + s exactly, and for a float |x| <= 2^22 the sum
+// x + kMagic rounded to nearest (ties to even; kMagic is even) has bits kMagicBits + rint(x).
+constexpr int32_t kMagicBits = 0x4B400000;
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+
+// s (|s| < 2^22) as a float, given s + kMagicBits.
+__device__ __forceinline__ float magic_to_float(int32_t biased) { return __fsub_rn(__int_as_float(biased), kMagic); }
+// rint(x) + kMagicBits for |x| <= 2^22 (round to nearest, ties to even, as __float2int_rn).
+__device__ __forceinline__ int32_t magic_rint_bits(float x) { return __float_as_int(__fadd_rn(x, kMagic)); }
+
+// 2^x, the hardware approximation (PTX ex2.approx.ftz.f32); 2^-inf = 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t elect_one_sync() {
   uint32_t pred = 0;
   asm volatile(
