@@ -523,13 +523,8 @@ int encode_map(crec_handle* h, CUtensorMap* m, const void* base, uint64_t d0, ui
   return CREC_OK;
 }
 
-// The crop kernel's shared memory: a crop at the widest bucket, the strip intermediate, the
-// vertical coefficients, the histogram and counters.
-size_t crop_smem_bytes(const crec_handle* h, int max_bw) {
-  return ((static_cast<size_t>(h->height) * max_bw + 15) & ~size_t(15)) + kStripBytes + kCoefBytes +
-         (static_cast<size_t>(h->height) * kMaxTaps + 2 * h->height + 256 + 8) * 4 +
-         (kStemMaxOut * 9 + 2 * kStemMaxOut + 4 * kStemMaxOut) * 4 + 256;
-}
+// The crop kernel's shared memory for a run whose widest bucket is max_bw.
+size_t crop_smem_bytes(const crec_handle* h, int max_bw) { return crop_smem(h->height, max_bw).total + 16; }
 
 // Kernel kinds of the profile: 0 crop+stem, 1 dense convolutions (tcgen05), 2 depthwise, 3 head+CTC, 4 collapse.
 enum ProfKind { kProfCrop = 0, kProfConv = 1, kProfDw = 2, kProfHead = 3, kProfCollapse = 4 };

@@ -125,151 +125,252 @@ __device__ __forceinline__ uint8_t clip8d(int32_t v) {
   return static_cast<uint8_t>(v < 0 ? 0 : v > 255 ? 255 : v);
 }
 
-// Shared memory: crop [height][bw] | strip intermediate (kStripBytes) | a strip's horizontal
-// coefficients (kCoefBytes: first and count a column, then taps) | vertical coefficients |
-// the stem's weights and per-channel constants | histogram and counters.
+// Shared memory, in this order: the crop with a border (qb: [height + 4][qpitch], crop pixel
+// (y, x) at row y + 2, column x + 4; the border holds the INT8 input's zero point, the stem's
+// padding) | the strip intermediate (kStripBytes) | a strip's horizontal coefficients
+// (kCoefBytes: first and count a column, then taps) | the stem's weights and per-channel
+// constants | vertical coefficients | histogram, counters and tables.
+struct CropSmem {
+  int qpitch;
+  unsigned qb, tmp, hk, wq, swf, soff, sscale, sbias, vk, vfirst, vcount, hist, red, ftab, stab, total;
+};
+
+__host__ __device__ inline CropSmem crop_smem(int height, int max_bw) {
+  CropSmem s{};
+  s.qpitch = (max_bw + 12 + 15) & ~15;
+  unsigned o = 0;
+  s.qb = o;
+  o += static_cast<unsigned>((height + 4) * s.qpitch);
+  s.tmp = o;
+  o += kStripBytes;
+  s.hk = o;
+  o += kCoefBytes;
+  s.wq = o;  // INT8 [cout][3] a kernel row's taps, 4 bytes a row
+  o += kStemMaxOut * 3 * 4;
+  s.swf = o;  // FP16 [cout][taps]
+  o += kStemMaxOut * 9 * 4;
+  s.soff = o;
+  o += kStemMaxOut * 4;
+  s.sscale = o;
+  o += kStemMaxOut * 4;
+  s.sbias = o;
+  o += kStemMaxOut * 4;
+  s.vk = o;
+  o += static_cast<unsigned>(height * kMaxTaps * 4);
+  s.vfirst = o;
+  o += static_cast<unsigned>(height * 4);
+  s.vcount = o;
+  o += static_cast<unsigned>(height * 4);
+  s.hist = o;
+  o += 256 * 4;
+  s.red = o;
+  o += 8 * 4;
+  s.ftab = o;
+  o += 256 * 4;
+  s.stab = o;
+  o += 256;
+  s.total = o;
+  return s;
+}
+
+// The value of the n-th (from 0) byte of a 256-bin histogram in increasing order of value (of
+// 255 - value when flipped), 255 if there are not that many; warp-wide, every lane returns it.
+__device__ __forceinline__ int hist_nth(const int32_t* hist, int n, bool flipped) {
+  const int lane = threadIdx.x & 31;
+  int c[8], s = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int v = lane * 8 + k;
+    c[k] = hist[flipped ? 255 - v : v];
+    s += c[k];
+  }
+  int incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int excl = incl - s;
+  const uint32_t hit = __ballot_sync(0xffffffffu, excl <= n && n < incl);
+  if (hit == 0) return 255;
+  int v = lane * 8 + 7, run = excl;  // in the lane that holds it: the first k whose running count passes n
+  bool found = false;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    run += c[k];
+    if (!found && run > n) {
+      v = lane * 8 + k;
+      found = true;
+    }
+  }
+  return __shfl_sync(0xffffffffu, v, __ffs(hit) - 1);
+}
+
 template <bool kInt8>
 __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_constant__ CropParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int line = blockIdx.x;
   const LineDesc L = p.lines[line];
   const PageDesc P = p.pages[L.page];
-  const int H = p.height, bw = L.bw, cw = L.width;
-  uint8_t* crop = sm;                                                   // [H][bw]
-  uint8_t* tmp = crop + ((H * p.max_bw + 15) & ~15);                    // [rows][strip]
-  int32_t* hk = reinterpret_cast<int32_t*>(tmp + kStripBytes);         // [strip][2 + T]
-  int32_t* vk = hk + kCoefBytes / 4;                                   // [H][kMaxTaps]
-  int32_t* vfirst = vk + H * kMaxTaps;                                 // [H]
-  int32_t* vcount = vfirst + H;                                        // [H]
-  int32_t* hist = vcount + H;                                          // [256]
-  int32_t* red = hist + 256;                                           // [8] reductions
-  float* sw_ = reinterpret_cast<float*>(red + 8);                      // stem weights [cout][taps] (FP16 engine)
-  float* sscale = sw_ + kStemMaxOut * 9;                               // [cout]
-  float* sbias = sscale + kStemMaxOut;                                 // [cout]
-  uint32_t* sw4 = reinterpret_cast<uint32_t*>(sbias + kStemMaxOut);    // INT8: [cout][3] taps packed 4 a word
-  int32_t* scol = reinterpret_cast<int32_t*>(sw4 + kStemMaxOut * 3);   // [cout] weight sums
-  uint8_t* stab = reinterpret_cast<uint8_t*>(scol + kStemMaxOut);      // [256] input table
-  const int tid = threadIdx.x;
+  const int H = p.height, bw = L.bw, cw = p.crops_in ? L.bw : L.width;
+  const CropSmem S = crop_smem(H, p.max_bw);
+  const int qpitch = S.qpitch;
+  uint8_t* qb = sm + S.qb;
+  uint8_t* tmp = sm + S.tmp;
+  int32_t* hk = reinterpret_cast<int32_t*>(sm + S.hk);
+  uint32_t* wq = reinterpret_cast<uint32_t*>(sm + S.wq);
+  float* swf = reinterpret_cast<float*>(sm + S.swf);
+  int32_t* soff = reinterpret_cast<int32_t*>(sm + S.soff);
+  float* sscale = reinterpret_cast<float*>(sm + S.sscale);
+  float* sbias = reinterpret_cast<float*>(sm + S.sbias);
+  int32_t* vk = reinterpret_cast<int32_t*>(sm + S.vk);
+  int32_t* vfirst = reinterpret_cast<int32_t*>(sm + S.vfirst);
+  int32_t* vcount = reinterpret_cast<int32_t*>(sm + S.vcount);
+  int32_t* hist = reinterpret_cast<int32_t*>(sm + S.hist);
+  int32_t* red = reinterpret_cast<int32_t*>(sm + S.red);
+  float* ftab = reinterpret_cast<float*>(sm + S.ftab);
+  uint8_t* stab = sm + S.stab;
+  const int tid = threadIdx.x, nthr = blockDim.x;
   const int taps_stem = p.kh * p.kw;
+  auto px = [&](int y, int x) -> uint8_t& { return qb[(y + 2) * qpitch + x + 4]; };
 
-  if (!kInt8)
-    for (int i = tid; i < p.cout * taps_stem; i += blockDim.x) sw_[i] = p.wf[i];
-  if (kInt8)
-    for (int i = tid; i < p.cout * 3; i += blockDim.x) {  // taps 4k .. 4k+3 of channel i / 3, zeros past the last
-      const int j = i / 3, k = i % 3;
+  // the stem's constants; INT8: a channel's taps as one word per kernel row (zeros past kw), and
+  // the offset that turns the sum into kMagicBits + (sum - in_zero * colsum): |sum| <= 9 * 255 * 128
+  if (kInt8) {
+    for (int i = tid; i < kStemMaxOut * 3; i += nthr) {
+      const int j = i / 3, ky = i % 3;
       uint32_t w = 0;
-      for (int b = 0; b < 4; ++b) {
-        const int t = 4 * k + b;
-        if (t < taps_stem) w |= static_cast<uint32_t>(static_cast<uint8_t>(p.w8[j * taps_stem + t])) << (8 * b);
-      }
-      sw4[i] = w;
+      if (j < p.cout && ky < p.kh)
+        for (int kx = 0; kx < p.kw && kx < 4; ++kx)
+          w |= static_cast<uint32_t>(static_cast<uint8_t>(p.w8[j * taps_stem + ky * p.kw + kx])) << (8 * kx);
+      wq[i] = w;
     }
-  for (int i = tid; i < p.cout; i += blockDim.x) {
-    sscale[i] = kInt8 ? p.scale[i] : 1.0f;
-    sbias[i] = p.bias[i];
-    scol[i] = kInt8 ? p.colsum[i] : 0;
-  }
-  if (kInt8)
-    for (int i = tid; i < 256; i += blockDim.x) stab[i] = p.in_table[i];
-  for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
-  if (tid < 8) red[tid] = 0;
-
-  if (p.crops_in) {  // a ready crop (already finished and padded to its bucket width)
-    const uint8_t* src = p.crops_in + static_cast<long long>(line) * H * p.crops_in_pitch;
-    for (int i = tid; i < H * bw; i += blockDim.x) crop[i] = src[(i / bw) * p.crops_in_pitch + i % bw];
-    __syncthreads();
   } else {
-    // vertical coefficients, one thread a row
-    for (int yy = tid; yy < H; yy += blockDim.x) {
+    for (int i = tid; i < p.cout * taps_stem; i += nthr) swf[i] = p.wf[i];
+  }
+  for (int i = tid; i < kStemMaxOut; i += nthr) {
+    const bool in = i < p.cout;
+    sscale[i] = kInt8 && in ? p.scale[i] : 1.0f;
+    sbias[i] = in ? p.bias[i] : 0.0f;
+    soff[i] = kInt8 && in ? kMagicBits - p.in_zero * p.colsum[i] : kMagicBits;
+  }
+  for (int i = tid; i < 256; i += nthr) {
+    if (kInt8) stab[i] = p.in_table[i];
+    // the FP16 engine's input: the ink 1 - p / 255 rounded to float16
+    ftab[i] = __half2float(__float2half_rn(__fsub_rn(1.0f, __fdiv_rn(static_cast<float>(i), 255.0f))));
+    hist[i] = 0;
+  }
+  if (tid < 8) red[tid] = 0;
+  __syncthreads();  // the tables and counters before any use (a ready crop goes straight to the final pass)
+
+  bool flip = false;
+  uint8_t ground = 0;
+  if (!p.crops_in) {
+    // this line's tap stride (PIL's ksize) and strip width, from a bound on the source rows the
+    // vertical windows span: each window lies within [y0 - support - 1, y1 + support + 1]
+    const double hscale = (L.x1 - L.x0) / cw;
+    const int T = min(kMaxTaps, static_cast<int>(ceil(hscale < 1.0 ? 1.0 : hscale)) * 2 + 1);
+    const double vspan = L.y1 - L.y0, vsup = vspan / H < 1.0 ? 1.0 : vspan / H;
+    const int rows_ub = static_cast<int>(ceil(vspan + 2.0 * vsup)) + 4;
+    const int strip = max(16, min(kMaxStripCols, min(kStripBytes / max(rows_ub, 1), kCoefBytes / (4 * (T + 2)))));
+    // vertical coefficients (a thread a row) and the first strip's horizontal ones (a thread a column)
+    for (int yy = tid; yy < H; yy += nthr) {
       int n;
       vfirst[yy] = coeffs(L.y0, L.y1, H, yy, vk + yy * kMaxTaps, &n);
       vcount[yy] = n;
     }
+    for (int xx = tid; xx < min(strip, cw); xx += nthr) {
+      int32_t* c = hk + xx * (T + 2);
+      int n;
+      c[0] = coeffs(L.x0, L.x1, cw, xx, c + 2, &n);
+      c[1] = n;
+    }
     __syncthreads();
     const int top = vfirst[0];
     const int rows = vfirst[H - 1] + vcount[H - 1] - top;
-    if (rows > kMaxSrcRows) {
+    if (rows > kMaxSrcRows || rows > rows_ub) {
       if (tid == 0) atomicCAS(p.err, 0, kErrBadShape);
       return;
     }
-    // this line's tap stride: the filter's most taps (PIL's ksize)
-    const double hscale = (L.x1 - L.x0) / cw;
-    const int T = min(kMaxTaps, static_cast<int>(ceil(hscale < 1.0 ? 1.0 : hscale)) * 2 + 1);
-    const int strip = max(16, min(kMaxStripCols, min(kStripBytes / max(rows, 1), kCoefBytes / (4 * (T + 2)))));
     for (int x0 = 0; x0 < cw; x0 += strip) {
       const int sc = min(strip, cw - x0);
-      // the strip's horizontal coefficients, a thread a column
-      for (int xx = tid; xx < sc; xx += blockDim.x) {
-        int32_t* c = hk + xx * (T + 2);
-        int n;
-        c[0] = coeffs(L.x0, L.x1, cw, x0 + xx, c + 2, &n);
-        c[1] = n;
+      if (x0 > 0) {
+        __syncthreads();  // the previous strip's vertical pass has read tmp and hk
+        for (int xx = tid; xx < sc; xx += nthr) {
+          int32_t* c = hk + xx * (T + 2);
+          int n;
+          c[0] = coeffs(L.x0, L.x1, cw, x0 + xx, c + 2, &n);
+          c[1] = n;
+        }
+        __syncthreads();
       }
-      __syncthreads();
-      // horizontal pass: a thread an (intermediate row, column)
-      for (int i = tid; i < rows * sc; i += blockDim.x) {
-        const int r = i / sc, xx = i - r * sc;
+      // a thread a column of the strip, the rows split into groups when the strip is narrow
+      const int groups = max(1, nthr / sc);
+      const int rg = tid / sc, xx = tid - rg * sc;
+      if (rg < groups) {
+        // horizontal pass: every source row the vertical windows read
         const int32_t* c = hk + xx * (T + 2);
         const int xmin = c[0], n = c[1];
-        const int y = top + r;
-        int32_t ss = 1 << 21;
-        if (y >= 0 && y < P.height) {
-          const uint8_t* src = P.data + static_cast<long long>(y) * P.stride;
-          if (xmin >= 0 && xmin + n <= P.width) {
-            for (int t = 0; t < n; ++t) ss += static_cast<int32_t>(__ldg(src + xmin + t)) * c[2 + t];
-          } else {
-            for (int t = 0; t < n; ++t) {
-              const int x = xmin + t;
-              ss += ((x >= 0 && x < P.width) ? static_cast<int32_t>(__ldg(src + x)) : 255) * c[2 + t];
+        const bool inside = xmin >= 0 && xmin + n <= P.width;
+        for (int r = rg; r < rows; r += groups) {
+          const int y = top + r;
+          int32_t ss = 1 << 21;
+          if (y >= 0 && y < P.height) {
+            const uint8_t* src = P.data + static_cast<long long>(y) * P.stride + xmin;
+            if (inside) {
+              for (int t = 0; t < n; ++t) ss += static_cast<int32_t>(__ldg(src + t)) * c[2 + t];
+            } else {
+              for (int t = 0; t < n; ++t) {
+                const int x = xmin + t;  // pixels off the page read as paper
+                ss += ((x >= 0 && x < P.width) ? static_cast<int32_t>(__ldg(src + t)) : 255) * c[2 + t];
+              }
             }
+          } else {
+            for (int t = 0; t < n; ++t) ss += 255 * c[2 + t];
           }
-        } else {
-          for (int t = 0; t < n; ++t) ss += 255 * c[2 + t];
+          tmp[r * strip + xx] = clip8d(ss);
         }
-        tmp[r * strip + xx] = clip8d(ss);
       }
       __syncthreads();
-      // vertical pass: a thread an output pixel
-      for (int i = tid; i < H * sc; i += blockDim.x) {
-        const int yy = i / sc, xx = i - yy * sc;
-        const int f = vfirst[yy] - top, n = vcount[yy];
-        int32_t ss = 1 << 21;
-        for (int t = 0; t < n; ++t) ss += tmp[(f + t) * strip + xx] * vk[yy * kMaxTaps + t];
-        crop[yy * bw + x0 + xx] = clip8d(ss);
+      if (rg < groups) {
+        // vertical pass: the strip's output pixels
+        for (int yy = rg; yy < H; yy += groups) {
+          const int f = vfirst[yy] - top, n = vcount[yy];
+          const int32_t* k = vk + yy * kMaxTaps;
+          int32_t ss = 1 << 21;
+          for (int t = 0; t < n; ++t) ss += tmp[(f + t) * strip + xx] * k[t];
+          px(yy, x0 + xx) = clip8d(ss);
+        }
       }
-      __syncthreads();
     }
-  // finish: the ground's histogram (first row, last row, last column)
-    for (int x = tid; x < cw; x += blockDim.x) {
-      atomicAdd(&hist[crop[x]], 1);
-      atomicAdd(&hist[crop[(H - 1) * bw + x]], 1);
+    __syncthreads();
+    // finish: the ground's histogram (first row, last row, last column)
+    for (int x = tid; x < cw; x += nthr) {
+      atomicAdd(&hist[px(0, x)], 1);
+      atomicAdd(&hist[px(H - 1, x)], 1);
     }
-    for (int y = tid; y < H; y += blockDim.x) atomicAdd(&hist[crop[y * bw + cw - 1]], 1);
+    for (int y = tid; y < H; y += nthr) atomicAdd(&hist[px(y, cw - 1)], 1);
     __syncthreads();
     const int count = 2 * cw + H;
-    auto nth = [&](int n, bool flipped) {
-      int seen = 0;
-      for (int v = 0; v < 256; ++v) {
-        seen += hist[flipped ? 255 - v : v];
-        if (seen > n) return v;
-      }
-      return 255;
-    };
     auto ground_of = [&](bool flipped) {
-      return count % 2 ? nth(count / 2, flipped) : (nth(count / 2 - 1, flipped) + nth(count / 2, flipped)) / 2;
+      return count % 2 ? hist_nth(hist, count / 2, flipped)
+                       : (hist_nth(hist, count / 2 - 1, flipped) + hist_nth(hist, count / 2, flipped)) / 2;
     };
-    if (tid == 0) red[0] = ground_of(false);
+    if (tid < 32) {
+      const int g = ground_of(false);
+      if (tid == 0) red[0] = g;
+    }
     __syncthreads();
-    bool flip = false;
     if (p.flip_margin > 0) {
       const int g = red[0], lo = g - p.flip_margin, hi = g + p.flip_margin;
       int below = 0, above = 0, dark = 0;
-      for (int i = tid; i < H * cw; i += blockDim.x) {
-        const int v = crop[(i / cw) * bw + i % cw];
-        below += v <= lo;
-        above += v >= hi;
-        dark += v <= 127;
-      }
+      for (int x = tid; x < cw; x += nthr)
+        for (int y = 0; y < H; ++y) {
+          const int v = px(y, x);
+          below += v <= lo;
+          above += v >= hi;
+          dark += v <= 127;
+        }
       for (int o = 16; o > 0; o >>= 1) {
         below += __shfl_xor_sync(0xffffffffu, below, o);
         above += __shfl_xor_sync(0xffffffffu, above, o);
@@ -284,86 +385,111 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
       flip = red[2] > red[1];
       if (flip && p.flip_needs_dark) flip = 2 * static_cast<long long>(red[3]) > static_cast<long long>(cw) * H;
     }
-    if (tid == 0) red[4] = ground_of(flip);
-    __syncthreads();
-    const uint8_t ground = static_cast<uint8_t>(red[4]);
-    for (int i = tid; i < H * bw; i += blockDim.x) {
-      const int y = i / bw, x = i % bw;
-      uint8_t v = crop[y * bw + x];
-      if (x >= cw) {
-        v = ground;
-      } else if (flip) {
-        v = static_cast<uint8_t>(255 - v);
-      }
-      crop[y * bw + x] = v;
+    if (tid < 32) {
+      const int g = ground_of(flip);
+      if (tid == 0) red[4] = g;
     }
     __syncthreads();
-    if (p.crops_out) {
-      uint8_t* dst = p.crops_out + static_cast<long long>(line) * H * p.crops_pitch;
-      for (int i = tid; i < H * bw; i += blockDim.x)
-      if (i % bw < p.crops_pitch) dst[(i / bw) * p.crops_pitch + i % bw] = crop[i];
-    }
-
+    ground = static_cast<uint8_t>(red[4]);
   }
-  // the stem on the quantized crop (its border the input's zero point: real zero), into the
-  // line's segment of the stem tensor; a thread an output pixel and all its channels
+  // the finished crop (flipped, padded to the bucket width with the ground) and, for INT8, its
+  // quantized input in place, the border the zero point; a thread a column of qb
+  {
+    const uint8_t* src = p.crops_in ? p.crops_in + static_cast<long long>(line) * H * p.crops_in_pitch : nullptr;
+    uint8_t* dst = p.crops_out ? p.crops_out + static_cast<long long>(line) * H * p.crops_pitch : nullptr;
+    const uint8_t zq = static_cast<uint8_t>(p.in_zero);
+    for (int c = tid; c < qpitch; c += nthr) {
+      const int x = c - 4;
+      const bool col_in = x >= 0 && x < bw;
+      for (int r = 0; r < H + 4; ++r) {
+        const int y = r - 2;
+        uint8_t& q = qb[r * qpitch + c];
+        if (!col_in || y < 0 || y >= H) {
+          if (kInt8) q = zq;
+          continue;
+        }
+        uint8_t v;
+        if (src) v = src[y * p.crops_in_pitch + x];
+        else if (x >= cw) v = ground;
+        else v = flip ? static_cast<uint8_t>(255 - q) : q;
+        if (dst && x < p.crops_pitch) dst[y * p.crops_pitch + x] = v;
+        q = kInt8 ? stab[v] : v;
+      }
+    }
+  }
+  __syncthreads();
+
+  // the stem, into the line's segment of the stem tensor: a thread an output pixel and all its channels
   const int oh = (H + 2 * p.pt - p.kh) / p.sh + 1, ow = (bw + 2 * p.pl - p.kw) / p.sw + 1;
   const long long col0 = static_cast<long long>(L.seg) >> p.out_shift;
   const int eb = kInt8 ? 1 : 2;
-  const bool fast = p.in_zero == 0 && p.out_zero == 0 && p.relu && p.cout == p.cp_out;
-  for (int i = tid; i < oh * ow; i += blockDim.x) {
+  const float lo = p.relu ? 0.0f : static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
+  const int32_t zc = p.out_zero - kMagicBits;
+  const bool windows = kInt8 && p.kh <= 3 && p.kw <= 4 && p.pt >= 0 && p.pt <= 2 && p.pl >= 0 && p.pl <= 4;
+  for (int i = tid; i < oh * ow; i += nthr) {
     const int oy = i / ow, ox = i - oy * ow;
     uint8_t* dst = p.out + (oy + p.out_ph) * p.out_pitch + (col0 + ox) * p.cp_out * eb;
     if constexpr (kInt8) {
-      // the taps' quantized inputs packed 4 a word (the border reads the zero point: real zero);
-      // sum over taps of (a - zero) * w = dp4a(a, w) - zero * sum(w), exact in int32
-      uint32_t a4[3] = {0, 0, 0};
-      for (int t = 0; t < taps_stem; ++t) {
-        const int y = oy * p.sh - p.pt + t / p.kw, x = ox * p.sw - p.pl + t % p.kw;
-        const uint32_t q = (y >= 0 && y < H && x >= 0 && x < bw) ? stab[crop[y * bw + x]] : static_cast<uint32_t>(p.in_zero);
-        a4[t >> 2] |= q << (8 * (t & 3));
-      }
-      uint32_t words[kStemMaxOut / 4];
-      const float lo = static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
-      for (int c0 = 0; c0 < p.cp_out; c0 += 4) {
-        uint32_t wv = 0;
+      // a kernel row's taps, 4 bytes a word (past kw: anything, the weights there are 0); the
+      // border reads the zero point: real zero
+      uint32_t a[3] = {0, 0, 0};
+      if (windows) {
+        const int cs = ox * p.sw - p.pl + 4, rs = oy * p.sh - p.pt + 2;
+        const int al = cs & ~3;
+        const uint32_t sel = 0x3210u + static_cast<uint32_t>(cs & 3) * 0x1111u;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = c0 + u;
-          uint32_t code = static_cast<uint32_t>(p.out_zero);
-          if (j < p.cout) {
-            const uint32_t* w = sw4 + j * 3;
-            int32_t sum = dp4a_us(a4[0], w[0], 0);
-            sum = dp4a_us(a4[1], w[1], sum);
-            sum = dp4a_us(a4[2], w[2], sum);
-            sum -= p.in_zero * scol[j];
-            float v = __fadd_rn(__fmul_rn(static_cast<float>(sum), sscale[j]), sbias[j]);
-            if (fast) {
-              code = cvt_rni_sat_u8(__fmul_rn(v, p.out_inv_scale));
-            } else {
-              if (p.relu) v = v > 0.0f ? v : 0.0f;
-              float q = __fmul_rn(v, p.out_inv_scale);
-              q = q > lo ? q : lo;
-              q = q < hi ? q : hi;
-              code = static_cast<uint32_t>(__float2int_rn(q) + p.out_zero);
-            }
+        for (int ky = 0; ky < 3; ++ky) {
+          if (ky < p.kh) {
+            const uint8_t* rp = qb + (rs + ky) * qpitch + al;
+            a[ky] = __byte_perm(*reinterpret_cast<const uint32_t*>(rp), *reinterpret_cast<const uint32_t*>(rp + 4), sel);
           }
-          wv |= (code & 0xffu) << (8 * u);
         }
-        words[c0 >> 2] = wv;
+      } else {
+        for (int ky = 0; ky < p.kh && ky < 3; ++ky)
+          for (int kx = 0; kx < p.kw && kx < 4; ++kx) {
+            const int y = oy * p.sh - p.pt + ky, x = ox * p.sw - p.pl + kx;
+            const uint32_t q = (y >= 0 && y < H && x >= 0 && x < bw) ? px(y, x) : static_cast<uint32_t>(p.in_zero);
+            a[ky] |= q << (8 * kx);
+          }
       }
-      for (int c0 = 0; c0 < p.cp_out; c0 += 16)
-        *reinterpret_cast<uint4*>(dst + c0) =
-            make_uint4(words[c0 >> 2], words[(c0 >> 2) + 1], words[(c0 >> 2) + 2], words[(c0 >> 2) + 3]);
+      // sum over taps of (a - zero) * w = dp4a(a, w) - zero * colsum, exact in int32; then the
+      // output stage with exact conversions (kMagic)
+      for (int c16 = 0; c16 < p.cp_out; c16 += 16) {
+        uint32_t wv[4];
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const int j = c16 + 4 * c4;
+          const uint4* w4 = reinterpret_cast<const uint4*>(wq + j * 3);
+          const uint4 wa = w4[0], wb = w4[1], wc = w4[2];
+          const uint32_t w[12] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w, wc.x, wc.y, wc.z, wc.w};
+          const int4 o4 = *reinterpret_cast<const int4*>(soff + j);
+          const float4 s4 = *reinterpret_cast<const float4*>(sscale + j);
+          const float4 b4 = *reinterpret_cast<const float4*>(sbias + j);
+          const int32_t oo[4] = {o4.x, o4.y, o4.z, o4.w};
+          const float ss[4] = {s4.x, s4.y, s4.z, s4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
+          int32_t code[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            int32_t acc = dp4a_us(a[0], w[3 * u], oo[u]);
+            acc = dp4a_us(a[1], w[3 * u + 1], acc);
+            acc = dp4a_us(a[2], w[3 * u + 2], acc);
+            const float v = __fadd_rn(__fmul_rn(magic_to_float(acc), ss[u]), bb[u]);
+            const float q = fminf(fmaxf(__fmul_rn(v, p.out_inv_scale), lo), hi);
+            code[u] = magic_rint_bits(q) + zc;
+          }
+          wv[c4] = __byte_perm(__byte_perm(code[0], code[1], 0x0040), __byte_perm(code[2], code[3], 0x0040), 0x5410);
+        }
+        *reinterpret_cast<uint4*>(dst + c16) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      }
     } else {
       float in[9];
+#pragma unroll
       for (int t = 0; t < 9; ++t) {
         in[t] = 0.0f;
         if (t >= taps_stem) continue;
         const int y = oy * p.sh - p.pt + t / p.kw, x = ox * p.sw - p.pl + t % p.kw;
         if (y < 0 || y >= H || x < 0 || x >= bw) continue;  // the border: real zero
-        // the FP16 engine's input: the ink 1 - p / 255 rounded to float16
-        in[t] = __half2float(__float2half_rn(__fsub_rn(1.0f, __fdiv_rn(static_cast<float>(crop[y * bw + x]), 255.0f))));
+        in[t] = ftab[px(y, x)];
       }
       for (int c0 = 0; c0 < p.cp_out; c0 += 16) {
         alignas(16) __half o[16];
@@ -372,7 +498,9 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
           const int j = c0 + u;
           float v = 0.0f;
           if (j < p.cout) {
-            for (int t = 0; t < taps_stem; ++t) v = __fmaf_rn(in[t], sw_[j * taps_stem + t], v);
+#pragma unroll
+            for (int t = 0; t < 9; ++t)
+              if (t < taps_stem) v = __fmaf_rn(in[t], swf[j * taps_stem + t], v);
             v = __fadd_rn(v, sbias[j]);
             if (p.relu) v = v > 0.0f ? v : 0.0f;
           }
@@ -385,14 +513,14 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
   }
   // the gap after this line's segment (and before the first line's), the zero point
   const long long gap0 = col0 + ow, gap1 = static_cast<long long>(L.next_seg) >> p.out_shift;
-  const long long lead = line == 0 ? col0 : 0;
-  const long long gapn = (gap1 - gap0) + lead;
+  const int lead = line == 0 ? static_cast<int>(col0) : 0;
+  const int gapn = static_cast<int>(gap1 - gap0) + lead;
   const int vec = p.cp_out * eb / 16;
   const uint32_t zb = kInt8 ? static_cast<uint32_t>(p.out_zero) * 0x01010101u : 0u;
   const uint4 z4 = make_uint4(zb, zb, zb, zb);
-  for (long long i = tid; i < gapn * oh * vec; i += blockDim.x) {
-    const long long v = i % vec, rest = i / vec;
-    const long long c = rest % gapn, oy = rest / gapn;
+  for (int i = tid; i < gapn * oh * vec; i += nthr) {
+    const int v = i % vec, rest = i / vec;
+    const int c = rest % gapn, oy = rest / gapn;
     const long long col = c < lead ? c : gap0 + (c - lead);
     *reinterpret_cast<uint4*>(p.out + (oy + p.out_ph) * p.out_pitch + col * p.cp_out * eb + v * 16) = z4;
   }
