@@ -258,6 +258,7 @@ def main() -> int:
     results = {}
     clocks = None
     prof = None
+    layers = None
     stats = None
     for prec in (["int8"] if args.no_fp16 else ["int8", "fp16"]):
         dev = native.RecDevice(blobs[prec], native.INT8 if prec == "int8" else native.FP16, device=local,
@@ -271,6 +272,7 @@ def main() -> int:
             dev.profile(1)
             with ClockSampler(local) as cs:
                 secs = timed(dev, step, args.steps)
+            layers = dev.profile_layers()
             prof = dev.profile(0)
             stats = dev.last_stats()
             clocks = cs.summary()
@@ -334,6 +336,9 @@ def main() -> int:
                          "avg_launch_ms": ms / launches if launches else None, "ops_per_launch": ops / launches if launches else None,
                          "traffic": None},
             "kernels": {k: {"launches": v[0], "ms": v[1], "ops": v[2]} for k, v in (prof or {}).items()},
+            "layers": [{"layer": i, "kernel": k, "launches": n, "ms": round(t, 3),
+                        "tops": round(o / t / 1e9, 1) if t > 0 else None}
+                       for i, (k, n, t, o) in enumerate(layers or []) if n],
             "clocks": clocks,
             "cpu_baseline": base,
         }

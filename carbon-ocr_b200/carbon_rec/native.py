@@ -26,7 +26,7 @@ _NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA
 EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec_set_pages", "crec_prefetch_pages",
            "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_ctc_greedy", "crec_ctc_greedy_noalloc", "crec_width_bucket", "crec_crop_region",
            "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats",
-           "crec_profile"]
+           "crec_profile", "crec_profile_layers"]
 
 
 class CrecError(RuntimeError):
@@ -111,6 +111,7 @@ def lib() -> C.CDLL:
         L.crec_debug_logits.argtypes = [p, p, i64]
         L.crec_last_stats.argtypes = [p, C.POINTER(Stats)]
         L.crec_profile.argtypes = [p, i, C.POINTER(ProfileEntry), i]
+        L.crec_profile_layers.argtypes = [p, C.POINTER(ProfileEntry), i]
         _lib = L
     return _lib
 
@@ -332,6 +333,14 @@ class RecDevice:
         ent = (ProfileEntry * 8)()
         n = lib().crec_profile(self._h, int(enable), ent, 8)
         return {ent[i].kernel.decode(): (ent[i].launches, ent[i].ms, ent[i].ops) for i in range(max(n, 0))}
+
+    def profile_layers(self) -> list:
+        """Per layer (then the collapse): (kernel, launches, ms, ops) since profiling was (re)started."""
+        ent = (ProfileEntry * 64)()
+        n = lib().crec_profile_layers(self._h, ent, 64)
+        if n < 0:
+            self._check(-n)
+        return [(ent[i].kernel.decode(), ent[i].launches, ent[i].ms, ent[i].ops) for i in range(n)]
 
     def arm_logits(self) -> None:
         self._check(lib().crec_debug_logits(self._h, None, 0))

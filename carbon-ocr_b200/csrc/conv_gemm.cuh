@@ -21,13 +21,16 @@
 // ReLU, * inv_scale, clamped to [-zero, 255 - zero], rounded half to even, + zero.
 // FP16: A and B float16, FP32 sums; bias, residual and ReLU in FP32, stored as float16.
 //
-// Warp roles (10 warps): 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-9 epilogue: two warps
-// for each TMEM lane quarter (the quarter of its warp index mod 4), each taking half of a tile's
-// channel groups.  The epilogue is where an INT8 layer's time goes (requantizing 128 x N outputs
-// costs more CUDA-core cycles than the tensor cores' MMAs for K below ~700), hence 8 warps, the
-// per-channel constants in shared memory, and for layers with both zero points 0 and a ReLU
-// (most of the backbone) one saturating convert: cvt.rni.sat.u8 rounds half to even and clamps
-// to [0, 255], which is the reference's ReLU, clamp and round for a zero point of 0.
+// Warp roles (10 warps): 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-9 epilogue: warps 2-5
+// take the CTA's even tiles, warps 6-9 its odd ones, each warp the 32 TMEM lanes (pixels) of its
+// quarter (its warp index mod 4) and all of a tile's channels.  Up to eight accumulators in TMEM
+// (512 columns over the tile's N rounded up to a power of two), so the MMA runs ahead of the
+// epilogue.  The epilogue is where an INT8 layer's time goes (requantizing 128 x N outputs costs
+// more CUDA-core cycles than the tensor cores' MMAs for K below ~700): the per-channel constants
+// in shared memory read four at a time, the line mask of the next tile loaded during this one,
+// and the int <-> float conversions done exactly on the FMA pipe (kMagic) wherever the layer's
+// sums fit in 22 bits (the host bounds them from the weights), the ReLU folded into the clamp
+// (v * inv_scale is monotone, so clamping at 0 is the ReLU).
 #pragma once
 
 #include <cuda.h>
@@ -35,7 +38,6 @@
 
 #include <cstdint>
 
-#include "crop_stem.cuh"  // cvt_rni_sat_u8
 #include "sm100.cuh"
 
 namespace crec {
@@ -53,10 +55,11 @@ struct ConvParams {
   int out_ph;
   long long out_pitch;  // bytes per output row
   int cp_out, c_out, ebytes;
-  const int32_t* colsum;  // [cp_out] sum of each output channel's int8 weights
+  const int32_t* off;     // INT8 [cp_out]: kMagicBits - in_zero * colsum (fast), else in_zero * colsum
   const float* scale;     // [cp_out] input scale * weight scale (int8)
   const float* bias;      // [cp_out]
-  int in_zero, out_zero, relu;
+  int out_zero, relu;
+  int n_acc;              // TMEM accumulators (a power of two, <= kMaxAcc), each 512 / n_acc columns
   float out_inv_scale;
   const uint8_t* res;  // residual tensor's first row, or null
   int res_ph, res_cp, res_shift, res_zero;
@@ -68,24 +71,29 @@ struct ConvParams {
 };
 
 constexpr int kConvThreads = 320;
-constexpr int kConvEpiWarps = 8;
+constexpr int kMaxAcc = 8;
 constexpr uint32_t kTmemCols = 512;
 
-template <bool kInt8>
+// The accumulators a layer with tiles of nt channels gets.
+__host__ __device__ constexpr int conv_accumulators(int nt) {
+  return nt <= 32 ? 8 : nt <= 64 ? 8 : nt <= 128 ? 4 : 2;
+}
+
+template <bool kInt8, bool kFast>
 __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid_constant__ ConvParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-aligned base for the swizzled stages
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
   uint64_t* empty = full + p.stages;
-  uint64_t* tmem_full = empty + p.stages;
-  uint64_t* tmem_empty = tmem_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
-  int32_t* s_colsum = reinterpret_cast<int32_t*>(tmem_slot + 4);  // [cp_out] per-channel constants
-  float* s_scale = reinterpret_cast<float*>(s_colsum + p.cp_out);
+  uint64_t* tmem_full = empty + p.stages;      // [kMaxAcc]
+  uint64_t* tmem_empty = tmem_full + kMaxAcc;  // [kMaxAcc]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + kMaxAcc);
+  int32_t* s_off = reinterpret_cast<int32_t*>(tmem_slot + 4);  // [cp_out] per-channel constants
+  float* s_scale = reinterpret_cast<float*>(s_off + p.cp_out);
   float* s_bias = s_scale + p.cp_out;
   for (int j = threadIdx.x; j < p.cp_out; j += blockDim.x) {
-    s_colsum[j] = p.colsum[j];
+    s_off[j] = kInt8 ? p.off[j] : 0;
     s_scale[j] = p.scale[j];
     s_bias[j] = p.bias[j];
   }
@@ -96,9 +104,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kMaxAcc; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], kConvEpiWarps);
+      mbar_init(&tmem_empty[a], 4);  // the four warps of the half that takes the tile
     }
     fence_mbar_init();
   }
@@ -111,6 +119,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int ksteps_per_tile = p.kh * p.nkb;
+  const uint32_t acc_cols = kTmemCols / static_cast<uint32_t>(p.n_acc);
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -145,31 +154,37 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = kInt8 ? idesc_i8(p.nt) : idesc_f16(p.nt);
+      // the stages' descriptors differ only in the start address (bits 0..13, address >> 4): a
+      // K step of 32 bytes adds 2, a stage stage_bytes >> 4
+      const uint64_t a_desc0 = umma_desc_sw128(smem_u32(smem)), b_desc0 = umma_desc_sw128(smem_u32(smem) + p.a_bytes);
+      const uint32_t stage_step = p.stage_bytes >> 4;
       int stage = 0;
       uint32_t phase = 0;
       int iter = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++iter) {
-        const int acc = iter & 1;
-        const uint32_t acc_phase = (iter >> 1) & 1;
+        const int acc = iter & (p.n_acc - 1);
+        const uint32_t acc_phase = (iter / p.n_acc) & 1;
         if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, p.err, kErrTimeoutTmemEmpty)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * 256);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc) * acc_cols;
         uint32_t accumulate = 0;
+        int kb = 0;
         for (int ks = 0; ks < ksteps_per_tile; ++ks) {
           if (!mbar_wait(&full[stage], phase, p.err, kErrTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a = smem_u32(smem + stage * p.stage_bytes);
-          const uint32_t b = a + p.a_bytes;
-          const int steps = (ks % p.nkb == p.nkb - 1) ? p.last_steps : 4;
-          for (int s = 0; s < steps; ++s) {
-            umma<kInt8>(d, umma_desc_sw128(a + s * 32), umma_desc_sw128(b + s * 32), idesc, accumulate);
-            accumulate = 1;
-          }
+          const uint64_t ad = a_desc0 + static_cast<uint64_t>(stage) * stage_step;
+          const uint64_t bd = b_desc0 + static_cast<uint64_t>(stage) * stage_step;
+          const int steps = ++kb == p.nkb ? p.last_steps : 4;
+          if (kb == p.nkb) kb = 0;
+#pragma unroll
+          for (int s = 0; s < 4; ++s)
+            if (s < steps) umma<kInt8>(d, ad + 2 * s, bd + 2 * s, idesc, accumulate | static_cast<uint32_t>(s));
           umma_commit(&empty[stage]);
+          accumulate = 1;
           if (++stage == p.stages) {
             stage = 0;
             phase ^= 1;
@@ -180,22 +195,34 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     }
   } else {
     // ---------------------------------------------------------------- epilogue
-    const int quarter = warp & 3;  // the TMEM lanes this warp may read
-    const int half = (warp - 2) >> 2;  // which half of the tile's channel groups
+    const int quarter = warp & 3;      // the TMEM lanes this warp may read
+    const int half = (warp - 2) >> 2;  // the CTA's even (0) or odd (1) tiles
     const int row = quarter * 32 + lane;
-    const bool fast = kInt8 && p.in_zero == 0 && p.out_zero == 0 && p.relu && !p.res && p.c_out == p.cp_out;
-    const int groups_all = p.nt / 16, g_lo = half ? (groups_all + 1) / 2 : 0,
-              g_hi = half ? groups_all : (groups_all + 1) / 2;
-    int iter = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++iter) {
-      const int acc = iter & 1;
-      const uint32_t acc_phase = (iter >> 1) & 1;
+    const int groups = p.nt / 16;
+    const float lo = p.relu ? 0.0f : static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
+    const int32_t zc = p.out_zero - kMagicBits, rzc = kMagicBits - p.res_zero;
+    const uint32_t zb = static_cast<uint32_t>(p.out_zero) * 0x01010101u;
+    // the line mask byte of this thread's pixel in tile t (0 past the output's width)
+    auto mask_of = [&](int t) -> int {
+      if (t >= p.num_tiles) return 0;
+      const int m = t / p.n_tiles;
+      const int ox = (m % p.m_per_row) * 128 + row;
+      return ox < p.ow ? __ldg(p.mask8 + ((static_cast<long long>(ox) << p.out_shift) >> 3)) : 0;
+    };
+    int iter = half;
+    int t = blockIdx.x + half * gridDim.x;
+    int mk = mask_of(t);
+    for (; t < p.num_tiles; t += 2 * gridDim.x, iter += 2) {
+      const int mk_next = mask_of(t + 2 * gridDim.x);  // in flight during this tile
+      const int acc = iter & (p.n_acc - 1);
+      const uint32_t acc_phase = (iter / p.n_acc) & 1;
       if (!mbar_wait(&tmem_full[acc], acc_phase, p.err, kErrTimeoutTmemFull)) break;
       tc_fence_after();
       const int n = t % p.n_tiles, m = t / p.n_tiles;
       const int oy = m / p.m_per_row, ox = (m % p.m_per_row) * 128 + row;
       const bool inside = ox < p.ow;
-      const bool valid = inside && p.mask8[(static_cast<long long>(ox) << p.out_shift) >> 3] != 0;
+      const bool valid = inside && mk != 0;
+      mk = mk_next;
       uint8_t* dst = p.out + (oy + p.out_ph) * p.out_pitch + static_cast<long long>(ox) * p.cp_out * p.ebytes;
       const uint8_t* res = nullptr;
       if (p.res && valid)
@@ -206,47 +233,47 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       auto store16 = [&](const uint32_t* r, int cb) {
         if (!inside || cb >= cend) return;
         if constexpr (kInt8) {
-          alignas(16) uint8_t o[16];
+          uint4 o;
           if (!valid) {
+            o = make_uint4(zb, zb, zb, zb);
+          } else {
+            int32_t code[16];
+            uint4 rv = make_uint4(0, 0, 0, 0);
+            if (res) rv = *reinterpret_cast<const uint4*>(res + cb);
+            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = static_cast<uint8_t>(p.out_zero);
-          } else if (fast) {
+            for (int k = 0; k < 4; ++k) {
+              const int4 o4 = *reinterpret_cast<const int4*>(s_off + cb + 4 * k);
+              const float4 s4 = *reinterpret_cast<const float4*>(s_scale + cb + 4 * k);
+              const float4 b4 = *reinterpret_cast<const float4*>(s_bias + cb + 4 * k);
+              const int32_t oo[4] = {o4.x, o4.y, o4.z, o4.w};
+              const float ss[4] = {s4.x, s4.y, s4.z, s4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int32_t a = static_cast<int32_t>(r[4 * k + u]);
+                const float f = kFast ? magic_to_float(a + oo[u]) : static_cast<float>(a - oo[u]);
+                float v = __fadd_rn(__fmul_rn(f, ss[u]), bb[u]);
+                if (res) {
+                  const int32_t rb = static_cast<int32_t>((rw[k] >> (8 * u)) & 0xffu);
+                  v = __fadd_rn(v, __fmul_rn(magic_to_float(rb + rzc), p.res_scale));
+                }
+                const float q = fminf(fmaxf(__fmul_rn(v, p.out_inv_scale), lo), hi);
+                code[4 * k + u] = magic_rint_bits(q) + zc;
+              }
+            }
+            if (cb + 16 > p.c_out) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (cb + i >= p.c_out) code[i] = p.out_zero;
+            }
             uint32_t w[4];
 #pragma unroll
-            for (int i4 = 0; i4 < 4; ++i4) {
-              const float4 sc = *reinterpret_cast<const float4*>(s_scale + cb + 4 * i4);
-              const float4 bi = *reinterpret_cast<const float4*>(s_bias + cb + 4 * i4);
-              const float scs[4] = {sc.x, sc.y, sc.z, sc.w}, bis[4] = {bi.x, bi.y, bi.z, bi.w};
-              uint32_t packed = 0;
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float v = __fadd_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[4 * i4 + k])), scs[k]), bis[k]);
-                packed |= cvt_rni_sat_u8(__fmul_rn(v, p.out_inv_scale)) << (8 * k);
-              }
-              w[i4] = packed;
-            }
-            *reinterpret_cast<uint4*>(dst + cb) = make_uint4(w[0], w[1], w[2], w[3]);
-            return;
-          } else {
-            alignas(16) uint8_t rb[16];
-            if (res) *reinterpret_cast<uint4*>(rb) = *reinterpret_cast<const uint4*>(res + cb);
-            const float lo = static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int j = cb + i;
-              const int32_t sum = static_cast<int32_t>(r[i]) - p.in_zero * s_colsum[j];
-              float v = __fmul_rn(static_cast<float>(sum), s_scale[j]);
-              v = __fadd_rn(v, s_bias[j]);
-              if (res) v = __fadd_rn(v, __fmul_rn(static_cast<float>(static_cast<int32_t>(rb[i]) - p.res_zero), p.res_scale));
-              if (p.relu) v = v > 0.0f ? v : 0.0f;
-              float q = __fmul_rn(v, p.out_inv_scale);
-              q = q > lo ? q : lo;
-              q = q < hi ? q : hi;
-              o[i] = static_cast<uint8_t>(__float2int_rn(q) + p.out_zero);
-              if (j >= p.c_out) o[i] = static_cast<uint8_t>(p.out_zero);
-            }
+            for (int k = 0; k < 4; ++k)
+              w[k] = __byte_perm(__byte_perm(code[4 * k], code[4 * k + 1], 0x0040),
+                                 __byte_perm(code[4 * k + 2], code[4 * k + 3], 0x0040), 0x5410);
+            o = make_uint4(w[0], w[1], w[2], w[3]);
           }
-          *reinterpret_cast<uint4*>(dst + cb) = *reinterpret_cast<const uint4*>(o);
+          *reinterpret_cast<uint4*>(dst + cb) = o;
         } else {
           alignas(16) __half o[16];
           if (!valid) {
@@ -271,33 +298,35 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
           *reinterpret_cast<uint4*>(dst + cb * 2 + 16) = *reinterpret_cast<const uint4*>(o + 8);
         }
       };
-      // TMEM read 32 columns at a time, the next load in flight while the current is stored
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * 256);
-      if (g_lo < g_hi) {
-        uint32_t ra[32], rb[32];
-        if (g_lo + 1 < g_hi) tmem_ld32(taddr + g_lo * 16, ra); else tmem_ld16(taddr + g_lo * 16, *reinterpret_cast<uint32_t(*)[16]>(ra));
-        tmem_wait_ld();
-        tmem_pin(ra);
-        for (int g = g_lo; g < g_hi;) {
-          const int w = g + 1 < g_hi ? 2 : 1;
-          const int gn = g + w;
-          if (gn + 1 < g_hi) {
-            tmem_ld32(taddr + gn * 16, rb);
-          } else if (gn < g_hi) {
-            tmem_ld16(taddr + gn * 16, *reinterpret_cast<uint32_t(*)[16]>(rb));
-          }
-          store16(ra, c0 + g * 16);
-          if (w == 2) store16(ra + 16, c0 + g * 16 + 16);
+      // TMEM read 32 columns at a time, the next load in flight while the current is stored; the
+      // accumulator goes back to the MMA as soon as its last load has completed
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc) * acc_cols;
+      uint32_t ra[32], rb[32];
+      if (groups >= 2) tmem_ld32(taddr, ra); else tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(ra));
+      tmem_wait_ld();
+      tmem_pin(ra);
+      for (int g = 0; g < groups;) {
+        const int w = g + 1 < groups ? 2 : 1;
+        const int gn = g + w;
+        if (gn + 1 < groups) {
+          tmem_ld32(taddr + gn * 16, rb);
+        } else if (gn < groups) {
+          tmem_ld16(taddr + gn * 16, *reinterpret_cast<uint32_t(*)[16]>(rb));
+        } else {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+        }
+        store16(ra, c0 + g * 16);
+        if (w == 2) store16(ra + 16, c0 + g * 16 + 16);
+        if (gn < groups) {
           tmem_wait_ld();
           tmem_pin(rb);
 #pragma unroll
           for (int i = 0; i < 32; ++i) ra[i] = rb[i];
-          g = gn;
         }
+        g = gn;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tmem_empty[acc]);
     }
   }
   tc_fence_before();

@@ -175,9 +175,12 @@ struct crec_handle {
   bool profile = false;
   std::vector<cudaEvent_t> ev_pool;  // pairs
   std::vector<int> ev_kind;          // a pair's kernel kind
+  std::vector<int> ev_layer;         // and its layer (the layer count for the collapse)
   size_t ev_used = 0;
   double prof_ms[8] = {0}, prof_ops[8] = {0};
   long long prof_count[8] = {0};
+  std::vector<double> lprof_ms, lprof_ops;  // by layer (and the collapse after the last)
+  std::vector<long long> lprof_count;
   // the last run
   int last_n = 0;
   long long last_cols = 0;
@@ -399,6 +402,27 @@ std::vector<uint8_t> weight_image(const crec_handle* h, const Layer& l, int cp_i
   return img;
 }
 
+// The INT8 epilogue's per-channel offsets (n of them) and whether its conversions may skip the
+// conversion unit: |acc - zero * colsum| <= max(zero, 255 - zero) * sum |w| over a channel's
+// weights; below 2^22 the kernel converts exactly with kMagic.
+int upload_offsets(crec_handle* h, Layer& l, int zero, const std::vector<int32_t>& colsum, int n) {
+  const long long reach = std::max(zero, 255 - zero);
+  const size_t per = l.w8.size() / static_cast<size_t>(l.cout);
+  long long worst = 0;
+  for (int j = 0; j < l.cout; ++j) {
+    long long a = 0;
+    for (size_t k = 0; k < per; ++k) a += std::abs(static_cast<int>(l.w8[j * per + k]));
+    worst = std::max(worst, a * reach);
+  }
+  l.fast = worst < (1LL << 22);
+  std::vector<int32_t> off(n, 0);
+  for (int j = 0; j < n; ++j) {
+    const int32_t zc = zero * colsum[j];
+    off[j] = l.fast ? kMagicBits - zc : zc;
+  }
+  return upload(h, &l.hoff, off);
+}
+
 int setup_layer(crec_handle* h, size_t li) {
   Layer& l = h->l[li];
   if (l.kind == kKindResize) return CREC_OK;
@@ -463,25 +487,7 @@ int setup_layer(crec_handle* h, size_t li) {
     const int ncls = l.chunks * l.nchunk;
     l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + head_tail_bytes(ncls);
     if (l.smem + 1024 > 232448) return set_error(h, CREC_E_MODEL, "the head does not fit in shared memory");
-    if (h->int8) {
-      // |acc - zero * colsum| <= max(zero, 255 - zero) * sum |w| over a class's weights: below 2^22
-      // the kernel converts with kMagic (exact), otherwise with the conversion unit
-      const int z = x.zero;
-      const long long reach = std::max(z, 255 - z);
-      long long worst = 0;
-      for (int j = 0; j < l.cout; ++j) {
-        long long a = 0;
-        for (int k = 0; k < l.cin; ++k) a += std::abs(static_cast<int>(l.w8[static_cast<size_t>(j) * l.cin + k]));
-        worst = std::max(worst, a * reach);
-      }
-      l.fast = worst < (1LL << 22);
-      std::vector<int32_t> off(ncls, 0);
-      for (int j = 0; j < ncls; ++j) {
-        const int32_t zc = z * colsum[j];
-        off[j] = l.fast ? kMagicBits - zc : zc;
-      }
-      if ((rc = upload(h, &l.hoff, off))) return rc;
-    }
+    if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, ncls))) return rc;
   } else {
     l.nt = std::min(256, round16(l.cout));
     l.n_tiles = (y.cp + l.nt - 1) / l.nt;
@@ -489,7 +495,8 @@ int setup_layer(crec_handle* h, size_t li) {
     l.b_bytes = static_cast<uint32_t>(l.nt) * 128;
     l.stage_bytes = l.a_bytes + l.b_bytes;
     l.stages = std::min<int>(8, (200 * 1024) / l.stage_bytes);
-    l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 4) * 8 + 16 + 12 * y.cp + 64;
+    l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 2 * kMaxAcc) * 8 + 16 + 12 * y.cp + 64;
+    if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, y.cp))) return rc;
   }
   const std::vector<uint8_t> img = weight_image(h, l, x.cp, l.nt, l.n_tiles, l.nkb);
   if ((rc = upload(h, &l.wimg, img))) return rc;
@@ -534,7 +541,7 @@ struct ProfScope {
   crec_handle* h;
   int kind;
   cudaEvent_t end = nullptr;
-  ProfScope(crec_handle* hh, int k) : h(hh), kind(k) {
+  ProfScope(crec_handle* hh, int k, int layer) : h(hh), kind(k) {
     ++h->st_launches;
     if (!h->profile) return;
     if (h->ev_used + 2 > h->ev_pool.size()) {
@@ -544,10 +551,12 @@ struct ProfScope {
         h->ev_pool.push_back(e);
       }
       h->ev_kind.resize(h->ev_pool.size() / 2);
+      h->ev_layer.resize(h->ev_pool.size() / 2);
     }
     cudaEventRecord(h->ev_pool[h->ev_used], h->stream);
     end = h->ev_pool[h->ev_used + 1];
     h->ev_kind[h->ev_used / 2] = k;
+    h->ev_layer[h->ev_used / 2] = layer;
     h->ev_used += 2;
   }
   ~ProfScope() {
@@ -561,6 +570,11 @@ void collect_profile(crec_handle* h) {
     if (cudaEventElapsedTime(&ms, h->ev_pool[i], h->ev_pool[i + 1]) == cudaSuccess) {
       h->prof_ms[h->ev_kind[i / 2]] += ms;
       h->prof_count[h->ev_kind[i / 2]] += 1;
+      const size_t li = static_cast<size_t>(h->ev_layer[i / 2]);
+      if (li < h->lprof_ms.size()) {
+        h->lprof_ms[li] += ms;
+        h->lprof_count[li] += 1;
+      }
     }
   }
   h->ev_used = 0;
@@ -578,12 +592,10 @@ void add_run_ops(crec_handle* h, const int* bw, int a, int b) {
     const Value& y = h->v[l.out];
     const double pixels = static_cast<double>(y.h) * static_cast<double>(width >> y.shift);
     const double taps = l.kh * l.kw;
-    if (l.kind == kKindDw) {
-      h->prof_ops[kProfDw] += 2.0 * pixels * taps * l.cout;
-    } else {
-      const int kind = li == 0 ? kProfCrop : li + 1 == h->l.size() ? kProfHead : kProfConv;
-      h->prof_ops[kind] += 2.0 * pixels * taps * l.cin * l.cout;
-    }
+    const int kind = l.kind == kKindDw ? kProfDw : li == 0 ? kProfCrop : li + 1 == h->l.size() ? kProfHead : kProfConv;
+    const double ops = 2.0 * pixels * taps * l.cout * (l.kind == kKindDw ? 1 : l.cin);
+    h->prof_ops[kind] += ops;
+    if (li < h->lprof_ops.size()) h->lprof_ops[li] += ops;
   }
 }
 
@@ -632,7 +644,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     for (int i = 0; i < n; ++i) max_bw = std::max(max_bw, h->run_bw[i]);
     p.max_bw = max_bw;
     const size_t smem = crop_smem_bytes(h, max_bw);
-    ProfScope prof(h, kProfCrop);
+    ProfScope prof(h, kProfCrop, 0);
     // the attribute is the function's, for every handle in the process: set it for this one's size
     if (h->int8) {
       CK(cudaFuncSetAttribute(crop_stem_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
@@ -681,7 +693,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.logits = h->d_logits;
       p.err = h->d_err;
       const int grid = std::min(p.num_tiles, h->sms);
-      ProfScope prof(h, kProfHead);
+      ProfScope prof(h, kProfHead, static_cast<int>(li));
       if (h->int8 && l.fast) {
         CK(cudaFuncSetAttribute(head_ctc_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
         head_ctc_kernel<true, true><<<grid, kHeadThreads, l.smem, s>>>(p);
@@ -725,7 +737,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.out_shift = y.shift;
       const long long total = static_cast<long long>(oh) * ow * (y.cp / 16);
       const int grid = static_cast<int>((total + 255) / 256);
-      ProfScope prof(h, kProfDw);
+      ProfScope prof(h, kProfDw, static_cast<int>(li));
       if (h->int8)
         dw_kernel<true><<<grid, 256, 0, s>>>(p);
       else
@@ -763,12 +775,12 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.cp_out = y.cp;
     p.c_out = l.cout;
     p.ebytes = h->eb;
-    p.colsum = l.colsum;
+    p.off = l.hoff;
     p.scale = l.scale;
     p.bias = l.dbias;
-    p.in_zero = x.zero;
     p.out_zero = y.zero;
     p.relu = l.relu;
+    p.n_acc = conv_accumulators(l.nt);
     p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
     if (l.residual >= 0) {
       const Value& r = h->v[l.residual];
@@ -785,13 +797,16 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.out_shift = y.shift;
     p.err = h->d_err;
     const int grid = std::min(p.num_tiles, h->sms);
-    ProfScope prof(h, kProfConv);
-    if (h->int8) {
-      CK(cudaFuncSetAttribute(conv_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-      conv_gemm_kernel<true><<<grid, kConvThreads, l.smem, s>>>(p);
+    ProfScope prof(h, kProfConv, static_cast<int>(li));
+    if (h->int8 && l.fast) {
+      CK(cudaFuncSetAttribute(conv_gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+      conv_gemm_kernel<true, true><<<grid, kConvThreads, l.smem, s>>>(p);
+    } else if (h->int8) {
+      CK(cudaFuncSetAttribute(conv_gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+      conv_gemm_kernel<true, false><<<grid, kConvThreads, l.smem, s>>>(p);
     } else {
-      CK(cudaFuncSetAttribute(conv_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-      conv_gemm_kernel<false><<<grid, kConvThreads, l.smem, s>>>(p);
+      CK(cudaFuncSetAttribute(conv_gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+      conv_gemm_kernel<false, false><<<grid, kConvThreads, l.smem, s>>>(p);
     }
     CK(cudaGetLastError());
   }
@@ -806,7 +821,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
   c.frames = h->d_frames;
   c.probs = h->d_probs;
   {
-    ProfScope prof(h, kProfCollapse);
+    ProfScope prof(h, kProfCollapse, static_cast<int>(h->l.size()));
     collapse_kernel<<<(n + 127) / 128, 128, 0, s>>>(c);
   }
   CK(cudaGetLastError());
@@ -967,7 +982,7 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
     h->run_bw = bw + r.a;
     if ((rc = launch_run(h, m, cols, h->d_crops != nullptr))) return rc;
     {  // this run's characters packed after the previous runs'
-      ProfScope prof(h, kProfCollapse);
+      ProfScope prof(h, kProfCollapse, static_cast<int>(h->l.size()));
       scan_counts_kernel<<<1, 1024, 0, s>>>(h->d_count, m, h->dp_counts + r.a, h->dp_offsets + r.a, h->d_total);
       pack_kernel<<<(m * 32 + 255) / 256, 256, 0, s>>>(h->d_ids, h->d_frames, h->d_probs, h->d_frame0,
                                                       h->dp_counts + r.a, h->dp_offsets + r.a, m, h->dp_ids,
@@ -1497,11 +1512,36 @@ int crec_profile(crec_handle* h, int enable, crec_profile_entry* out, int capaci
   }
   if (enable >= 0) {  // (re)start: clear the totals
     h->profile = enable != 0;
+    h->lprof_ms.assign(h->l.size() + 1, 0.0);
+    h->lprof_ops.assign(h->l.size() + 1, 0.0);
+    h->lprof_count.assign(h->l.size() + 1, 0);
     for (int k = 0; k < 8; ++k) {
       h->prof_ms[k] = 0;
       h->prof_ops[k] = 0;
       h->prof_count[k] = 0;
     }
+  }
+  return n;
+}
+
+int crec_profile_layers(crec_handle* h, crec_profile_entry* out, int capacity) {
+  if (!h || (!out && capacity > 0)) return CREC_E_INVALID;
+  const size_t nl = h->l.size();
+  int n = 0;
+  for (size_t li = 0; li <= nl && n < capacity; ++li, ++n) {
+    const char* name = "collapse";
+    if (li < nl) {
+      const Layer& l = h->l[li];
+      name = li == 0                   ? "crop_stem"
+             : li + 1 == nl            ? "head_ctc_tcgen05"
+             : l.kind == kKindDw       ? "depthwise"
+             : l.kind == kKindResize   ? "resize (read in place)"
+                                       : "conv_gemm_tcgen05";
+    }
+    out[n].kernel = name;
+    out[n].launches = li < h->lprof_count.size() ? h->lprof_count[li] : 0;
+    out[n].ms = li < h->lprof_ms.size() ? h->lprof_ms[li] : 0.0;
+    out[n].ops = li < h->lprof_ops.size() ? h->lprof_ops[li] : 0.0;
   }
   return n;
 }

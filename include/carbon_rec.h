@@ -187,6 +187,12 @@ typedef struct crec_profile_entry {
 } crec_profile_entry;
 CREC_API int crec_profile(crec_handle* h, int enable, crec_profile_entry* out, int capacity);
 
+/* The profile by layer: entry i for the model's layer i (0 the crop and stem, the last the head
+ * with CTC; a Resize read in place has no launches), then one for the collapse; the same totals
+ * crec_profile gathers, cleared and enabled by it.  Returns the entries written (at most
+ * capacity), or a negative status.  No counterpart in the reference (a diagnostic). */
+CREC_API int crec_profile_layers(crec_handle* h, crec_profile_entry* out, int capacity);
+
 /* The CUDA stream (a cudaStream_t) the handle's work runs on, for device-side timing. */
 CREC_API void* crec_stream(crec_handle* h);
 
