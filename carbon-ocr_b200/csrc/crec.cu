@@ -63,7 +63,9 @@ struct Layer {
   float* dbias = nullptr;
   int8_t* dw8 = nullptr;  // depthwise [taps][cp], stem [cout][taps]
   float* dwf = nullptr;
-  int32_t* hoff = nullptr;  // the INT8 head's per-class offsets (HeadParams::off)
+  int32_t* hoff = nullptr;  // the INT8 epilogue's per-channel offsets (HeadParams::off, ConvParams::off, DwParams::off)
+  uint32_t* dwt = nullptr;  // the INT8 row depthwise's tap-transposed weights (DwParams::wt)
+  uint32_t* dwc = nullptr;  // and its per-channel constants (DwParams::dwc)
   bool fast = false;        // its sums fit the exact conversions without the conversion unit
   int nkb = 0, last_steps = 0, nt = 0, n_tiles = 0, stages = 0, nchunk = 0, chunks = 0;
   uint32_t stage_bytes = 0, a_bytes = 0, b_bytes = 0, smem = 0;
@@ -464,6 +466,18 @@ int setup_layer(crec_handle* h, size_t li) {
       for (int c = 0; c < l.cout; ++c)
         for (int t = 0; t < taps; ++t) w[static_cast<size_t>(t) * cp + c] = l.w8[static_cast<size_t>(c) * taps + t];
       if ((rc = upload(h, &l.dw8, w))) return rc;
+      if (l.kh == 1 && l.kw <= 12 && x.cp == cp) {  // the row kernel: channel c's taps 4j .. 4j+3 in slot j
+        std::vector<uint32_t> wt(3 * static_cast<size_t>(cp), 0u), dc(3 * static_cast<size_t>(cp), 0u);
+        for (int c = 0; c < cp; ++c) {
+          for (int t = 0; t < l.kw && c < l.cout; ++t)
+            wt[dw_row_index(t / 4, c, cp)] |= static_cast<uint32_t>(static_cast<uint8_t>(l.w8[static_cast<size_t>(c) * taps + t])) << (8 * (t % 4));
+          const int32_t off = kMagicBits - x.zero * colsum[c];
+          std::memcpy(&dc[dw_row_index(0, c, cp)], &off, 4);
+          std::memcpy(&dc[dw_row_index(1, c, cp)], &scale[c], 4);
+          std::memcpy(&dc[dw_row_index(2, c, cp)], &bias[c], 4);
+        }
+        if ((rc = upload(h, &l.dwt, wt)) || (rc = upload(h, &l.dwc, dc))) return rc;
+      }
     } else {
       std::vector<float> w(static_cast<size_t>(taps) * cp, 0.0f);
       for (int c = 0; c < l.cout; ++c)
@@ -735,13 +749,23 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.out_pitch = y.pitch;
       p.mask8 = h->d_mask;
       p.out_shift = y.shift;
-      const long long total = static_cast<long long>(oh) * ow * (y.cp / 16);
-      const int grid = static_cast<int>((total + 255) / 256);
+      p.wt = l.dwt;
+      p.dwc = l.dwc;
       ProfScope prof(h, kProfDw, static_cast<int>(li));
-      if (h->int8)
-        dw_kernel<true><<<grid, 256, 0, s>>>(p);
-      else
-        dw_kernel<false><<<grid, 256, 0, s>>>(p);
+      if (h->int8 && l.dwt) {
+        const long long tiles = static_cast<long long>(oh) * ((ow + kDwTile - 1) / kDwTile);
+        const int ncols = dw_row_cols(l.kw, x.extra);
+        const int smem = ((ncols * y.cp + 15) & ~15) + 24 * y.cp;
+        CK(cudaFuncSetAttribute(dw_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        dw_row_kernel<<<static_cast<int>(tiles), 256, smem, s>>>(p);
+      } else {
+        const long long total = static_cast<long long>(oh) * ow * (y.cp / 16);
+        const int grid = static_cast<int>((total + 255) / 256);
+        if (h->int8)
+          dw_kernel<true><<<grid, 256, 0, s>>>(p);
+        else
+          dw_kernel<false><<<grid, 256, 0, s>>>(p);
+      }
       CK(cudaGetLastError());
       continue;
     }
@@ -1032,6 +1056,8 @@ void free_all(crec_handle* h) {
     cudaFree(l.dw8);
     cudaFree(l.dwf);
     cudaFree(l.hoff);
+    cudaFree(l.dwt);
+    cudaFree(l.dwc);
   }
   cudaFree(h->in_table);
   cudaFree(h->head_table);

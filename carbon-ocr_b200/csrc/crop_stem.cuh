@@ -120,6 +120,13 @@ __device__ __forceinline__ int32_t dp4a_us(uint32_t a, uint32_t b, int32_t c) {
   return d;
 }
 
+// Four unsigned bytes of a times four unsigned bytes of b, summed into c.
+__device__ __forceinline__ uint32_t dp4a_uu(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint8_t clip8d(int32_t v) {
   v >>= 22;
   return static_cast<uint8_t>(v < 0 ? 0 : v > 255 ? 255 : v);
@@ -266,6 +273,21 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
   bool flip = false;
   uint8_t ground = 0;
   if (!p.crops_in) {
+    // the source region into L2 first (every 128-byte line of the rows and columns the filters'
+    // windows can reach): DRAM streams it in while the coefficients are computed
+    {
+      const double vsup = (L.y1 - L.y0) / H < 1.0 ? 1.0 : (L.y1 - L.y0) / H;
+      const double hsup = (L.x1 - L.x0) / cw < 1.0 ? 1.0 : (L.x1 - L.x0) / cw;
+      const int ylo = max(0, static_cast<int>(floor(L.y0 - vsup)) - 2), yhi = min(P.height, static_cast<int>(ceil(L.y1 + vsup)) + 2);
+      const int xlo = max(0, static_cast<int>(floor(L.x0 - hsup)) - 2), xhi = min(P.width, static_cast<int>(ceil(L.x1 + hsup)) + 2);
+      if (yhi > ylo && xhi > xlo) {
+        const int per_row = (xhi - xlo + 127) / 128 + 1;
+        for (int i = tid; i < (yhi - ylo) * per_row; i += nthr) {
+          const int y = ylo + i / per_row, x = min(xhi - 1, xlo + (i % per_row) * 128);
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(P.data + static_cast<long long>(y) * P.stride + x));
+        }
+      }
+    }
     // this line's tap stride (PIL's ksize) and strip width, from a bound on the source rows the
     // vertical windows span: each window lies within [y0 - support - 1, y1 + support + 1]
     const double hscale = (L.x1 - L.x0) / cw;
@@ -308,16 +330,86 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
       const int groups = max(1, nthr / sc);
       const int rg = tid / sc, xx = tid - rg * sc;
       if (rg < groups) {
-        // horizontal pass: every source row the vertical windows read
+        // horizontal pass: every source row the vertical windows read.  Up to 16 taps the weights
+        // (non-negative, at most 2^22) split into three byte planes, and a row's taps are summed
+        // four at a time with dp4a on the source words realigned by a byte permute: the same
+        // integer sum.  Reads stay inside the row: from 3 bytes before xmin to 17 after.
         const int32_t* c = hk + xx * (T + 2);
         const int xmin = c[0], n = c[1];
         const bool inside = xmin >= 0 && xmin + n <= P.width;
-        for (int r = rg; r < rows; r += groups) {
+        const bool planes = n <= 16 && xmin >= 3 && xmin + 17 <= P.width;
+        const int nw = (n + 3) >> 2;  // words of taps
+        uint32_t k0[4] = {0, 0, 0, 0}, k1[4] = {0, 0, 0, 0}, k2[4] = {0, 0, 0, 0};
+        int32_t paper = 0;  // a row off the page: 255 * the weights' sum
+        for (int t = 0; t < n; ++t) paper += 255 * c[2 + t];
+        if (planes) {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const uint32_t k = t < n ? static_cast<uint32_t>(c[2 + t]) : 0u;
+            k0[t >> 2] |= (k & 0xffu) << (8 * (t & 3));
+            k1[t >> 2] |= ((k >> 8) & 0xffu) << (8 * (t & 3));
+            k2[t >> 2] |= ((k >> 16) & 0xffu) << (8 * (t & 3));
+          }
+        }
+        // rows RU at a time in the common case (up to 12 taps, all those rows on the page): their
+        // loads are in flight together
+        int r = rg;
+        if (planes && nw <= 3) {
+          constexpr int RU = 3;
+          for (; r + (RU - 1) * groups < rows; r += RU * groups) {
+            const int y0 = top + r;
+            if (y0 < 0 || y0 + (RU - 1) * groups >= P.height) break;
+            uint32_t w[RU][4];
+            uint32_t sel[RU];
+#pragma unroll
+            for (int q = 0; q < RU; ++q) {
+              const uintptr_t a = reinterpret_cast<uintptr_t>(P.data + static_cast<long long>(y0 + q * groups) * P.stride + xmin);
+              const uint32_t* wp = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+              sel[q] = 0x3210u + static_cast<uint32_t>(a & 3) * 0x1111u;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) w[q][j] = j <= nw ? __ldg(wp + j) : 0u;
+            }
+#pragma unroll
+            for (int q = 0; q < RU; ++q) {
+              uint32_t s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+              for (int j = 0; j < 3; ++j) {
+                if (j < nw) {
+                  const uint32_t x = __byte_perm(w[q][j], w[q][j + 1], sel[q]);
+                  s0 = dp4a_uu(x, k0[j], s0);
+                  s1 = dp4a_uu(x, k1[j], s1);
+                  s2 = dp4a_uu(x, k2[j], s2);
+                }
+              }
+              tmp[(r + q * groups) * strip + xx] = clip8d((1 << 21) + static_cast<int32_t>(s0 + (s1 << 8) + (s2 << 16)));
+            }
+          }
+        }
+        for (; r < rows; r += groups) {
           const int y = top + r;
           int32_t ss = 1 << 21;
           if (y >= 0 && y < P.height) {
             const uint8_t* src = P.data + static_cast<long long>(y) * P.stride + xmin;
-            if (inside) {
+            if (planes) {
+              const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+              const uint32_t* wp = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+              const uint32_t sel = 0x3210u + static_cast<uint32_t>(a & 3) * 0x1111u;
+              uint32_t w[5];
+              w[0] = __ldg(wp);
+#pragma unroll
+              for (int j = 1; j < 5; ++j) w[j] = j <= nw ? __ldg(wp + j) : 0u;
+              uint32_t s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                if (j < nw) {
+                  const uint32_t x = __byte_perm(w[j], w[j + 1], sel);
+                  s0 = dp4a_uu(x, k0[j], s0);
+                  s1 = dp4a_uu(x, k1[j], s1);
+                  s2 = dp4a_uu(x, k2[j], s2);
+                }
+              }
+              ss += static_cast<int32_t>(s0 + (s1 << 8) + (s2 << 16));
+            } else if (inside) {
               for (int t = 0; t < n; ++t) ss += static_cast<int32_t>(__ldg(src + t)) * c[2 + t];
             } else {
               for (int t = 0; t < n; ++t) {
@@ -326,7 +418,7 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
               }
             }
           } else {
-            for (int t = 0; t < n; ++t) ss += 255 * c[2 + t];
+            ss += paper;
           }
           tmp[r * strip + xx] = clip8d(ss);
         }

@@ -7,6 +7,7 @@
 
 #include <cstdint>
 
+#include "crop_stem.cuh"  // dp4a_us
 #include "sm100.cuh"
 
 namespace crec {
@@ -36,7 +37,18 @@ struct DwParams {
   long long out_pitch;
   const uint8_t* mask8;
   int out_shift;
+  // the row kernel (INT8, one kernel row, kw <= 12); channel c = 16 g + 4 q + u of G = cp / 16
+  // groups sits at ((slot * 4 + q) * G + g) * 4 + u, so that the 16 groups of a warp's
+  // threads read 16 consecutive 16-byte words
+  const uint32_t* wt;   // [3 slots]: channel c's taps 4j .. 4j+3 in slot j (zeros past kw)
+  const uint32_t* dwc;  // [3 slots]: kMagicBits - in_zero * (the channel's weight sum), scale, bias (bits)
 };
+
+// The row kernel's interleaved index of channel c (of cp) in slot `slot`.
+__host__ __device__ inline int dw_row_index(int slot, int c, int cp) {
+  const int g = c >> 4, q = (c >> 2) & 3, u = c & 3;
+  return ((slot * 4 + q) * (cp >> 4) + g) * 4 + u;
+}
 
 template <bool kInt8>
 __global__ void __launch_bounds__(256) dw_kernel(const __grid_constant__ DwParams p) {
@@ -104,6 +116,112 @@ __global__ void __launch_bounds__(256) dw_kernel(const __grid_constant__ DwParam
     }
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(o);
     *reinterpret_cast<uint4*>(dst + 16) = *reinterpret_cast<const uint4*>(o + 8);
+  }
+}
+
+// The INT8 depthwise convolution of one kernel row (1 x kw, kw <= 12), a CTA a tile of
+// kDwTile output pixels of one row and all channels.  The input columns the tile reads are
+// staged in shared memory with 16-byte loads; a thread takes a (pixel, 16 channels) item: the
+// taps' bytes, four taps by four channels at a time, are transposed with byte permutes so that
+// each channel's four taps are one word, and dp4a sums them against the channel's weights
+// (stored tap-transposed).  The sum is the reference's integer sum of (a - zero) * w (through
+// the weights' sum), |sum| <= 12 * 255 * 128 < 2^22, so the output stage converts exactly with
+// kMagic.
+constexpr int kDwTile = 64;
+
+__host__ __device__ inline int dw_row_cols(int kw, int in_shift) { return ((kDwTile - 1 + kw - 1) >> in_shift) + 2; }
+
+__global__ void __launch_bounds__(256) dw_row_kernel(const __grid_constant__ DwParams p) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int cp = p.cp, G = cp >> 4;
+  const int tiles_per_row = (p.ow + kDwTile - 1) / kDwTile;
+  const int oy = blockIdx.x / tiles_per_row, ox0 = (blockIdx.x - oy * tiles_per_row) * kDwTile;
+  const int sh = p.in_shift;
+  const int pc0 = (ox0 - p.pl) >> sh;  // the first input column the tile reads (arithmetic shift: floor)
+  const int ncols = dw_row_cols(p.kw, sh);
+  uint8_t* sin = sm;  // [ncols][cp]
+  uint32_t* swt = reinterpret_cast<uint32_t*>(sm + ((ncols * cp + 15) & ~15));  // [3 slots], interleaved
+  uint32_t* sc = swt + 3 * cp;                                                  // [3 slots], interleaved
+  {
+    const uint8_t* src = p.in + static_cast<long long>(oy - p.pt + p.in_ph) * p.in_pitch + static_cast<long long>(pc0) * cp;
+    const int n16 = ncols * cp / 16;
+    for (int i = threadIdx.x; i < n16; i += blockDim.x)
+      reinterpret_cast<uint4*>(sin)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+    for (int i = threadIdx.x; i < 3 * cp; i += blockDim.x) {
+      swt[i] = p.wt[i];
+      sc[i] = p.dwc[i];
+    }
+  }
+  __syncthreads();
+  const float lo = p.relu ? 0.0f : static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
+  const int32_t zc = p.out_zero - kMagicBits;
+  const uint32_t zb = static_cast<uint32_t>(p.out_zero) * 0x01010101u;
+  for (int it = threadIdx.x; it < kDwTile * G; it += blockDim.x) {
+    const int px = it / G, g = it - px * G;
+    const int ox = ox0 + px;
+    if (ox >= p.ow) continue;
+    uint8_t* dst = p.out + static_cast<long long>(oy + p.out_ph) * p.out_pitch + static_cast<long long>(ox) * cp + g * 16;
+    if (p.mask8[(static_cast<long long>(ox) << p.out_shift) >> 3] == 0) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(zb, zb, zb, zb);
+      continue;
+    }
+    const int c0 = g * 16;
+    const uint4* sc4 = reinterpret_cast<const uint4*>(sc);  // slot s, quad k: sc4[(s * 4 + k) * G + g]
+    int32_t acc[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int4 o4 = *reinterpret_cast<const int4*>(sc4 + k * G + g);
+      acc[4 * k] = o4.x;
+      acc[4 * k + 1] = o4.y;
+      acc[4 * k + 2] = o4.z;
+      acc[4 * k + 3] = o4.w;
+    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      if (4 * j >= p.kw) break;
+      uint32_t a[4][4];
+#pragma unroll
+      for (int tt = 0; tt < 4; ++tt) {
+        const int t = 4 * j + tt;
+        if (t < p.kw) {
+          const int col = ((ox - p.pl + t) >> sh) - pc0;
+          const uint4 v = *reinterpret_cast<const uint4*>(sin + col * cp + c0);
+          a[tt][0] = v.x;
+          a[tt][1] = v.y;
+          a[tt][2] = v.z;
+          a[tt][3] = v.w;
+        } else {
+          a[tt][0] = a[tt][1] = a[tt][2] = a[tt][3] = 0u;
+        }
+      }
+      const uint4* w4 = reinterpret_cast<const uint4*>(swt);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 wq = w4[(j * 4 + q) * G + g];
+        const uint32_t x01l = __byte_perm(a[0][q], a[1][q], 0x5140), x01h = __byte_perm(a[0][q], a[1][q], 0x7362);
+        const uint32_t x23l = __byte_perm(a[2][q], a[3][q], 0x5140), x23h = __byte_perm(a[2][q], a[3][q], 0x7362);
+        acc[4 * q] = dp4a_us(__byte_perm(x01l, x23l, 0x5410), wq.x, acc[4 * q]);
+        acc[4 * q + 1] = dp4a_us(__byte_perm(x01l, x23l, 0x7632), wq.y, acc[4 * q + 1]);
+        acc[4 * q + 2] = dp4a_us(__byte_perm(x01h, x23h, 0x5410), wq.z, acc[4 * q + 2]);
+        acc[4 * q + 3] = dp4a_us(__byte_perm(x01h, x23h, 0x7632), wq.w, acc[4 * q + 3]);
+      }
+    }
+    uint32_t wv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4 s4 = *reinterpret_cast<const float4*>(sc4 + (4 + k) * G + g);
+      const float4 b4 = *reinterpret_cast<const float4*>(sc4 + (8 + k) * G + g);
+      const float ss[4] = {s4.x, s4.y, s4.z, s4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
+      int32_t code[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float v = __fadd_rn(__fmul_rn(magic_to_float(acc[4 * k + u]), ss[u]), bb[u]);
+        const float q = fminf(fmaxf(__fmul_rn(v, p.out_inv_scale), lo), hi);
+        code[u] = c0 + 4 * k + u < p.c ? magic_rint_bits(q) + zc : p.out_zero;
+      }
+      wv[k] = __byte_perm(__byte_perm(code[0], code[1], 0x0040), __byte_perm(code[2], code[3], 0x0040), 0x5410);
+    }
+    *reinterpret_cast<uint4*>(dst) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
   }
 }
 
