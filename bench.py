@@ -74,6 +74,11 @@ def workload(rank: int, world: int, pages_total: int = PAGES_TOTAL):
     return pages, boxes, page_of, allb, bws
 
 
+# measured: dram__bytes_read.sum + dram__bytes_write.sum of all conv_gemm launches of one
+# 524,288-column run / 11, x 4 (a 2,097,152-column run)
+CONV_TRAFFIC_PER_LAUNCH = 646.2e6 / 11 * 4
+
+
 class ClockSampler:
     """nvidia-smi samples of the SM clock and throttle reasons while the timed region runs."""
 
@@ -334,7 +339,11 @@ def main() -> int:
                          "frac": achieved / peak_tops if peak_tops else None,
                          "peak_source": f"2 x bf16_tflops {tag}" if "int8_tops" not in peaks else f"int8 {tag}",
                          "avg_launch_ms": ms / launches if launches else None, "ops_per_launch": ops / launches if launches else None,
-                         "traffic": None},
+                         # DRAM bytes a conv launch: the 11 launches of a 524,288-column run under ncu
+                         # (profiles/conv_gemm_tcgen05_int8_config5_128pages.md: 646 MB), scaled by
+                         # columns to this run size; a lower bound (less stays in L2 at full size)
+                         "traffic": CONV_TRAFFIC_PER_LAUNCH * args.max_columns / (1 << 21),
+                         "traffic_unit": "bytes/launch"},
             "kernels": {k: {"launches": v[0], "ms": v[1], "ops": v[2]} for k, v in (prof or {}).items()},
             "layers": [{"layer": i, "kernel": k, "launches": n, "ms": round(t, 3),
                         "tops": round(o / t / 1e9, 1) if t > 0 else None}
