@@ -214,7 +214,7 @@ __device__ __forceinline__ int hist_nth(const int32_t* hist, int n, bool flipped
 }
 
 template <bool kInt8>
-__global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_constant__ CropParams p) {
+__global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid_constant__ CropParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int line = blockIdx.x;
   const LineDesc L = p.lines[line];
@@ -351,9 +351,44 @@ __global__ void __launch_bounds__(kCropThreads) crop_stem_kernel(const __grid_co
             k2[t >> 2] |= ((k >> 16) & 0xffu) << (8 * (t & 3));
           }
         }
-        // rows RU at a time in the common case (up to 12 taps, all those rows on the page): their
-        // loads are in flight together
+        // rows several at a time in the common case (all of them on the page), their loads in
+        // flight together: 8 rows for up to 8 taps, 3 rows for up to 12
         int r = rg;
+        if (planes && nw <= 2 && (P.stride & 3) == 0) {
+          // word-aligned rows: every row's first tap word has the same byte offset
+          constexpr int RU = 8;
+          const uintptr_t a0 = reinterpret_cast<uintptr_t>(P.data + xmin);
+          const uint32_t sel = 0x3210u + static_cast<uint32_t>(a0 & 3) * 0x1111u;
+          const uint32_t* base = reinterpret_cast<const uint32_t*>(a0 & ~uintptr_t(3));
+          const long long wstride = P.stride >> 2;  // words a row
+          for (; r + (RU - 1) * groups < rows; r += RU * groups) {
+            const int y0 = top + r;
+            if (y0 < 0 || y0 + (RU - 1) * groups >= P.height) break;
+            uint32_t w[RU][3];
+            const uint32_t* wp = base + static_cast<long long>(y0) * wstride;
+            const long long step = static_cast<long long>(groups) * wstride;
+#pragma unroll
+            for (int q = 0; q < RU; ++q, wp += step) {
+              w[q][0] = __ldg(wp);
+              w[q][1] = __ldg(wp + 1);
+              w[q][2] = nw == 2 ? __ldg(wp + 2) : 0u;
+            }
+#pragma unroll
+            for (int q = 0; q < RU; ++q) {
+              uint32_t s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                if (j < nw) {
+                  const uint32_t x = __byte_perm(w[q][j], w[q][j + 1], sel);
+                  s0 = dp4a_uu(x, k0[j], s0);
+                  s1 = dp4a_uu(x, k1[j], s1);
+                  s2 = dp4a_uu(x, k2[j], s2);
+                }
+              }
+              tmp[(r + q * groups) * strip + xx] = clip8d((1 << 21) + static_cast<int32_t>(s0 + (s1 << 8) + (s2 << 16)));
+            }
+          }
+        }
         if (planes && nw <= 3) {
           constexpr int RU = 3;
           for (; r + (RU - 1) * groups < rows; r += RU * groups) {
