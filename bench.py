@@ -74,6 +74,17 @@ def workload(rank: int, world: int, pages_total: int = PAGES_TOTAL):
     return pages, boxes, page_of, allb, bws
 
 
+def reduce_max(v: float, world: int, device: str) -> float:
+    """The job's time: the maximum of every rank's (a collective; every rank calls it)."""
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 # measured: dram__bytes_read.sum + dram__bytes_write.sum of all conv_gemm launches of one
 # 524,288-column run / 11, x 4 (a 2,097,152-column run)
 CONV_TRAFFIC_PER_LAUNCH = 646.2e6 / 11 * 4
@@ -241,11 +252,7 @@ def main() -> int:
             dist.barrier()
 
     def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_max(v, world, "cuda")
 
     def timed(dev, fn, steps):
         stream = torch.cuda.ExternalStream(dev.stream)
