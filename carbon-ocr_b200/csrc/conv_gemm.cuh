@@ -42,10 +42,18 @@
 
 namespace crec {
 
+constexpr int kMaxKRows = 12;  // input rows a tile's K runs over
+
+// Row stacking: a tile may compute q_rows output rows at once, N = q_rows x cq (each output
+// row's cq channels one after the other), so that a narrow layer's MMAs still fill N (a
+// tcgen05.mma of M = 128, K = 32 bytes costs about the same at any N up to 256).  K then runs
+// over the (q_rows - 1) * sh + kh input rows the tile's output rows read; the weight image holds
+// zeros where an output row does not read an input row.
 struct ConvParams {
-  CUtensorMap tmap[3];  // one per kernel row (kh <= 3)
+  CUtensorMap tmap[kMaxKRows];  // one per input row of a tile (3rd coordinate: the tile's row group)
   const uint8_t* wimg;  // [n tile][ky][kb][nt rows][128 bytes], each block in the 128-byte swizzle
-  int kh, nkb, last_steps;  // K blocks of 128 bytes per kernel row; 32-byte K steps in each row's last block
+  int krows, nkb, last_steps;  // input rows; K blocks of 128 bytes a row; 32-byte K steps in a row's last block
+  int q_rows, cq;              // output rows a tile; its channels an output row (cq = nt when q_rows is 1)
   int nt, n_tiles;          // output channels a tile (multiple of 16, <= 256), tiles across the channels
   int oh, ow, m_per_row, num_tiles;
   int stages;
@@ -112,13 +120,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   if (warp == 0 && lane == 0) {
-    for (int k = 0; k < p.kh; ++k) prefetch_tmap(&p.tmap[k]);
+    for (int k = 0; k < p.krows; ++k) prefetch_tmap(&p.tmap[k]);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int ksteps_per_tile = p.kh * p.nkb;
+  const int ksteps_per_tile = p.krows * p.nkb;
   const uint32_t acc_cols = kTmemCols / static_cast<uint32_t>(p.n_acc);
 
   if (warp == 0) {
@@ -130,7 +138,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         const int n = t % p.n_tiles, m = t / p.n_tiles;
         const int oy = m / p.m_per_row, ox0 = (m % p.m_per_row) * 128;
-        for (int ky = 0; ky < p.kh && ok; ++ky) {
+        for (int ky = 0; ky < p.krows && ok; ++ky) {
           for (int kb = 0; kb < p.nkb; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutEmpty)) {
               ok = false;
@@ -140,7 +148,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
             uint8_t* b = a + p.a_bytes;
             mbar_expect_tx(&full[stage], p.a_bytes + p.b_bytes);
             tma_load_3d(a, &p.tmap[ky], kb * 128, ox0, oy, &full[stage]);
-            const uint8_t* w = p.wimg + (static_cast<size_t>((n * p.kh + ky) * p.nkb + kb)) * p.b_bytes;
+            const uint8_t* w = p.wimg + (static_cast<size_t>((n * p.krows + ky) * p.nkb + kb)) * p.b_bytes;
             bulk_load(b, w, p.b_bytes, &full[stage]);
             if (++stage == p.stages) {
               stage = 0;
@@ -219,19 +227,21 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       if (!mbar_wait(&tmem_full[acc], acc_phase, p.err, kErrTimeoutTmemFull)) break;
       tc_fence_after();
       const int n = t % p.n_tiles, m = t / p.n_tiles;
-      const int oy = m / p.m_per_row, ox = (m % p.m_per_row) * 128 + row;
+      const int oy = (m / p.m_per_row) * p.q_rows, ox = (m % p.m_per_row) * 128 + row;
       const bool inside = ox < p.ow;
       const bool valid = inside && mk != 0;
       mk = mk_next;
-      uint8_t* dst = p.out + (oy + p.out_ph) * p.out_pitch + static_cast<long long>(ox) * p.cp_out * p.ebytes;
+      uint8_t* dst0 = p.out + (oy + p.out_ph) * p.out_pitch + static_cast<long long>(ox) * p.cp_out * p.ebytes;
       const uint8_t* res = nullptr;
       if (p.res && valid)
         res = p.res + (oy + p.res_ph) * p.res_pitch + static_cast<long long>(ox >> p.res_shift) * p.res_cp * p.ebytes;
       const int c0 = n * p.nt;
-      const int cend = min(c0 + p.nt, p.cp_out);
-      // 16 channels from r[0..16) to the output at channel cb
-      auto store16 = [&](const uint32_t* r, int cb) {
-        if (!inside || cb >= cend) return;
+      // 16 of the tile's columns from r[0..16), starting at tile column tc: output row oy + q, channel cb
+      auto store16 = [&](const uint32_t* r, int tc) {
+        const int q = p.q_rows > 1 ? tc / p.cq : 0;
+        const int cb = c0 + tc - q * p.cq;
+        if (!inside || cb >= p.cp_out || oy + q >= p.oh) return;
+        uint8_t* dst = dst0 + q * p.out_pitch;
         if constexpr (kInt8) {
           uint4 o;
           if (!valid) {
@@ -317,8 +327,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
           __syncwarp();
           if (lane == 0) mbar_arrive(&tmem_empty[acc]);
         }
-        store16(ra, c0 + g * 16);
-        if (w == 2) store16(ra + 16, c0 + g * 16 + 16);
+        store16(ra, g * 16);
+        if (w == 2) store16(ra + 16, g * 16 + 16);
         if (gn < groups) {
           tmem_wait_ld();
           tmem_pin(rb);

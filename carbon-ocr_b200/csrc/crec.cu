@@ -68,6 +68,7 @@ struct Layer {
   uint32_t* dwc = nullptr;  // and its per-channel constants (DwParams::dwc)
   bool fast = false;        // its sums fit the exact conversions without the conversion unit
   int nkb = 0, last_steps = 0, nt = 0, n_tiles = 0, stages = 0, nchunk = 0, chunks = 0;
+  int krows = 0, q_rows = 1, cq = 0;  // dense convs: input rows a tile reads, output rows it stacks, channels a row
   uint32_t stage_bytes = 0, a_bytes = 0, b_bytes = 0, smem = 0;
 };
 
@@ -376,14 +377,18 @@ inline size_t swz(int j, int b) { return static_cast<size_t>(j) * 128 + (((b >> 
 // [n tile][ky][kb][nt rows][128 bytes]; byte `off` of kernel row ky's window is (kx, channel, byte).
 std::vector<uint8_t> weight_image(const crec_handle* h, const Layer& l, int cp_in, int nt, int n_tiles, int nkb) {
   const int eb = h->eb, taps = l.kh * l.kw, window = l.kw * cp_in * eb;
-  std::vector<uint8_t> img(static_cast<size_t>(n_tiles) * l.kh * nkb * nt * 128, 0);
+  // blocks [n tile][input row i][kb]; tile column j is output row q = j / cq of the tile's
+  // stacked rows, channel co; it reads input row i through kernel row i - q * sh (zeros where
+  // that is outside the kernel)
+  std::vector<uint8_t> img(static_cast<size_t>(n_tiles) * l.krows * nkb * nt * 128, 0);
   for (int n = 0; n < n_tiles; ++n)
-    for (int ky = 0; ky < l.kh; ++ky)
+    for (int i = 0; i < l.krows; ++i)
       for (int kb = 0; kb < nkb; ++kb) {
-        uint8_t* blk = img.data() + (static_cast<size_t>((n * l.kh + ky) * nkb + kb)) * nt * 128;
+        uint8_t* blk = img.data() + (static_cast<size_t>((n * l.krows + i) * nkb + kb)) * nt * 128;
         for (int j = 0; j < nt; ++j) {
-          const int co = n * nt + j;
-          if (co >= l.cout) continue;
+          const int q = l.q_rows > 1 ? j / l.cq : 0;
+          const int co = n * nt + j - q * l.cq, ky = i - q * l.sh;
+          if (co >= l.cout || ky < 0 || ky >= l.kh) continue;
           for (int b = 0; b < 128; ++b) {
             const int off = kb * 128 + b;
             if (off >= window) break;
@@ -491,9 +496,11 @@ int setup_layer(crec_handle* h, size_t li) {
   l.last_steps = (window - (l.nkb - 1) * 128 + 31) / 32;
   if (li + 1 == h->l.size()) {  // the head
     if (l.nkb * 16384 > 65536) return set_error(h, CREC_E_MODEL, "a head reading more than 512 bytes a frame");
+    l.krows = 1;
     l.nchunk = std::min(kHeadChunk, round16(l.cout));
     l.chunks = (l.cout + l.nchunk - 1) / l.nchunk;
     l.nt = l.nchunk;
+    l.cq = l.nt;
     l.n_tiles = l.chunks;
     l.a_bytes = static_cast<uint32_t>(l.nkb) * 16384;
     l.b_bytes = static_cast<uint32_t>(l.nkb) * l.nchunk * 128;
@@ -503,8 +510,27 @@ int setup_layer(crec_handle* h, size_t li) {
     if (l.smem + 1024 > 232448) return set_error(h, CREC_E_MODEL, "the head does not fit in shared memory");
     if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, ncls))) return rc;
   } else {
-    l.nt = std::min(256, round16(l.cout));
+    // row stacking: the number of output rows a tile computes that gets the most outputs from
+    // an MMA (N up to 256; the rows divide the output's height; no residual), where that is at
+    // least a quarter more than one row gets (measured: 1.2x predicted was no faster)
+    const int cq = round16(l.cout), steps_row = (l.nkb - 1) * 4 + l.last_steps;
+    double best = 0.0;
+    l.q_rows = 1;
+    for (int q = 1; q <= y.h && q * cq <= 256 && (q == 1 || l.residual < 0); ++q) {
+      const int rows = (q - 1) * l.sh + l.kh;
+      if (y.h % q || rows > kMaxKRows) continue;
+      const double per_mma = static_cast<double>(q) / (rows * steps_row);
+      if (per_mma > best * 1.001) {
+        best = per_mma;
+        l.q_rows = q;
+      }
+    }
+    if (best < 1.25 / (l.kh * steps_row)) l.q_rows = 1;
+    l.krows = (l.q_rows - 1) * l.sh + l.kh;
+    l.nt = l.q_rows > 1 ? l.q_rows * cq : std::min(256, cq);
+    l.cq = l.q_rows > 1 ? cq : l.nt;
     l.n_tiles = (y.cp + l.nt - 1) / l.nt;
+    if (l.q_rows > 1) l.n_tiles = 1;
     l.a_bytes = 16384;
     l.b_bytes = static_cast<uint32_t>(l.nt) * 128;
     l.stage_bytes = l.a_bytes + l.b_bytes;
@@ -772,15 +798,17 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     ConvParams p{};
     const long long in_pitch = xp.pitch;
     const uint64_t px = static_cast<uint64_t>(x.cp) * h->eb;
-    for (int ky = 0; ky < l.kh; ++ky) {
-      const uint8_t* base = xp.base + static_cast<long long>(ky - l.pt + xp.ph) * in_pitch - static_cast<long long>(l.pl) * px;
-      int rc = encode_map(h, &p.tmap[ky], base, static_cast<uint64_t>(l.nkb) * 128, static_cast<uint64_t>(ow),
-                          static_cast<uint64_t>(oh), static_cast<uint64_t>(l.sw) * px,
-                          static_cast<uint64_t>(l.sh) * in_pitch);
+    for (int i = 0; i < l.krows; ++i) {  // input row i of a tile's group of q_rows output rows
+      const uint8_t* base = xp.base + static_cast<long long>(i - l.pt + xp.ph) * in_pitch - static_cast<long long>(l.pl) * px;
+      int rc = encode_map(h, &p.tmap[i], base, static_cast<uint64_t>(l.nkb) * 128, static_cast<uint64_t>(ow),
+                          static_cast<uint64_t>(oh / l.q_rows), static_cast<uint64_t>(l.sw) * px,
+                          static_cast<uint64_t>(l.q_rows) * l.sh * in_pitch);
       if (rc) return rc;
     }
     p.wimg = l.wimg;
-    p.kh = l.kh;
+    p.krows = l.krows;
+    p.q_rows = l.q_rows;
+    p.cq = l.cq;
     p.nkb = l.nkb;
     p.last_steps = l.last_steps;
     p.nt = l.nt;
@@ -788,7 +816,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.oh = oh;
     p.ow = static_cast<int>(ow);
     p.m_per_row = static_cast<int>((ow + 127) / 128);
-    p.num_tiles = oh * p.m_per_row * l.n_tiles;
+    p.num_tiles = (oh / l.q_rows) * p.m_per_row * l.n_tiles;
     p.stages = l.stages;
     p.stage_bytes = l.stage_bytes;
     p.a_bytes = l.a_bytes;
