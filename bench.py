@@ -292,14 +292,21 @@ def main() -> int:
             secs = timed(dev, step, args.steps)
         secs = max_over_ranks(secs)
 
+        # a step: take the pages prefetched during the step before (their upload from pinned
+        # memory ran beside that step's runs), give the next step's pages (uploaded beside this
+        # step's runs, as the reference's pipeline does with prefetch_pages), recognize, read
+        # the decodings back: one page upload and one result read-back a step
         def e2e_step():
             dev.set_pages(host_pages, rows)
+            dev.prefetch_pages(host_pages, rows)
             dev.recognize_lines(page_of, allb, bws, flat=True)
 
         for _ in range(max(1, args.warmup // 2)):
             e2e_step()
         esecs = max_over_ranks(timed(dev, e2e_step, args.steps))
+        # one step's bytes: the prefetch's page upload, then the recognize call's own copies
         dev.set_pages(host_pages, rows)
+        dev.prefetch_pages(host_pages, rows)
         h2d_pages = dev.last_stats()["h2d_bytes"]
         dev.recognize_lines(page_of, allb, bws, flat=True)
         st = dev.last_stats()

@@ -220,7 +220,10 @@ class RecDevice:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 (interpreter shutdown: the module may be gone)
+            pass
 
     def _check(self, rc: int) -> None:
         if rc != OK:
@@ -234,23 +237,28 @@ class RecDevice:
     def stream(self) -> int:
         return lib().crec_stream(self._h)
 
+    def _runs(self, rows, keep):
+        if rows is None:
+            return None
+        rr = []
+        for r in rows:
+            if r:
+                a = np.ascontiguousarray(np.asarray(r, np.int32).reshape(-1))
+                keep.append(a)
+                rr.append(RowRuns(a.ctypes.data, len(a) // 2))
+            else:
+                rr.append(RowRuns(None, 0))
+        return (RowRuns * len(rr))(*rr)
+
     def set_pages(self, pages, rows=None) -> None:
-        """pages: list of 2-d uint8 arrays (paper 255); rows: per page a list of (first, last) row runs or None."""
+        """pages: list of 2-d uint8 arrays (paper 255); rows: per page a list of (first, last) row runs or None.
+        The arrays are kept alive here until the next set_pages or prefetch_pages call returns."""
         arr = [np.ascontiguousarray(p, np.uint8) for p in pages]
         descs = (Page * max(1, len(arr)))(*[Page(a.ctypes.data, a.shape[1], a.shape[0], a.strides[0]) for a in arr])
-        runs = None
-        keep = []
-        if rows is not None:
-            rr = []
-            for r in rows:
-                if r:
-                    a = np.ascontiguousarray(np.asarray(r, np.int32).reshape(-1))
-                    keep.append(a)
-                    rr.append(RowRuns(a.ctypes.data, len(a) // 2))
-                else:
-                    rr.append(RowRuns(None, 0))
-            runs = (RowRuns * len(rr))(*rr)
+        keep: list = []
+        runs = self._runs(rows, keep)
         self._check(lib().crec_set_pages(self._h, descs, len(arr), runs))
+        self._alive = arr
 
     def set_pages_device(self, pages) -> None:
         """pages: list of (device pointer, width, height, stride) already in this GPU's memory."""
@@ -258,9 +266,14 @@ class RecDevice:
         self._check(lib().crec_set_pages_device(self._h, descs, len(pages)))
 
     def prefetch_pages(self, pages, rows=None) -> None:
+        """The next group's pages, uploaded beside the current group's work; a set_pages with the same
+        arrays then takes them.  Kept alive here until the next set_pages or prefetch_pages call returns."""
         arr = [np.ascontiguousarray(p, np.uint8) for p in pages]
         descs = (Page * max(1, len(arr)))(*[Page(a.ctypes.data, a.shape[1], a.shape[0], a.strides[0]) for a in arr])
-        self._check(lib().crec_prefetch_pages(self._h, descs, len(arr), None))
+        keep: list = []
+        runs = self._runs(rows, keep)
+        self._check(lib().crec_prefetch_pages(self._h, descs, len(arr), runs))
+        self._alive = arr
 
     def _lines(self, n: int, cap: int):
         bufs = dict(counts=np.empty(n, np.int32), lengths=np.empty(n, np.int32), offsets=np.empty(n, np.int32),

@@ -130,12 +130,27 @@ struct crec_handle {
   uint8_t* in_table = nullptr;
   float* head_table = nullptr;
   float* ctc_terms = nullptr;  // INT8: [256][256] exp_neg(table[q] - table[best])
-  // pages
-  std::vector<PageDesc> pages;  // device pointers
-  uint8_t* page_mem = nullptr;
-  size_t page_cap = 0;
-  bool pages_owned = true;
-  PageDesc* d_pages = nullptr;
+  // pages: two slots, the group being read and the next group's upload (prefetch_pages, on the
+  // copy stream while the current group's runs go on), as the reference's CUDA device keeps them
+  // (carbon/src/cuda/pipeline_cuda.cpp:407-437); or the caller's own device pages
+  struct PageSlot {
+    uint8_t* mem = nullptr;
+    size_t cap = 0;
+    PageDesc* d_pages = nullptr;     // [max_pages]
+    std::vector<PageDesc> pages;     // device pointers
+    std::vector<crec_page> views;    // the host pages uploaded (what set_pages compares)
+    cudaEvent_t done = nullptr;      // its upload, recorded on the copy stream
+    cudaEvent_t unused = nullptr;    // the last recognize work that read it, on the recognize stream
+    bool ready = false;              // a prefetch's upload set_pages has not taken yet
+    bool recorded = false;           // `unused` recorded
+  };
+  PageSlot slot[2];
+  int cur = 0;
+  cudaEvent_t last_upload = nullptr;  // the previous set_pages / prefetch_pages call's upload
+  cudaStream_t copy_stream = nullptr;
+  PageDesc* d_ext_pages = nullptr;  // set_pages_device's descriptors
+  std::vector<PageDesc> pages;      // the current group's, device pointers
+  PageDesc* d_pages = nullptr;      // and their descriptors on the device
   int max_pages = 0;
   // run buffers
   LineDesc* d_lines = nullptr;
@@ -1090,8 +1105,14 @@ void free_all(crec_handle* h) {
   cudaFree(h->in_table);
   cudaFree(h->head_table);
   cudaFree(h->ctc_terms);
-  if (h->pages_owned) cudaFree(h->page_mem);
-  cudaFree(h->d_pages);
+  for (auto& sl : h->slot) {
+    cudaFree(sl.mem);
+    cudaFree(sl.d_pages);
+    if (sl.done) cudaEventDestroy(sl.done);
+    if (sl.unused) cudaEventDestroy(sl.unused);
+  }
+  cudaFree(h->d_ext_pages);
+  if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
   cudaFree(h->d_lines);
   cudaFree(h->d_mask);
   cudaFree(h->d_frame0);
@@ -1174,7 +1195,14 @@ int open_impl(crec_handle* h, const crec_config* c) {
   const int ml = c->max_lines;
   const size_t frames = static_cast<size_t>(h->max_cols >> h->head_shift);
   h->max_pages = std::max(1, c->max_pages);
-  if ((rc = dev_alloc(h, &h->d_pages, h->max_pages)) || (rc = dev_alloc(h, &h->d_lines, ml)) ||
+  CK(cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking));
+  for (auto& sl : h->slot) {
+    CK(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&sl.unused, cudaEventDisableTiming));
+    if ((rc = dev_alloc(h, &sl.d_pages, h->max_pages))) return rc;
+  }
+  h->d_pages = h->slot[0].d_pages;
+  if ((rc = dev_alloc(h, &h->d_ext_pages, h->max_pages)) || (rc = dev_alloc(h, &h->d_lines, ml)) ||
       (rc = dev_alloc(h, &h->d_mask, h->max_cols / 8)) || (rc = dev_alloc(h, &h->d_frame0, ml)) ||
       (rc = dev_alloc(h, &h->d_length, ml)) || (rc = dev_alloc(h, &h->d_frame_id, frames)) ||
       (rc = dev_alloc(h, &h->d_frame_prob, frames)) || (rc = dev_alloc(h, &h->d_count, ml)) ||
@@ -1276,6 +1304,7 @@ int crec_close(crec_handle* h) {
   if (!h) return CREC_OK;
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
+  if (h->copy_stream) cudaStreamSynchronize(h->copy_stream);
   free_all(h);
   delete h;
   return CREC_OK;
@@ -1285,61 +1314,114 @@ const char* crec_last_error(const crec_handle* h) { return h ? h->error.c_str() 
 int crec_is_broken(const crec_handle* h) { return h && h->broken ? 1 : 0; }
 void* crec_stream(crec_handle* h) { return h ? static_cast<void*>(h->stream) : nullptr; }
 
+namespace {
+
+// The pages (only rows[i]'s runs where given) into a slot, queued on the copy stream once the
+// recognize work that last read the slot is done; its `done` event follows them.
+int upload_slot(crec_handle* h, crec_handle::PageSlot& sl, const crec_page* pages, int n, const crec_row_runs* rows) {
+  size_t need = 0;
+  for (int i = 0; i < n; ++i) need += (static_cast<size_t>(pages[i].height) * pages[i].width + 255) / 256 * 256;
+  if (need > sl.cap) {
+    const size_t limit = h->cfg.max_page_bytes > 0 ? static_cast<size_t>(h->cfg.max_page_bytes)
+                                                   : static_cast<size_t>(h->max_pages) * 1700 * 2200;
+    if (need > std::max(limit + static_cast<size_t>(n) * 256, sl.cap))
+      return set_error(h, CREC_E_RANGE, "set_pages: more page bytes than configured");
+    CK(cudaStreamSynchronize(h->stream));  // nothing queued may still read the old memory
+    CK(cudaStreamSynchronize(h->copy_stream));
+    cudaFree(sl.mem);
+    sl.mem = nullptr;
+    sl.cap = 0;
+    CK(cudaMalloc(&sl.mem, need));
+    sl.cap = need;
+  }
+  if (sl.recorded) CK(cudaStreamWaitEvent(h->copy_stream, sl.unused, 0));
+  sl.pages.resize(n);
+  sl.views.assign(pages, pages + n);
+  size_t at = 0;
+  auto rows_of = [&](const crec_page& pg, uint8_t* d, int y0, int y1) -> int {
+    if (pg.stride == pg.width) {  // contiguous rows: one copy
+      CK(cudaMemcpyAsync(d + static_cast<size_t>(y0) * pg.width, pg.data + static_cast<size_t>(y0) * pg.stride,
+                         static_cast<size_t>(y1 - y0) * pg.width, cudaMemcpyHostToDevice, h->copy_stream));
+    } else {
+      CK(cudaMemcpy2DAsync(d + static_cast<size_t>(y0) * pg.width, pg.width, pg.data + static_cast<size_t>(y0) * pg.stride,
+                           pg.stride, pg.width, y1 - y0, cudaMemcpyHostToDevice, h->copy_stream));
+    }
+    h->st_h2d += static_cast<long long>(y1 - y0) * pg.width;
+    return CREC_OK;
+  };
+  for (int i = 0; i < n; ++i) {
+    const crec_page& pg = pages[i];
+    uint8_t* d = sl.mem + at;
+    sl.pages[i] = {d, pg.width, pg.height, static_cast<long long>(pg.width)};
+    int rc;
+    if (rows && rows[i].count > 0 && rows[i].runs) {
+      for (int r = 0; r < rows[i].count; ++r) {
+        const int y0 = std::max(0, rows[i].runs[2 * r]), y1 = std::min(pg.height, rows[i].runs[2 * r + 1]);
+        if (y1 > y0 && (rc = rows_of(pg, d, y0, y1))) return rc;
+      }
+    } else if ((rc = rows_of(pg, d, 0, pg.height))) {
+      return rc;
+    }
+    at += (static_cast<size_t>(pg.height) * pg.width + 255) / 256 * 256;
+  }
+  if (n > 0) CK(cudaMemcpyAsync(sl.d_pages, sl.pages.data(), sizeof(PageDesc) * n, cudaMemcpyHostToDevice, h->copy_stream));
+  CK(cudaEventRecord(sl.done, h->copy_stream));
+  h->last_upload = sl.done;
+  return CREC_OK;
+}
+
+// The previous call's pages are the caller's again once its upload is done (the pages of a
+// set_pages or prefetch_pages call stay alive until the next such call returns).
+int release_previous(crec_handle* h) {
+  if (h->last_upload) CK(cudaEventSynchronize(h->last_upload));
+  h->last_upload = nullptr;
+  return CREC_OK;
+}
+
+bool same_pages(const std::vector<crec_page>& a, const crec_page* b, int n) {
+  if (static_cast<int>(a.size()) != n) return false;
+  for (int i = 0; i < n; ++i)
+    if (a[i].data != b[i].data || a[i].width != b[i].width || a[i].height != b[i].height || a[i].stride != b[i].stride)
+      return false;
+  return true;
+}
+
+}  // namespace
+
 int crec_set_pages(crec_handle* h, const crec_page* pages, int n, const crec_row_runs* rows) {
   int rc = pages_common(h, pages, n);
   if (rc) return rc;
   CK(cudaSetDevice(h->device));
-  size_t need = 0;
-  for (int i = 0; i < n; ++i) need += (static_cast<size_t>(pages[i].height) * pages[i].width + 255) / 256 * 256;
-  if (!h->pages_owned) {
-    h->page_mem = nullptr;
-    h->page_cap = 0;
-    h->pages_owned = true;
-  }
-  if (need > h->page_cap) {
-    const size_t limit = h->cfg.max_page_bytes > 0 ? static_cast<size_t>(h->cfg.max_page_bytes)
-                                                   : static_cast<size_t>(h->max_pages) * 1700 * 2200;
-    if (need > std::max(limit + static_cast<size_t>(n) * 256, h->page_cap))
-      return set_error(h, CREC_E_RANGE, "set_pages: more page bytes than configured");
-    CK(cudaStreamSynchronize(h->stream));
-    cudaFree(h->page_mem);
-    h->page_mem = nullptr;
-    h->page_cap = 0;
-    CK(cudaMalloc(&h->page_mem, need));
-    h->page_cap = need;
-  }
-  h->pages.resize(n);
   h->st_h2d = 0;
   h->st_d2h = 0;
   h->st_launches = 0;
   h->st_runs = 0;
-  size_t at = 0;
-  for (int i = 0; i < n; ++i) {
-    const crec_page& pg = pages[i];
-    uint8_t* d = h->page_mem + at;
-    h->pages[i] = {d, pg.width, pg.height, static_cast<long long>(pg.width)};
-    if (rows && rows[i].count > 0 && rows[i].runs) {
-      for (int r = 0; r < rows[i].count; ++r) {
-        const int y0 = std::max(0, rows[i].runs[2 * r]), y1 = std::min(pg.height, rows[i].runs[2 * r + 1]);
-        if (y1 <= y0) continue;
-        CK(cudaMemcpy2DAsync(d + static_cast<size_t>(y0) * pg.width, pg.width, pg.data + y0 * pg.stride, pg.stride,
-                             pg.width, y1 - y0, cudaMemcpyHostToDevice, h->stream));
-        h->st_h2d += static_cast<long long>(y1 - y0) * pg.width;
-      }
-    } else {
-      CK(cudaMemcpy2DAsync(d, pg.width, pg.data, pg.stride, pg.width, pg.height, cudaMemcpyHostToDevice, h->stream));
-      h->st_h2d += static_cast<long long>(pg.height) * pg.width;
-    }
-    at += (static_cast<size_t>(pg.height) * pg.width + 255) / 256 * 256;
-  }
-  if (n > 0) CK(cudaMemcpyAsync(h->d_pages, h->pages.data(), sizeof(PageDesc) * n, cudaMemcpyHostToDevice, h->stream));
-  CK(cudaStreamSynchronize(h->stream));  // the caller may reuse its pages now
+  crec_handle::PageSlot& next = h->slot[1 - h->cur];
+  const bool taken = next.ready && same_pages(next.views, pages, n);
+  if ((rc = release_previous(h))) return rc;  // a taken prefetch's upload too: done by now when it ran beside a group
+  if (!taken && (rc = upload_slot(h, next, pages, n, rows))) return rc;
+  next.ready = false;
+  // the slot left behind is free once the recognize work queued so far is done
+  crec_handle::PageSlot& old = h->slot[h->cur];
+  CK(cudaEventRecord(old.unused, h->stream));
+  old.recorded = true;
+  h->cur = 1 - h->cur;
+  h->pages = next.pages;
+  h->d_pages = next.d_pages;
+  CK(cudaStreamWaitEvent(h->stream, next.done, 0));  // the recognize stream waits for the upload alone
   return CREC_OK;
 }
 
 int crec_prefetch_pages(crec_handle* h, const crec_page* pages, int n, const crec_row_runs* rows) {
-  (void)rows;
-  return pages_common(h, pages, n);
+  int rc = pages_common(h, pages, n);
+  if (rc) return rc;
+  CK(cudaSetDevice(h->device));
+  if ((rc = release_previous(h))) return rc;
+  crec_handle::PageSlot& next = h->slot[1 - h->cur];
+  next.ready = false;
+  if ((rc = upload_slot(h, next, pages, n, rows))) return rc;
+  next.ready = true;
+  return CREC_OK;
 }
 
 int crec_set_pages_device(crec_handle* h, const crec_page* pages, int n) {
@@ -1348,8 +1430,9 @@ int crec_set_pages_device(crec_handle* h, const crec_page* pages, int n) {
   CK(cudaSetDevice(h->device));
   h->pages.resize(n);
   for (int i = 0; i < n; ++i) h->pages[i] = {pages[i].data, pages[i].width, pages[i].height, static_cast<long long>(pages[i].stride)};
-  if (n > 0) CK(cudaMemcpyAsync(h->d_pages, h->pages.data(), sizeof(PageDesc) * n, cudaMemcpyHostToDevice, h->stream));
+  if (n > 0) CK(cudaMemcpyAsync(h->d_ext_pages, h->pages.data(), sizeof(PageDesc) * n, cudaMemcpyHostToDevice, h->stream));
   CK(cudaStreamSynchronize(h->stream));
+  h->d_pages = h->d_ext_pages;
   return CREC_OK;
 }
 

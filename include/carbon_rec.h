@@ -113,11 +113,15 @@ CREC_API const char* crec_last_error(const crec_handle* h);
 /* Whether a sticky error left the GPU unusable for this process (PipelineModels::broken). */
 CREC_API int crec_is_broken(const crec_handle* h);
 
-/* The pages the recognize calls that follow crop from, copied to the GPU (only rows[i]'s runs
- * where given). The caller may reuse its pages once the call returns. */
+/* The pages the recognize calls that follow crop from, on the GPU (only rows[i]'s runs copied
+ * where given): the pages a prefetch_pages call gave already (same pointers and sizes), else
+ * uploaded now. The copies run on their own stream; the recognize work waits for them on the
+ * device. The pages must stay alive and unchanged until the next set_pages or prefetch_pages
+ * call returns (or crec_close), as the reference's contract has them (pipeline.h:118-120). */
 CREC_API int crec_set_pages(crec_handle* h, const crec_page* pages, int n, const crec_row_runs* rows);
-/* The next group's pages, given while the current group is read. This build uploads at
- * set_pages; the call validates its arguments and returns. */
+/* The next group's pages, given while the current group is read (pipeline.h:121-124): uploaded
+ * now into the second page buffer on the copy stream, beside the current group's runs; the
+ * set_pages with these same pages then only switches buffers. Same lifetime rule. */
 CREC_API int crec_prefetch_pages(crec_handle* h, const crec_page* pages, int n, const crec_row_runs* rows);
 /* Pages already in this handle's GPU memory (data are device pointers): used in place. */
 CREC_API int crec_set_pages_device(crec_handle* h, const crec_page* pages, int n);

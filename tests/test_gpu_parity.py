@@ -189,6 +189,44 @@ def test_scheduler_runs_are_independent_of_grouping(rec_latin):
         small.close()
 
 
+def test_prefetched_pages_give_the_same_decodings(rec_latin):
+    """Two groups of pages alternating as the reference's pipeline gives them: the next group
+    prefetched (uploaded into the other page buffer beside the current group's runs), then taken by
+    set_pages; a prefetch that set_pages does not take (other pages) is uploaded again.  Every
+    decoding equals the one of plain set_pages, bit for bit."""
+    groups = [synth.pages(31 + g, 2, 1400, 1000, 12) for g in range(2)]
+    blob = rec_latin[0].to_blob()
+    plain = native.RecDevice(blob, native.INT8, max_lines=64, max_width=2048, max_pages=2)
+    piped = native.RecDevice(blob, native.INT8, max_lines=64, max_width=2048, max_pages=2)
+    try:
+        want = []
+        for pages, boxes in groups:
+            plain.set_pages(pages)
+            page_of = np.repeat(np.arange(2), 12).astype(np.int32)
+            want.append(plain.recognize_lines(page_of, np.concatenate(boxes)))
+        rows = [[native.rows_read(b, 1000) for b in boxes] for _, boxes in groups]
+        order = [0, 1, 0, 1, 1]
+        piped.set_pages(groups[0][0], rows[0])
+        for k, g in enumerate(order):
+            if k > 0:
+                piped.set_pages(groups[g][0], rows[g])
+            nxt = order[k + 1] if k + 1 < len(order) else None
+            if nxt is not None and nxt != g:
+                piped.prefetch_pages(groups[nxt][0], rows[nxt])
+            elif nxt is not None:
+                piped.prefetch_pages(groups[1 - g][0], rows[1 - g])  # not taken: the next set_pages uploads again
+            page_of = np.repeat(np.arange(2), 12).astype(np.int32)
+            got, lengths = piped.recognize_lines(page_of, np.concatenate(groups[g][1]))
+            wl, wlen = want[g]
+            assert np.array_equal(lengths, wlen)
+            for x, y in zip(got, wl):
+                assert np.array_equal(x.ids, y.ids) and np.array_equal(x.frames, y.frames)
+                assert np.array_equal(x.probs.view(np.int32), y.probs.view(np.int32))
+    finally:
+        plain.close()
+        piped.close()
+
+
 def test_mini_model_odd_channels_bit_exact(mini, orc, golden):
     """A recognizer whose channel counts are not multiples of 16 (padded on the device)."""
     import hashlib
