@@ -29,7 +29,7 @@ constexpr int kCropThreads = 512;
 constexpr int kMaxTaps = 32;          // taps a sample may have: downscales up to 15x (the host checks)
 constexpr int kStripBytes = 32 << 10;  // the horizontal pass's intermediate: source rows x strip columns
 constexpr int kCoefBytes = 16 << 10;   // a strip's horizontal coefficients: columns x taps x 4 bytes
-constexpr int kMaxStripCols = 512;    // output columns a strip at most
+constexpr int kMaxStripCols = 256;    // output columns a strip at most (two row groups keep all 512 threads busy)
 constexpr int kMaxSrcRows = 1024;     // source rows a crop's vertical windows may span (the host checks)
 constexpr int kStemMaxOut = 64;       // the stem's output channels at most (padded)
 
