@@ -85,6 +85,17 @@ def reduce_max(v: float, world: int, device: str) -> float:
     return float(t.item())
 
 
+def reduce_sum(v: float, world: int, device: str) -> float:
+    """A count summed over the ranks (a collective; every rank calls it)."""
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 # measured: dram__bytes_read.sum + dram__bytes_write.sum of all conv_gemm launches of one
 # 524,288-column run / 11, x 4 (a 2,097,152-column run)
 CONV_TRAFFIC_PER_LAUNCH = 646.2e6 / 11 * 4
@@ -313,8 +324,9 @@ def main() -> int:
         total_lines = args.pages * LINES_PER_PAGE
         results[prec] = {"value": total_lines * args.steps / secs, "ms_per_step": 1000 * secs / args.steps,
                          "e2e": {"value": total_lines * args.steps / esecs, "unit": "lines/s",
-                                 "h2d_bytes_per_step": int(h2d_pages + st["h2d_bytes"]),
-                                 "d2h_bytes_per_step": int(st["d2h_bytes"])},
+                                 # the whole job's bytes a step: every rank's summed
+                                 "h2d_bytes_per_step": int(reduce_sum(h2d_pages + st["h2d_bytes"], world, "cuda")),
+                                 "d2h_bytes_per_step": int(reduce_sum(st["d2h_bytes"], world, "cuda"))},
                          "launches_per_step": int(st["launches"])}
         dev.close()
 

@@ -34,8 +34,9 @@ def _rank_main(rank: int, world: int, port: int, pages_total: int, out_dir: str)
         _, _, page_of, boxes, bws = bench.workload(rank, world, pages_total)
         # each rank's own step time; the job's is the slowest rank's
         t = bench.reduce_max(0.5 + rank, world, "cpu")
+        total = bench.reduce_sum(10 + rank, world, "cpu")
         dist.barrier()
-        np.savez(Path(out_dir) / f"rank{rank}.npz", page_of=page_of, boxes=boxes, bws=bws, t=t)
+        np.savez(Path(out_dir) / f"rank{rank}.npz", page_of=page_of, boxes=boxes, bws=bws, t=t, total=total)
     finally:
         dist.destroy_process_group()
 
@@ -57,6 +58,7 @@ def test_two_ranks_shard_pages_and_take_the_max(tmp_path):
     assert np.array_equal(np.concatenate([p["bws"] for p in parts]), bws1)
     assert [len(p["page_of"]) for p in parts] == [pages_total // world * bench.LINES_PER_PAGE] * world
     assert all(float(p["t"]) == 0.5 + (world - 1) for p in parts)
+    assert all(float(p["total"]) == 10 * world + world * (world - 1) // 2 for p in parts)
 
 
 def test_reference_arm_runs_on_rank_zero_only():
