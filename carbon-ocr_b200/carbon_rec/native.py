@@ -26,7 +26,7 @@ _NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA
 EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec_set_pages", "crec_prefetch_pages",
            "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_ctc_greedy", "crec_ctc_greedy_noalloc", "crec_width_bucket", "crec_crop_region",
            "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats",
-           "crec_profile", "crec_profile_layers"]
+           "crec_profile", "crec_profile_layers", "crec_mma_peak"]
 
 
 class CrecError(RuntimeError):
@@ -112,8 +112,18 @@ def lib() -> C.CDLL:
         L.crec_last_stats.argtypes = [p, C.POINTER(Stats)]
         L.crec_profile.argtypes = [p, i, C.POINTER(ProfileEntry), i]
         L.crec_profile_layers.argtypes = [p, C.POINTER(ProfileEntry), i]
+        L.crec_mma_peak.argtypes = [i, i, i, i, C.POINTER(C.c_double)]
         _lib = L
     return _lib
+
+
+def mma_peak(device: int = 0, precision: int = 0, n: int = 256, iters: int = 4096) -> float:
+    """The tensor cores' measured dense rate (TOP/s): back-to-back tcgen05.mma, M = 128, K = 32 bytes."""
+    out = C.c_double(0.0)
+    rc = lib().crec_mma_peak(device, precision, n, iters, C.byref(out))
+    if rc != 0:
+        raise CrecError(rc, "crec_mma_peak")
+    return out.value
 
 
 def ctc_greedy(logits_ptr: int, n: int, classes: int, frames: int, lengths, stream: int = 0):

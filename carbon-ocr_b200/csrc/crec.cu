@@ -27,6 +27,7 @@
 #include "crop_stem.cuh"
 #include "ctc.cuh"
 #include "dw_head.cuh"
+#include "peak.cuh"
 #include "sm100.cuh"
 
 using namespace crec;
@@ -1738,3 +1739,47 @@ int crec_debug_value(crec_handle* h, int value, void* out, int64_t capacity) {
 }
 
 }  // extern "C"
+
+int crec_mma_peak(int device, int precision, int n, int iters, double* tera_ops) {
+  if (!tera_ops || n < 16 || n > 256 || n % 16 || iters < 1 || (precision != CREC_INT8 && precision != CREC_FP16))
+    return CREC_E_INVALID;
+  if (cudaSetDevice(device) != cudaSuccess) return CREC_E_CUDA;
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return CREC_E_CUDA;
+  if (prop.major != 10) return CREC_E_INVALID;
+  int* err = nullptr;
+  if (cudaMalloc(&err, sizeof(int)) != cudaSuccess) return CREC_E_NOMEM;
+  cudaMemset(err, 0, sizeof(int));
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  const int smem = kPeakSmem;
+  auto launch = [&](int it) {
+    if (precision == CREC_INT8) {
+      cudaFuncSetAttribute(mma_peak_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      mma_peak_kernel<true><<<prop.multiProcessorCount, 128, smem>>>(n, it, err);
+    } else {
+      cudaFuncSetAttribute(mma_peak_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      mma_peak_kernel<false><<<prop.multiProcessorCount, 128, smem>>>(n, it, err);
+    }
+  };
+  launch(16);  // warm-up
+  cudaEventRecord(e0);
+  launch(iters);
+  cudaEventRecord(e1);
+  int rc = cudaEventSynchronize(e1) == cudaSuccess ? CREC_OK : CREC_E_CUDA;
+  int h_err = 0;
+  if (rc == CREC_OK && cudaMemcpy(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) rc = CREC_E_CUDA;
+  if (rc == CREC_OK && cudaGetLastError() != cudaSuccess) rc = CREC_E_CUDA;
+  if (rc == CREC_OK && h_err) rc = CREC_E_TIMEOUT;
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  // multiply-adds an MMA: 128 x n x K, K = 32 bytes (32 int8, 16 fp16)
+  const double k = precision == CREC_INT8 ? 32.0 : 16.0;
+  const double ops = 2.0 * 128.0 * n * k * 4.0 * iters * prop.multiProcessorCount;
+  *tera_ops = rc == CREC_OK && ms > 0 ? ops / (ms * 1e-3) / 1e12 : 0.0;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFree(err);
+  return rc;
+}

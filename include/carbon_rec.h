@@ -197,6 +197,13 @@ CREC_API int crec_profile(crec_handle* h, int enable, crec_profile_entry* out, i
  * capacity), or a negative status.  No counterpart in the reference (a diagnostic). */
 CREC_API int crec_profile_layers(crec_handle* h, crec_profile_entry* out, int capacity);
 
+/* The tensor cores' dense rate, measured on GPU `device`: every SM issuing back-to-back
+ * tcgen05.mma (M = 128, K = 32 bytes, N = n, 16..256) of `precision` (CREC_INT8: u8 x s8 -> s32;
+ * CREC_FP16: f16 -> f32) from shared memory into TMEM, `iters` x 4 each. *tera_ops: 2 x
+ * multiply-adds a second / 1e12. The roofline's denominator for this build's tensor kernels.
+ * No counterpart in the reference (a measurement). */
+CREC_API int crec_mma_peak(int device, int precision, int n, int iters, double* tera_ops);
+
 /* The CUDA stream (a cudaStream_t) the handle's work runs on, for device-side timing. */
 CREC_API void* crec_stream(crec_handle* h);
 
