@@ -131,75 +131,86 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        const int n = t % p.n_tiles, m = t / p.n_tiles;
-        const int oy = m / p.m_per_row, ox0 = (m % p.m_per_row) * 128;
-        for (int ky = 0; ky < p.krows && ok; ++ky) {
-          for (int kb = 0; kb < p.nkb; ++kb) {
-            if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutEmpty)) {
-              ok = false;
-              break;
-            }
+    // The whole warp runs the loop (its counters, coordinates and addresses warp-uniform), one
+    // elected lane issues the copies.
+    const bool leader = elect_one();
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      const int n = t % p.n_tiles, m = t / p.n_tiles;
+      const int oy = m / p.m_per_row, ox0 = (m % p.m_per_row) * 128;
+      for (int ky = 0; ky < p.krows && ok; ++ky) {
+        for (int kb = 0; kb < p.nkb; ++kb) {
+          if (!mbar_wait_warp(&empty[stage], phase ^ 1, p.err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (leader) {
             uint8_t* a = smem + stage * p.stage_bytes;
             uint8_t* b = a + p.a_bytes;
             mbar_expect_tx(&full[stage], p.a_bytes + p.b_bytes);
             tma_load_3d(a, &p.tmap[ky], kb * 128, ox0, oy, &full[stage]);
             const uint8_t* w = p.wimg + (static_cast<size_t>((n * p.krows + ky) * p.nkb + kb)) * p.b_bytes;
             bulk_load(b, w, p.b_bytes, &full[stage]);
-            if (++stage == p.stages) {
-              stage = 0;
-              phase ^= 1;
-            }
+          }
+          __syncwarp();
+          if (++stage == p.stages) {
+            stage = 0;
+            phase ^= 1;
           }
         }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = kInt8 ? idesc_i8(p.nt) : idesc_f16(p.nt);
-      // the stages' descriptors differ only in the start address (bits 0..13, address >> 4): a
-      // K step of 32 bytes adds 2, a stage stage_bytes >> 4
-      const uint64_t a_desc0 = umma_desc_sw128(smem_u32(smem)), b_desc0 = umma_desc_sw128(smem_u32(smem) + p.a_bytes);
-      const uint32_t stage_step = p.stage_bytes >> 4;
-      int stage = 0;
-      uint32_t phase = 0;
-      int iter = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++iter) {
-        const int acc = iter & (p.n_acc - 1);
-        const uint32_t acc_phase = (iter / p.n_acc) & 1;
-        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, p.err, kErrTimeoutTmemEmpty)) break;
+    // As the producer: the warp runs the loop, so the descriptors, the accumulator address and
+    // the accumulate flag the MMAs take are warp-uniform; one elected lane issues the MMAs and
+    // their commits (a commit tracks the MMAs of the lane that issues it).
+    const bool leader = elect_one();
+    const uint32_t tmem = __shfl_sync(0xffffffffu, tmem_base, 0);
+    const uint32_t idesc = kInt8 ? idesc_i8(p.nt) : idesc_f16(p.nt);
+    // the stages' descriptors differ only in the start address (bits 0..13, address >> 4): a
+    // K step of 32 bytes adds 2, a stage stage_bytes >> 4
+    const uint64_t a_desc0 = umma_desc_sw128(smem_u32(smem)), b_desc0 = umma_desc_sw128(smem_u32(smem) + p.a_bytes);
+    const uint32_t stage_step = p.stage_bytes >> 4;
+    int stage = 0;
+    uint32_t phase = 0;
+    int iter = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++iter) {
+      const int acc = iter & (p.n_acc - 1);
+      const uint32_t acc_phase = (iter / p.n_acc) & 1;
+      if (!mbar_wait_warp(&tmem_empty[acc], acc_phase ^ 1, p.err, kErrTimeoutTmemEmpty)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + static_cast<uint32_t>(acc) * acc_cols;
+      uint32_t accumulate = 0;
+      int kb = 0;
+      for (int ks = 0; ks < ksteps_per_tile; ++ks) {
+        if (!mbar_wait_warp(&full[stage], phase, p.err, kErrTimeoutFull)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc) * acc_cols;
-        uint32_t accumulate = 0;
-        int kb = 0;
-        for (int ks = 0; ks < ksteps_per_tile; ++ks) {
-          if (!mbar_wait(&full[stage], phase, p.err, kErrTimeoutFull)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t ad = a_desc0 + static_cast<uint64_t>(stage) * stage_step;
-          const uint64_t bd = b_desc0 + static_cast<uint64_t>(stage) * stage_step;
-          const int steps = ++kb == p.nkb ? p.last_steps : 4;
-          if (kb == p.nkb) kb = 0;
+        const uint64_t ad = a_desc0 + static_cast<uint64_t>(stage) * stage_step;
+        const uint64_t bd = b_desc0 + static_cast<uint64_t>(stage) * stage_step;
+        const int steps = ++kb == p.nkb ? p.last_steps : 4;
+        if (kb == p.nkb) kb = 0;
+        if (leader) {
 #pragma unroll
           for (int s = 0; s < 4; ++s)
             if (s < steps) umma<kInt8>(d, ad + 2 * s, bd + 2 * s, idesc, accumulate | static_cast<uint32_t>(s));
           umma_commit(&empty[stage]);
-          accumulate = 1;
-          if (++stage == p.stages) {
-            stage = 0;
-            phase ^= 1;
-          }
         }
-        umma_commit(&tmem_full[acc]);
+        __syncwarp();
+        accumulate = 1;
+        if (++stage == p.stages) {
+          stage = 0;
+          phase ^= 1;
+        }
       }
+      if (leader) umma_commit(&tmem_full[acc]);
+      __syncwarp();
     }
   } else {
     // ---------------------------------------------------------------- epilogue

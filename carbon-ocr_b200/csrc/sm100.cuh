@@ -85,6 +85,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// One lane of a converged warp (the same lane each call while the whole warp is active).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n" : "=r"(e));
+  return e != 0;
+}
+
+// mbar_wait by every lane of a converged warp; the vote makes the result warp-uniform, so a
+// loop that leaves on a timeout keeps its counters uniform (and the MMA and TMA operands
+// derived from them in uniform registers).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code));
+}
+
 // TMA: a tiled box of a 3-d tensor map into shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
   asm volatile(
