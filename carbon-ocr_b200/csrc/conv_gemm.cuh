@@ -67,6 +67,8 @@ struct ConvParams {
   const float* scale;     // [cp_out] input scale * weight scale (int8)
   const float* bias;      // [cp_out]
   int out_zero, relu;
+  int sat;      // INT8: |v * inv_scale| < 2^21 for every output, so it may be rounded before the clamp
+  int code_lo;  // the lowest code: the zero point after a ReLU, else 0
   int n_acc;              // TMEM accumulators (a power of two, <= kMaxAcc), each 512 / n_acc columns
   float out_inv_scale;
   const uint8_t* res;  // residual tensor's first row, or null
@@ -257,6 +259,53 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
           uint4 o;
           if (!valid) {
             o = make_uint4(zb, zb, zb, zb);
+          } else if constexpr (kFast) {
+            // the output stage; where the layer's bound allows, rounded before the clamp and the
+            // clamp done by the saturating byte pack (clamp and round-to-integer commute for
+            // integer bounds)
+            int32_t code[16];
+            uint4 rv = make_uint4(0, 0, 0, 0);
+            if (res) rv = *reinterpret_cast<const uint4*>(res + cb);
+            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int4 o4 = *reinterpret_cast<const int4*>(s_off + cb + 4 * k);
+              const float4 s4 = *reinterpret_cast<const float4*>(s_scale + cb + 4 * k);
+              const float4 b4 = *reinterpret_cast<const float4*>(s_bias + cb + 4 * k);
+              const int32_t oo[4] = {o4.x, o4.y, o4.z, o4.w};
+              const float ss[4] = {s4.x, s4.y, s4.z, s4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+              for (int u = 0; u < 4; u += 2) {
+                const int32_t a0 = static_cast<int32_t>(r[4 * k + u]), a1 = static_cast<int32_t>(r[4 * k + u + 1]);
+                float2 v;
+                v.x = __fadd_rn(__fmul_rn(magic_to_float(a0 + oo[u]), ss[u]), bb[u]);
+                v.y = __fadd_rn(__fmul_rn(magic_to_float(a1 + oo[u + 1]), ss[u + 1]), bb[u + 1]);
+                if (res) {
+                  const int32_t r0 = static_cast<int32_t>((rw[k] >> (8 * u)) & 0xffu);
+                  const int32_t r1 = static_cast<int32_t>((rw[k] >> (8 * u + 8)) & 0xffu);
+                  v.x = __fadd_rn(v.x, __fmul_rn(magic_to_float(r0 + rzc), p.res_scale));
+                  v.y = __fadd_rn(v.y, __fmul_rn(magic_to_float(r1 + rzc), p.res_scale));
+                }
+                float2 q = make_float2(__fmul_rn(v.x, p.out_inv_scale), __fmul_rn(v.y, p.out_inv_scale));
+                if (!p.sat) {
+                  q.x = fminf(fmaxf(q.x, lo), hi);
+                  q.y = fminf(fmaxf(q.y, lo), hi);
+                }
+                const int32_t t0 = magic_rint_bits(q.x), t1 = magic_rint_bits(q.y);
+                code[4 * k + u] = t0 + zc;
+                code[4 * k + u + 1] = t1 + zc;
+              }
+            }
+            if (p.sat && p.code_lo > 0) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) code[i] = max(code[i], p.code_lo);
+            }
+            if (cb + 16 > p.c_out) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (cb + i >= p.c_out) code[i] = p.out_zero;
+            }
+            o = make_uint4(pack_sat_u8x4(code), pack_sat_u8x4(code + 4), pack_sat_u8x4(code + 8), pack_sat_u8x4(code + 12));
           } else {
             int32_t code[16];
             uint4 rv = make_uint4(0, 0, 0, 0);
@@ -272,7 +321,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 const int32_t a = static_cast<int32_t>(r[4 * k + u]);
-                const float f = kFast ? magic_to_float(a + oo[u]) : static_cast<float>(a - oo[u]);
+                const float f = static_cast<float>(a - oo[u]);
                 float v = __fadd_rn(__fmul_rn(f, ss[u]), bb[u]);
                 if (res) {
                   const int32_t rb = static_cast<int32_t>((rw[k] >> (8 * u)) & 0xffu);
@@ -287,12 +336,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
               for (int i = 0; i < 16; ++i)
                 if (cb + i >= p.c_out) code[i] = p.out_zero;
             }
-            uint32_t w[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              w[k] = __byte_perm(__byte_perm(code[4 * k], code[4 * k + 1], 0x0040),
-                                 __byte_perm(code[4 * k + 2], code[4 * k + 3], 0x0040), 0x5410);
-            o = make_uint4(w[0], w[1], w[2], w[3]);
+            o = make_uint4(pack_sat_u8x4(code), pack_sat_u8x4(code + 4), pack_sat_u8x4(code + 8), pack_sat_u8x4(code + 12));
           }
           *reinterpret_cast<uint4*>(dst + cb) = o;
         } else {

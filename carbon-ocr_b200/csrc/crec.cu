@@ -68,6 +68,7 @@ struct Layer {
   uint32_t* dwt = nullptr;  // the INT8 row depthwise's tap-transposed weights (DwParams::wt)
   uint32_t* dwc = nullptr;  // and its per-channel constants (DwParams::dwc)
   bool fast = false;        // its sums fit the exact conversions without the conversion unit
+  bool sat = false;         // INT8 conv: |v * inv_scale| < 2^21 always (round, then clamp while packing)
   int nkb = 0, last_steps = 0, nt = 0, n_tiles = 0, stages = 0, nchunk = 0, chunks = 0;
   int krows = 0, q_rows = 1, cq = 0;  // dense convs: input rows a tile reads, output rows it stacks, channels a row
   uint32_t stage_bytes = 0, a_bytes = 0, b_bytes = 0, smem = 0;
@@ -553,6 +554,21 @@ int setup_layer(crec_handle* h, size_t li) {
     l.stages = std::min<int>(8, (200 * 1024) / l.stage_bytes);
     l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 2 * kMaxAcc) * 8 + 16 + 12 * y.cp + 64;
     if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, y.cp))) return rc;
+    // the output stage's value before the clamp, v * inv_scale, bounded from the weights: with
+    // |v| <= sum |w| * reach * scale + |bias| + 255 * residual scale (and a margin for the
+    // roundings) below 2^21, rounding first and clamping after gives the same code
+    if (h->int8 && l.fast) {
+      const double reach = std::max(x.zero, 255 - x.zero);
+      const double rs = l.residual >= 0 ? 255.0 * std::fabs(h->v[l.residual].scale) : 0.0;
+      const size_t per = l.w8.size() / static_cast<size_t>(l.cout);
+      double worst = 0.0;
+      for (int j = 0; j < l.cout; ++j) {
+        double a = 0.0;
+        for (size_t k = 0; k < per; ++k) a += std::abs(static_cast<int>(l.w8[j * per + k]));
+        worst = std::max(worst, a * reach * std::fabs(scale[j]) + std::fabs(bias[j]) + rs);
+      }
+      l.sat = worst * 1.01 * std::fabs(1.0 / y.scale) < static_cast<double>(1 << 21);
+    }
   }
   const std::vector<uint8_t> img = weight_image(h, l, x.cp, l.nt, l.n_tiles, l.nkb);
   if ((rc = upload(h, &l.wimg, img))) return rc;
@@ -848,6 +864,8 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.bias = l.dbias;
     p.out_zero = y.zero;
     p.relu = l.relu;
+    p.sat = l.sat;
+    p.code_lo = l.relu ? y.zero : 0;
     p.n_acc = conv_accumulators(l.nt);
     p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
     if (l.residual >= 0) {

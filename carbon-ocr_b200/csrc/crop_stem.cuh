@@ -32,6 +32,7 @@ constexpr int kCoefBytes = 16 << 10;   // a strip's horizontal coefficients: col
 constexpr int kMaxStripCols = 256;    // output columns a strip at most (two row groups keep all 512 threads busy)
 constexpr int kMaxSrcRows = 1024;     // source rows a crop's vertical windows may span (the host checks)
 constexpr int kStemMaxOut = 64;       // the stem's output channels at most (padded)
+constexpr int kMaxHWords = 6;         // horizontal windows of up to 24 taps in the dp4a pass (wider: the generic one)
 
 struct PageDesc {
   const uint8_t* data;
@@ -139,7 +140,7 @@ __device__ __forceinline__ uint8_t clip8d(int32_t v) {
 // constants | vertical coefficients | histogram, counters and tables.
 struct CropSmem {
   int qpitch;
-  unsigned qb, tmp, hk, wq, swf, soff, sscale, sbias, vk, vfirst, vcount, hist, red, ftab, stab, total;
+  unsigned qb, tmp, hk, wq, swf, soff, sscale, sbias, vk, vkp, vfirst, vcount, hist, red, ftab, stab, total;
 };
 
 __host__ __device__ inline CropSmem crop_smem(int height, int max_bw) {
@@ -164,6 +165,8 @@ __host__ __device__ inline CropSmem crop_smem(int height, int max_bw) {
   o += kStemMaxOut * 4;
   s.vk = o;
   o += static_cast<unsigned>(height * kMaxTaps * 4);
+  s.vkp = o;  // the vertical weights' byte planes: [height][3][8] words
+  o += static_cast<unsigned>(height * 24 * 4);
   s.vfirst = o;
   o += static_cast<unsigned>(height * 4);
   s.vcount = o;
@@ -213,6 +216,134 @@ __device__ __forceinline__ int hist_nth(const int32_t* hist, int n, bool flipped
   return __shfl_sync(0xffffffffu, v, __ffs(hit) - 1);
 }
 
+// The byte planes of a window's 22-bit weights (non-negative): k0 / k1 / k2 hold bits 0-7 /
+// 8-15 / 16-23 of taps 4j .. 4j+3 in word j, zero past the window's n taps.
+template <int NW>
+__device__ __forceinline__ void weight_planes(const int32_t* k, int n, uint32_t (&k0)[NW], uint32_t (&k1)[NW], uint32_t (&k2)[NW]) {
+#pragma unroll
+  for (int j = 0; j < NW; ++j) {
+    uint32_t a = 0, b = 0, d = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = 4 * j + i;
+      const uint32_t w = t < n ? static_cast<uint32_t>(k[t]) : 0u;
+      a |= (w & 0xffu) << (8 * i);
+      b |= ((w >> 8) & 0xffu) << (8 * i);
+      d |= ((w >> 16) & 0xffu) << (8 * i);
+    }
+    k0[j] = a;
+    k1[j] = b;
+    k2[j] = d;
+  }
+}
+
+// 2^21 plus a window's bytes times its weights: the bytes realigned from the words w[0 .. NW] by
+// the byte permute `sel`, four taps a dp4a on each weight plane.  The three plane sums recombine
+// modulo 2^32 to the integer sum, which is below 255 * 2^22 * (1 + 2^-20) and so exact.
+template <int NW>
+__device__ __forceinline__ int32_t window_sum(const uint32_t (&w)[NW + 1], uint32_t sel, const uint32_t (&k0)[NW],
+                                              const uint32_t (&k1)[NW], const uint32_t (&k2)[NW]) {
+  uint32_t s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+  for (int j = 0; j < NW; ++j) {
+    const uint32_t x = __byte_perm(w[j], w[j + 1], sel);
+    s0 = dp4a_uu(x, k0[j], s0);
+    s1 = dp4a_uu(x, k1[j], s1);
+    s2 = dp4a_uu(x, k2[j], s2);
+  }
+  return (1 << 21) + static_cast<int32_t>(s0 + (s1 << 8) + (s2 << 16));
+}
+
+// Four window sums as the intermediate's bytes: >> 22, saturated to [0, 255] (clip8d).
+__device__ __forceinline__ uint32_t clip8x4(const int32_t* v) {
+  const int32_t c[4] = {v[0] >> 22, v[1] >> 22, v[2] >> 22, v[3] >> 22};
+  return pack_sat_u8x4(c);
+}
+
+// Horizontal pass of one output column over source rows in chunks of 8 (chunk ch: rows
+// top + 8 ch .. + 7), every tap window at most 4 * NW taps and its word reads on the page
+// (checked by the caller).  The column of the intermediate is contiguous (col[r] = row r), so a
+// chunk is stored as two words.  Rows off the page read as paper.  kSameSel: the page's rows
+// are 4-byte aligned, so every row's window has the same byte offset within its first word.
+template <int NW, bool kSameSel>
+__device__ __forceinline__ void hpass(const PageDesc& P, const int32_t* c, int32_t paper, int top, int first, int nchunks,
+                                      int step, uint8_t* col) {
+  const int xmin = c[0], n = c[1];
+  uint32_t k0[NW], k1[NW], k2[NW];
+  weight_planes<NW>(c + 2, n, k0, k1, k2);
+  constexpr int RU = NW <= 2 ? 8 : NW <= 4 ? 4 : 2;  // rows whose loads are in flight together
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(P.data + xmin);
+  const uint32_t sel0 = 0x3210u + static_cast<uint32_t>(a0 & 3) * 0x1111u;
+  const uint32_t* base = reinterpret_cast<const uint32_t*>(a0 & ~uintptr_t(3));
+  const long long wstride = P.stride >> 2;
+  auto row_words = [&](int y, uint32_t (&w)[NW + 1], uint32_t& sel) {
+    const uint32_t* wp;
+    if (kSameSel) {
+      wp = base + static_cast<long long>(y) * wstride;
+      sel = sel0;
+    } else {
+      const uintptr_t a = a0 + static_cast<uintptr_t>(static_cast<long long>(y) * P.stride);
+      wp = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+      sel = 0x3210u + static_cast<uint32_t>(a & 3) * 0x1111u;
+    }
+#pragma unroll
+    for (int j = 0; j <= NW; ++j) w[j] = __ldg(wp + j);
+  };
+  for (int ch = first; ch < nchunks; ch += step) {
+    const int y0 = top + ch * 8;
+    int32_t v[8];
+    if (y0 >= 0 && y0 + 8 <= P.height) {
+#pragma unroll
+      for (int h = 0; h < 8; h += RU) {
+        uint32_t w[RU][NW + 1], sel[RU];
+#pragma unroll
+        for (int q = 0; q < RU; ++q) row_words(y0 + h + q, w[q], sel[q]);
+#pragma unroll
+        for (int q = 0; q < RU; ++q) v[h + q] = window_sum<NW>(w[q], sel[q], k0, k1, k2);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int y = y0 + q;
+        v[q] = (1 << 21) + paper;
+        if (y >= 0 && y < P.height) {
+          uint32_t w[NW + 1], sel;
+          row_words(y, w, sel);
+          v[q] = window_sum<NW>(w, sel, k0, k1, k2);
+        }
+      }
+    }
+    uint32_t* o = reinterpret_cast<uint32_t*>(col + ch * 8);
+    o[0] = clip8x4(v);
+    o[1] = clip8x4(v + 4);
+  }
+}
+
+// Vertical pass of one output column: output rows first, first + step, ... < H, row yy's window
+// at col[vfirst[yy] - top ..), its weight planes at vkp[yy * 24 ..] (k0 | k1 | k2, 8 words
+// each); every window at most 4 * NW taps, and the word reads inside the column's slot.
+template <int NW>
+__device__ __forceinline__ void vpass(const uint8_t* col, const int32_t* vfirst, const uint32_t* vkp, int top, int H,
+                                      int first, int step, uint8_t* out, int qpitch) {
+  for (int yy = first; yy < H; yy += step) {
+    const int f = vfirst[yy] - top;
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(col + (f & ~3));
+    const uint32_t sel = 0x3210u + static_cast<uint32_t>(f & 3) * 0x1111u;
+    uint32_t w[NW + 1], k0[NW], k1[NW], k2[NW];
+#pragma unroll
+    for (int j = 0; j <= NW; ++j) w[j] = wp[j];
+    const uint32_t* k = vkp + yy * 24;
+#pragma unroll
+    for (int j = 0; j < NW; ++j) {
+      k0[j] = k[j];
+      k1[j] = k[8 + j];
+      k2[j] = k[16 + j];
+    }
+    const int32_t v = window_sum<NW>(w, sel, k0, k1, k2) >> 22;
+    out[yy * qpitch] = static_cast<uint8_t>(v < 0 ? 0 : v > 255 ? 255 : v);
+  }
+}
+
 template <bool kInt8>
 __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid_constant__ CropParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
@@ -231,6 +362,7 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
   float* sscale = reinterpret_cast<float*>(sm + S.sscale);
   float* sbias = reinterpret_cast<float*>(sm + S.sbias);
   int32_t* vk = reinterpret_cast<int32_t*>(sm + S.vk);
+  uint32_t* vkp = reinterpret_cast<uint32_t*>(sm + S.vkp);
   int32_t* vfirst = reinterpret_cast<int32_t*>(sm + S.vfirst);
   int32_t* vcount = reinterpret_cast<int32_t*>(sm + S.vcount);
   int32_t* hist = reinterpret_cast<int32_t*>(sm + S.hist);
@@ -288,185 +420,146 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
         }
       }
     }
-    // this line's tap stride (PIL's ksize) and strip width, from a bound on the source rows the
-    // vertical windows span: each window lies within [y0 - support - 1, y1 + support + 1]
-    const double hscale = (L.x1 - L.x0) / cw;
-    const int T = min(kMaxTaps, static_cast<int>(ceil(hscale < 1.0 ? 1.0 : hscale)) * 2 + 1);
+    // this line's tap stride (PIL's ksize), from a bound on the source rows the vertical windows
+    // span (each window lies within [y0 - support - 1, y1 + support + 1]), and the taps a window
+    // has at most: [floor(c - s + 0.5), floor(c + s + 0.5)) holds at most ceil(2 s) + 1 samples
+    // (in words of 4 taps, the dp4a passes' unrolling, uniform over the line; the coefficient
+    // setup checks every window against it)
+    const double hscale = (L.x1 - L.x0) / cw, hsup = hscale < 1.0 ? 1.0 : hscale;
+    const int T = min(kMaxTaps, static_cast<int>(ceil(hsup)) * 2 + 1);
     const double vspan = L.y1 - L.y0, vsup = vspan / H < 1.0 ? 1.0 : vspan / H;
     const int rows_ub = static_cast<int>(ceil(vspan + 2.0 * vsup)) + 4;
-    const int strip = max(16, min(kMaxStripCols, min(kStripBytes / max(rows_ub, 1), kCoefBytes / (4 * (T + 2)))));
-    // vertical coefficients (a thread a row) and the first strip's horizontal ones (a thread a column)
+    const int nwh = (min(kMaxTaps, static_cast<int>(ceil(2.0 * hsup)) + 1) + 3) >> 2;
+    const int nwv = (min(kMaxTaps, static_cast<int>(ceil(2.0 * vsup)) + 1) + 3) >> 2;
+    // the intermediate, column-major: a column of the strip holds its source rows contiguous in
+    // rp bytes (the 8-row chunks, and the vertical windows' word reads, stay inside), rp / 4 odd
+    // so that a warp's columns fall in distinct banks
+    int rp = max((rows_ub + 7) & ~7, rows_ub + 4 * nwv + 4);
+    rp = (rp + 3) & ~3;
+    if (((rp >> 2) & 1) == 0) rp += 4;
+    const int strip = max(16, min(kMaxStripCols, min(kStripBytes / rp, kCoefBytes / (4 * (T + 2)))));
+    // a strip's horizontal coefficients (a thread a column): true where a window does not fit the
+    // dp4a pass (more taps than the bound, or than kMaxHWords words, or its word reads off the page)
+    auto hcoeffs = [&](int x0, int sc) {
+      bool bad = false;
+      for (int xx = tid; xx < sc; xx += nthr) {
+        int32_t* c = hk + xx * (T + 2);
+        int n;
+        c[0] = coeffs(L.x0, L.x1, cw, x0 + xx, c + 2, &n);
+        c[1] = n;
+        bad |= nwh > kMaxHWords || n > 4 * nwh || c[0] < 0 || c[0] + 4 * nwh + 4 > P.width;
+      }
+      return bad;
+    };
+    // vertical coefficients (a thread a row, with their byte planes) and the first strip's
+    // horizontal ones
+    bool vbad_t = false;
     for (int yy = tid; yy < H; yy += nthr) {
       int n;
-      vfirst[yy] = coeffs(L.y0, L.y1, H, yy, vk + yy * kMaxTaps, &n);
+      int32_t* k = vk + yy * kMaxTaps;
+      vfirst[yy] = coeffs(L.y0, L.y1, H, yy, k, &n);
       vcount[yy] = n;
+      vbad_t |= n > 4 * nwv;
+      uint32_t k0[8], k1[8], k2[8];
+      weight_planes<8>(k, n, k0, k1, k2);
+      uint32_t* kp = vkp + yy * 24;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        kp[j] = k0[j];
+        kp[8 + j] = k1[j];
+        kp[16 + j] = k2[j];
+      }
     }
-    for (int xx = tid; xx < min(strip, cw); xx += nthr) {
-      int32_t* c = hk + xx * (T + 2);
-      int n;
-      c[0] = coeffs(L.x0, L.x1, cw, xx, c + 2, &n);
-      c[1] = n;
-    }
-    __syncthreads();
+    const bool hbad_t = hcoeffs(0, min(strip, cw));
+    const bool vbad = __syncthreads_or(vbad_t) != 0;
+    bool hbad = __syncthreads_or(hbad_t) != 0;
     const int top = vfirst[0];
     const int rows = vfirst[H - 1] + vcount[H - 1] - top;
-    if (rows > kMaxSrcRows || rows > rows_ub) {
+    if (rows > kMaxSrcRows || rows > rows_ub || strip * rp > kStripBytes) {
       if (tid == 0) atomicCAS(p.err, 0, kErrBadShape);
       return;
     }
+    const int nchunks = (rows + 7) >> 3;
+    const bool same_sel = (P.stride & 3) == 0;
     for (int x0 = 0; x0 < cw; x0 += strip) {
       const int sc = min(strip, cw - x0);
       if (x0 > 0) {
         __syncthreads();  // the previous strip's vertical pass has read tmp and hk
-        for (int xx = tid; xx < sc; xx += nthr) {
-          int32_t* c = hk + xx * (T + 2);
-          int n;
-          c[0] = coeffs(L.x0, L.x1, cw, x0 + xx, c + 2, &n);
-          c[1] = n;
-        }
-        __syncthreads();
+        hbad = __syncthreads_or(hcoeffs(x0, sc)) != 0;
       }
       // a thread a column of the strip, the rows split into groups when the strip is narrow
       const int groups = max(1, nthr / sc);
       const int rg = tid / sc, xx = tid - rg * sc;
       if (rg < groups) {
-        // horizontal pass: every source row the vertical windows read.  Up to 16 taps the weights
-        // (non-negative, at most 2^22) split into three byte planes, and a row's taps are summed
-        // four at a time with dp4a on the source words realigned by a byte permute: the same
-        // integer sum.  Reads stay inside the row: from 3 bytes before xmin to 17 after.
+        // horizontal pass: every source row the vertical windows read, 8-row chunks split over
+        // the row groups
         const int32_t* c = hk + xx * (T + 2);
         const int xmin = c[0], n = c[1];
-        const bool inside = xmin >= 0 && xmin + n <= P.width;
-        const bool planes = n <= 16 && xmin >= 3 && xmin + 17 <= P.width;
-        const int nw = (n + 3) >> 2;  // words of taps
-        uint32_t k0[4] = {0, 0, 0, 0}, k1[4] = {0, 0, 0, 0}, k2[4] = {0, 0, 0, 0};
         int32_t paper = 0;  // a row off the page: 255 * the weights' sum
         for (int t = 0; t < n; ++t) paper += 255 * c[2 + t];
-        if (planes) {
-#pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            const uint32_t k = t < n ? static_cast<uint32_t>(c[2 + t]) : 0u;
-            k0[t >> 2] |= (k & 0xffu) << (8 * (t & 3));
-            k1[t >> 2] |= ((k >> 8) & 0xffu) << (8 * (t & 3));
-            k2[t >> 2] |= ((k >> 16) & 0xffu) << (8 * (t & 3));
+        uint8_t* col = tmp + xx * rp;
+        if (!hbad) {
+#define CREC_HPASS(NW)                                                                  \
+  case NW:                                                                              \
+    if (same_sel) hpass<NW, true>(P, c, paper, top, rg, nchunks, groups, col);          \
+    else hpass<NW, false>(P, c, paper, top, rg, nchunks, groups, col);                  \
+    break;
+          switch (nwh) {
+            CREC_HPASS(1)
+            CREC_HPASS(2)
+            CREC_HPASS(3)
+            CREC_HPASS(4)
+            CREC_HPASS(5)
+            CREC_HPASS(6)
           }
-        }
-        // rows several at a time in the common case (all of them on the page), their loads in
-        // flight together: 8 rows for up to 8 taps, 3 rows for up to 12
-        int r = rg;
-        if (planes && nw <= 2 && (P.stride & 3) == 0) {
-          // word-aligned rows: every row's first tap word has the same byte offset
-          constexpr int RU = 8;
-          const uintptr_t a0 = reinterpret_cast<uintptr_t>(P.data + xmin);
-          const uint32_t sel = 0x3210u + static_cast<uint32_t>(a0 & 3) * 0x1111u;
-          const uint32_t* base = reinterpret_cast<const uint32_t*>(a0 & ~uintptr_t(3));
-          const long long wstride = P.stride >> 2;  // words a row
-          for (; r + (RU - 1) * groups < rows; r += RU * groups) {
-            const int y0 = top + r;
-            if (y0 < 0 || y0 + (RU - 1) * groups >= P.height) break;
-            uint32_t w[RU][3];
-            const uint32_t* wp = base + static_cast<long long>(y0) * wstride;
-            const long long step = static_cast<long long>(groups) * wstride;
-#pragma unroll
-            for (int q = 0; q < RU; ++q, wp += step) {
-              w[q][0] = __ldg(wp);
-              w[q][1] = __ldg(wp + 1);
-              w[q][2] = nw == 2 ? __ldg(wp + 2) : 0u;
-            }
-#pragma unroll
-            for (int q = 0; q < RU; ++q) {
-              uint32_t s0 = 0, s1 = 0, s2 = 0;
-#pragma unroll
-              for (int j = 0; j < 2; ++j) {
-                if (j < nw) {
-                  const uint32_t x = __byte_perm(w[q][j], w[q][j + 1], sel);
-                  s0 = dp4a_uu(x, k0[j], s0);
-                  s1 = dp4a_uu(x, k1[j], s1);
-                  s2 = dp4a_uu(x, k2[j], s2);
-                }
-              }
-              tmp[(r + q * groups) * strip + xx] = clip8d((1 << 21) + static_cast<int32_t>(s0 + (s1 << 8) + (s2 << 16)));
-            }
-          }
-        }
-        if (planes && nw <= 3) {
-          constexpr int RU = 3;
-          for (; r + (RU - 1) * groups < rows; r += RU * groups) {
-            const int y0 = top + r;
-            if (y0 < 0 || y0 + (RU - 1) * groups >= P.height) break;
-            uint32_t w[RU][4];
-            uint32_t sel[RU];
-#pragma unroll
-            for (int q = 0; q < RU; ++q) {
-              const uintptr_t a = reinterpret_cast<uintptr_t>(P.data + static_cast<long long>(y0 + q * groups) * P.stride + xmin);
-              const uint32_t* wp = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-              sel[q] = 0x3210u + static_cast<uint32_t>(a & 3) * 0x1111u;
-#pragma unroll
-              for (int j = 0; j < 4; ++j) w[q][j] = j <= nw ? __ldg(wp + j) : 0u;
-            }
-#pragma unroll
-            for (int q = 0; q < RU; ++q) {
-              uint32_t s0 = 0, s1 = 0, s2 = 0;
-#pragma unroll
-              for (int j = 0; j < 3; ++j) {
-                if (j < nw) {
-                  const uint32_t x = __byte_perm(w[q][j], w[q][j + 1], sel[q]);
-                  s0 = dp4a_uu(x, k0[j], s0);
-                  s1 = dp4a_uu(x, k1[j], s1);
-                  s2 = dp4a_uu(x, k2[j], s2);
-                }
-              }
-              tmp[(r + q * groups) * strip + xx] = clip8d((1 << 21) + static_cast<int32_t>(s0 + (s1 << 8) + (s2 << 16)));
-            }
-          }
-        }
-        for (; r < rows; r += groups) {
-          const int y = top + r;
-          int32_t ss = 1 << 21;
-          if (y >= 0 && y < P.height) {
-            const uint8_t* src = P.data + static_cast<long long>(y) * P.stride + xmin;
-            if (planes) {
-              const uintptr_t a = reinterpret_cast<uintptr_t>(src);
-              const uint32_t* wp = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-              const uint32_t sel = 0x3210u + static_cast<uint32_t>(a & 3) * 0x1111u;
-              uint32_t w[5];
-              w[0] = __ldg(wp);
-#pragma unroll
-              for (int j = 1; j < 5; ++j) w[j] = j <= nw ? __ldg(wp + j) : 0u;
-              uint32_t s0 = 0, s1 = 0, s2 = 0;
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                if (j < nw) {
-                  const uint32_t x = __byte_perm(w[j], w[j + 1], sel);
-                  s0 = dp4a_uu(x, k0[j], s0);
-                  s1 = dp4a_uu(x, k1[j], s1);
-                  s2 = dp4a_uu(x, k2[j], s2);
-                }
-              }
-              ss += static_cast<int32_t>(s0 + (s1 << 8) + (s2 << 16));
-            } else if (inside) {
-              for (int t = 0; t < n; ++t) ss += static_cast<int32_t>(__ldg(src + t)) * c[2 + t];
-            } else {
+#undef CREC_HPASS
+        } else {
+          // a window off the page's edge (pixels there read as paper) or wider than the bound
+          for (int r = rg; r < rows; r += groups) {
+            const int y = top + r;
+            int32_t ss = 1 << 21;
+            if (y >= 0 && y < P.height) {
+              const uint8_t* src = P.data + static_cast<long long>(y) * P.stride + xmin;
               for (int t = 0; t < n; ++t) {
-                const int x = xmin + t;  // pixels off the page read as paper
+                const int x = xmin + t;
                 ss += ((x >= 0 && x < P.width) ? static_cast<int32_t>(__ldg(src + t)) : 255) * c[2 + t];
               }
+            } else {
+              ss += paper;
             }
-          } else {
-            ss += paper;
+            col[r] = clip8d(ss);
           }
-          tmp[r * strip + xx] = clip8d(ss);
         }
       }
       __syncthreads();
       if (rg < groups) {
         // vertical pass: the strip's output pixels
-        for (int yy = rg; yy < H; yy += groups) {
-          const int f = vfirst[yy] - top, n = vcount[yy];
-          const int32_t* k = vk + yy * kMaxTaps;
-          int32_t ss = 1 << 21;
-          for (int t = 0; t < n; ++t) ss += tmp[(f + t) * strip + xx] * k[t];
-          px(yy, x0 + xx) = clip8d(ss);
+        const uint8_t* col = tmp + xx * rp;
+        uint8_t* out = &px(0, x0 + xx);
+        if (!vbad) {
+#define CREC_VPASS(NW) \
+  case NW:             \
+    vpass<NW>(col, vfirst, vkp, top, H, rg, groups, out, qpitch); \
+    break;
+          switch (nwv) {
+            CREC_VPASS(1)
+            CREC_VPASS(2)
+            CREC_VPASS(3)
+            CREC_VPASS(4)
+            CREC_VPASS(5)
+            CREC_VPASS(6)
+            CREC_VPASS(7)
+            CREC_VPASS(8)
+          }
+#undef CREC_VPASS
+        } else {
+          for (int yy = rg; yy < H; yy += groups) {
+            const int f = vfirst[yy] - top, n = vcount[yy];
+            const int32_t* k = vk + yy * kMaxTaps;
+            int32_t ss = 1 << 21;
+            for (int t = 0; t < n; ++t) ss += col[f + t] * k[t];
+            out[yy * qpitch] = clip8d(ss);
+          }
         }
       }
     }

@@ -230,6 +230,18 @@ __device__ __forceinline__ float magic_to_float(int32_t biased) { return __fsub_
 // rint(x) + kMagicBits for |x| <= 2^22 (round to nearest, ties to even, as __float2int_rn).
 __device__ __forceinline__ int32_t magic_rint_bits(float x) { return __float_as_int(__fadd_rn(x, kMagic)); }
 
+// Bytes hi and lo, each saturated to [0, 255], above them the low 16 bits of `upper`:
+// upper << 16 | sat(hi) << 8 | sat(lo) (PTX cvt.pack.sat.u8.s32.b32).
+__device__ __forceinline__ uint32_t pack_sat_u8x2(int32_t hi, int32_t lo, uint32_t upper) {
+  uint32_t d;
+  asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(hi), "r"(lo), "r"(upper));
+  return d;
+}
+// Four codes as bytes (c[0] lowest), each saturated to [0, 255].
+__device__ __forceinline__ uint32_t pack_sat_u8x4(const int32_t* c) {
+  return pack_sat_u8x2(c[1], c[0], pack_sat_u8x2(c[3], c[2], 0u));
+}
+
 // 2^x, the hardware approximation (PTX ex2.approx.ftz.f32); 2^-inf = 0.
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

@@ -156,6 +156,48 @@ def test_pages_crops_and_ctc_bit_exact(rec_latin, orc, rule):
         assert np.array_equal(got[i].probs.view(np.int32), pr.view(np.int32))
 
 
+def tall_pages(seed=11):
+    """Pages whose rows are not 4-byte aligned (odd widths) and lines up to 300 px tall: windows of
+    3 to 19 taps each way (downscales to ~13x), boxes over every page edge."""
+    rng = np.random.default_rng(seed)
+    pages, boxes, page_of = [], [], []
+    for p, (w, h) in enumerate(((2481, 1803), (1203, 2999))):
+        page = np.clip(rng.normal(228, 12, (h, w)), 0, 255).astype(np.uint8)
+        for _ in range(600):
+            x, y = int(rng.integers(0, w - 40)), int(rng.integers(0, h - 40))
+            page[y:y + int(rng.integers(4, 40)), x:x + int(rng.integers(2, 16))] = int(rng.integers(0, 90))
+        pages.append(page)
+        k = 0
+        while k < 90:
+            bh = rng.uniform(20, 300)
+            x0, y0 = rng.uniform(-60, w - 30), rng.uniform(-80, h - 20)
+            bw = rng.uniform(30, 2400)
+            if (bw + 0.6 * bh) * 32 / (1.4 * bh) > 1000:
+                continue
+            boxes.append([x0, y0, x0 + bw, y0 + bh])
+            page_of.append(p)
+            k += 1
+    return pages, np.asarray(boxes), np.asarray(page_of, np.int32)
+
+
+def test_tall_lines_and_odd_strides_crop_bit_exact(rec_latin, orc):
+    pages, boxes, page_of = tall_pages()
+    dev = native.RecDevice(rec_latin[0].to_blob(), native.INT8, max_lines=256, max_width=1024, max_pages=4)
+    try:
+        dev.set_pages(pages)
+        dev.arm_crops(1024)
+        dev.recognize(page_of, boxes, 1024)
+        crops = dev.crops(len(boxes), 1024)
+    finally:
+        dev.close()
+    ocr = O.CropRule.default()
+    for p in range(2):
+        sel = np.nonzero(page_of == p)[0]
+        want, _ = orc.crop_lines(pages[p], boxes[sel], 1024, ocr)
+        for j, i in enumerate(sel):
+            assert np.array_equal(crops[i], want[j]), (p, int(i), boxes[i])
+
+
 def test_scheduler_runs_are_independent_of_grouping(rec_latin):
     """Lines of several pages at their ladder buckets, cut into many runs (a small column budget) or
     one: the same decodings, each line's also the same as when it is read alone."""
