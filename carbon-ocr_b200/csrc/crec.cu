@@ -447,6 +447,24 @@ int upload_offsets(crec_handle* h, Layer& l, int zero, const std::vector<int32_t
   return upload(h, &l.hoff, off);
 }
 
+// Whether an INT8 layer's output stage may round before it clamps: the value before the clamp,
+// v * inv_scale, bounded from the weights (|v| <= sum |w| * reach * scale + |bias| + 255 *
+// residual scale, with a margin for the roundings) below 2^21, where the magic rounding is exact
+// and clamping after rounding gives the same code (the bounds are integers).
+bool round_first(const crec_handle* h, const Layer& l, const Value& x, const Value& y, const std::vector<float>& scale,
+                 const std::vector<float>& bias) {
+  const double reach = std::max(x.zero, 255 - x.zero);
+  const double rs = l.residual >= 0 ? 255.0 * std::fabs(h->v[l.residual].scale) : 0.0;
+  const size_t per = l.w8.size() / static_cast<size_t>(l.cout);
+  double worst = 0.0;
+  for (int j = 0; j < l.cout; ++j) {
+    double a = 0.0;
+    for (size_t k = 0; k < per; ++k) a += std::abs(static_cast<int>(l.w8[j * per + k]));
+    worst = std::max(worst, a * reach * std::fabs(scale[j]) + std::fabs(bias[j]) + rs);
+  }
+  return worst * 1.01 * std::fabs(1.0 / y.scale) < static_cast<double>(1 << 21);
+}
+
 int setup_layer(crec_handle* h, size_t li) {
   Layer& l = h->l[li];
   if (l.kind == kKindResize) return CREC_OK;
@@ -473,6 +491,7 @@ int setup_layer(crec_handle* h, size_t li) {
     return rc;
   if (li == 0) {  // the stem: [cout][taps]
     if (h->int8) {
+      l.sat = round_first(h, l, x, y, scale, bias);  // the stem's sums always fit the magic conversions
       if ((rc = upload(h, &l.dw8, l.w8))) return rc;
     } else {
       std::vector<float> wf(l.wf.size());
@@ -554,21 +573,7 @@ int setup_layer(crec_handle* h, size_t li) {
     l.stages = std::min<int>(8, (200 * 1024) / l.stage_bytes);
     l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 2 * kMaxAcc) * 8 + 16 + 12 * y.cp + 64;
     if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, y.cp))) return rc;
-    // the output stage's value before the clamp, v * inv_scale, bounded from the weights: with
-    // |v| <= sum |w| * reach * scale + |bias| + 255 * residual scale (and a margin for the
-    // roundings) below 2^21, rounding first and clamping after gives the same code
-    if (h->int8 && l.fast) {
-      const double reach = std::max(x.zero, 255 - x.zero);
-      const double rs = l.residual >= 0 ? 255.0 * std::fabs(h->v[l.residual].scale) : 0.0;
-      const size_t per = l.w8.size() / static_cast<size_t>(l.cout);
-      double worst = 0.0;
-      for (int j = 0; j < l.cout; ++j) {
-        double a = 0.0;
-        for (size_t k = 0; k < per; ++k) a += std::abs(static_cast<int>(l.w8[j * per + k]));
-        worst = std::max(worst, a * reach * std::fabs(scale[j]) + std::fabs(bias[j]) + rs);
-      }
-      l.sat = worst * 1.01 * std::fabs(1.0 / y.scale) < static_cast<double>(1 << 21);
-    }
+    if (h->int8 && l.fast) l.sat = round_first(h, l, x, y, scale, bias);
   }
   const std::vector<uint8_t> img = weight_image(h, l, x.cp, l.nt, l.n_tiles, l.nkb);
   if ((rc = upload(h, &l.wimg, img))) return rc;
@@ -706,6 +711,8 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.in_zero = x0.zero;
     p.out_zero = s0.zero;
     p.relu = stem.relu;
+    p.sat = stem.sat;
+    p.code_lo = stem.relu ? s0.zero : 0;
     p.out_inv_scale = h->int8 ? 1.0f / s0.scale : 1.0f;
     p.out = s0.base;
     p.out_ph = s0.ph;

@@ -20,6 +20,7 @@
 #include <cuda_fp16.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "sm100.cuh"
 
@@ -32,7 +33,7 @@ constexpr int kCoefBytes = 16 << 10;   // a strip's horizontal coefficients: col
 constexpr int kMaxStripCols = 256;    // output columns a strip at most (two row groups keep all 512 threads busy)
 constexpr int kMaxSrcRows = 1024;     // source rows a crop's vertical windows may span (the host checks)
 constexpr int kStemMaxOut = 64;       // the stem's output channels at most (padded)
-constexpr int kMaxHWords = 6;         // horizontal windows of up to 24 taps in the dp4a pass (wider: the generic one)
+constexpr int kMaxHWords = 5;         // horizontal windows of up to 20 taps in the dp4a pass (wider: the generic one)
 
 struct PageDesc {
   const uint8_t* data;
@@ -66,6 +67,8 @@ struct CropParams {
   const int32_t* colsum;  // [cout] sum of each output channel's int8 weights
   const uint8_t* in_table;  // [256] the INT8 input table
   int in_zero, out_zero, relu;
+  int sat;      // INT8: |v * inv_scale| < 2^21 for every output (round, then clamp while packing)
+  int code_lo;  // the lowest code: the zero point after a ReLU, else 0
   float out_inv_scale;
   uint8_t* out;  // stem tensor's first row
   int out_ph;
@@ -405,18 +408,23 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
   bool flip = false;
   uint8_t ground = 0;
   if (!p.crops_in) {
-    // the source region into L2 first (every 128-byte line of the rows and columns the filters'
-    // windows can reach): DRAM streams it in while the coefficients are computed
+    // the source region into L2 first (the rows and columns the filters' windows can reach), a
+    // bulk prefetch a row (the copy engine streams it in from DRAM while the coefficients are
+    // computed; no thread waits on it), each range rounded to 16 bytes inside the page's buffer
     {
       const double vsup = (L.y1 - L.y0) / H < 1.0 ? 1.0 : (L.y1 - L.y0) / H;
       const double hsup = (L.x1 - L.x0) / cw < 1.0 ? 1.0 : (L.x1 - L.x0) / cw;
       const int ylo = max(0, static_cast<int>(floor(L.y0 - vsup)) - 2), yhi = min(P.height, static_cast<int>(ceil(L.y1 + vsup)) + 2);
       const int xlo = max(0, static_cast<int>(floor(L.x0 - hsup)) - 2), xhi = min(P.width, static_cast<int>(ceil(L.x1 + hsup)) + 2);
-      if (yhi > ylo && xhi > xlo) {
-        const int per_row = (xhi - xlo + 127) / 128 + 1;
-        for (int i = tid; i < (yhi - ylo) * per_row; i += nthr) {
-          const int y = ylo + i / per_row, x = min(xhi - 1, xlo + (i % per_row) * 128);
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(P.data + static_cast<long long>(y) * P.stride + x));
+      if (xhi > xlo) {
+        const uintptr_t first = reinterpret_cast<uintptr_t>(P.data);
+        const uintptr_t last = first + static_cast<uintptr_t>(static_cast<long long>(P.height - 1) * P.stride + P.width);
+        for (int y = ylo + tid; y < yhi; y += nthr) {
+          const uintptr_t row = first + static_cast<uintptr_t>(static_cast<long long>(y) * P.stride);
+          uintptr_t a = (row + xlo) & ~uintptr_t(15), b = (row + xhi + 15) & ~uintptr_t(15);
+          if (a < first) a += 16;
+          if (b > last) b -= 16;
+          if (b > a) l2_prefetch_bulk(reinterpret_cast<const void*>(a), static_cast<uint32_t>(b - a));
         }
       }
     }
@@ -438,23 +446,27 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
     rp = (rp + 3) & ~3;
     if (((rp >> 2) & 1) == 0) rp += 4;
     const int strip = max(16, min(kMaxStripCols, min(kStripBytes / rp, kCoefBytes / (4 * (T + 2)))));
-    // a strip's horizontal coefficients (a thread a column): true where a window does not fit the
-    // dp4a pass (more taps than the bound, or than kMaxHWords words, or its word reads off the page)
-    auto hcoeffs = [&](int x0, int sc) {
-      bool bad = false;
-      for (int xx = tid; xx < sc; xx += nthr) {
+    // horizontal coefficients (a thread a column) of `count` columns from x0: hk holds ncoef
+    // columns' (at least a strip's; a line's whole width when it fits, so that the strips after
+    // the first do not wait on the double-precision setup)
+    const int ncoef = kCoefBytes / (4 * (T + 2));
+    auto hcoeffs = [&](int x0, int count) {
+      for (int xx = tid; xx < count; xx += nthr) {
         int32_t* c = hk + xx * (T + 2);
         int n;
         c[0] = coeffs(L.x0, L.x1, cw, x0 + xx, c + 2, &n);
         c[1] = n;
-        bad |= nwh > kMaxHWords || n > 4 * nwh || c[0] < 0 || c[0] + 4 * nwh + 4 > P.width;
       }
-      return bad;
     };
-    // vertical coefficients (a thread a row, with their byte planes) and the first strip's
-    // horizontal ones
+    // a window that does not fit the dp4a pass: more taps than the bound (or than kMaxHWords
+    // words), or its word reads off the page
+    auto hbad_of = [&](const int32_t* c) {
+      return nwh > kMaxHWords || c[1] > 4 * nwh || c[0] < 0 || c[0] + 4 * nwh + 4 > P.width;
+    };
+    // vertical coefficients (rows from the last thread down, with their byte planes) and the
+    // first block of horizontal ones (columns from thread 0 up)
     bool vbad_t = false;
-    for (int yy = tid; yy < H; yy += nthr) {
+    for (int yy = nthr - 1 - tid; yy < H; yy += nthr) {
       int n;
       int32_t* k = vk + yy * kMaxTaps;
       vfirst[yy] = coeffs(L.y0, L.y1, H, yy, k, &n);
@@ -470,9 +482,9 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
         kp[16 + j] = k2[j];
       }
     }
-    const bool hbad_t = hcoeffs(0, min(strip, cw));
+    hcoeffs(0, min(cw, ncoef));
+    int xc0 = 0;  // the first column hk holds
     const bool vbad = __syncthreads_or(vbad_t) != 0;
-    bool hbad = __syncthreads_or(hbad_t) != 0;
     const int top = vfirst[0];
     const int rows = vfirst[H - 1] + vcount[H - 1] - top;
     if (rows > kMaxSrcRows || rows > rows_ub || strip * rp > kStripBytes) {
@@ -483,17 +495,21 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
     const bool same_sel = (P.stride & 3) == 0;
     for (int x0 = 0; x0 < cw; x0 += strip) {
       const int sc = min(strip, cw - x0);
-      if (x0 > 0) {
-        __syncthreads();  // the previous strip's vertical pass has read tmp and hk
-        hbad = __syncthreads_or(hcoeffs(x0, sc)) != 0;
+      if (x0 + sc > xc0 + ncoef) {
+        __syncthreads();  // the previous strip's passes are done with hk
+        xc0 = x0;
+        hcoeffs(x0, min(cw - x0, ncoef));
+        __syncthreads();
       }
       // a thread a column of the strip, the rows split into groups when the strip is narrow
       const int groups = max(1, nthr / sc);
       const int rg = tid / sc, xx = tid - rg * sc;
+      const int32_t* c = hk + (x0 - xc0 + xx) * (T + 2);
+      // (also: the previous strip's vertical pass is done with tmp)
+      const bool hbad = __syncthreads_or(rg < groups && hbad_of(c)) != 0;
       if (rg < groups) {
         // horizontal pass: every source row the vertical windows read, 8-row chunks split over
         // the row groups
-        const int32_t* c = hk + xx * (T + 2);
         const int xmin = c[0], n = c[1];
         int32_t paper = 0;  // a row off the page: 255 * the weights' sum
         for (int t = 0; t < n; ++t) paper += 255 * c[2 + t];
@@ -510,7 +526,6 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
             CREC_HPASS(3)
             CREC_HPASS(4)
             CREC_HPASS(5)
-            CREC_HPASS(6)
           }
 #undef CREC_HPASS
         } else {
@@ -618,6 +633,52 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
     const uint8_t* src = p.crops_in ? p.crops_in + static_cast<long long>(line) * H * p.crops_in_pitch : nullptr;
     uint8_t* dst = p.crops_out ? p.crops_out + static_cast<long long>(line) * H * p.crops_pitch : nullptr;
     const uint8_t zq = static_cast<uint8_t>(p.in_zero);
+    if (!src && !dst) {
+      // a thread a word (4 columns) of qb's rows: the flip a XOR, the INT8 input table a byte at
+      // a time; words across the border, the pad or the crop's right edge byte by byte
+      // item i: row i / wpr, word i % wpr (the quotient a multiply-high by 2^32 / wpr rounded up,
+      // exact while i * wpr < 2^32)
+      const int wpr = qpitch >> 2;
+      const uint32_t inv = static_cast<uint32_t>(0xffffffffu / static_cast<uint32_t>(wpr)) + 1u;
+      const uint32_t fx = flip ? 0xffffffffu : 0u;
+      for (int i = tid; i < (H + 4) * wpr; i += nthr) {
+        const int r = static_cast<int>(__umulhi(static_cast<uint32_t>(i), inv)), w4 = i - r * wpr;
+        const int x0 = 4 * w4 - 4;
+        {
+          const int y = r - 2;
+          uint32_t* qw = reinterpret_cast<uint32_t*>(qb + r * qpitch) + w4;
+          if (y < 0 || y >= H || x0 + 3 < 0 || x0 >= bw) {
+            if (kInt8) *qw = static_cast<uint32_t>(zq) * 0x01010101u;
+            continue;
+          }
+          const uint32_t old = *qw;
+          uint32_t v = 0;
+          if (x0 >= 0 && x0 + 3 < cw) {
+            const uint32_t f = old ^ fx;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t b = (f >> (8 * k)) & 0xffu;
+              v |= static_cast<uint32_t>(kInt8 ? stab[b] : b) << (8 * k);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int x = x0 + k;
+              uint32_t b;
+              if (x < 0 || x >= bw) {
+                b = kInt8 ? zq : (old >> (8 * k)) & 0xffu;
+              } else {
+                const uint32_t pix = x >= cw ? ground : ((old >> (8 * k)) & 0xffu) ^ (fx & 0xffu);
+                b = kInt8 ? stab[pix] : pix;
+              }
+              v |= b << (8 * k);
+            }
+          }
+          *qw = v;
+        }
+      }
+    } else {
+      // tests (the finished crops copied out) and crops given ready: a thread a column of qb
     for (int c = tid; c < qpitch; c += nthr) {
       const int x = c - 4;
       const bool col_in = x >= 0 && x < bw;
@@ -635,6 +696,7 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
         if (dst && x < p.crops_pitch) dst[y * p.crops_pitch + x] = v;
         q = kInt8 ? stab[v] : v;
       }
+    }
     }
   }
   __syncthreads();
@@ -673,7 +735,10 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
           }
       }
       // sum over taps of (a - zero) * w = dp4a(a, w) - zero * colsum, exact in int32; then the
-      // output stage with exact conversions (kMagic)
+      // output stage with exact conversions (kMagic), rounded before the clamp where the host's
+      // bound allows (the clamp is then the saturating byte pack)
+      auto channels = [&](auto round_first) {
+      constexpr bool kRound = decltype(round_first)::value;
       for (int c16 = 0; c16 < p.cp_out; c16 += 16) {
         uint32_t wv[4];
 #pragma unroll
@@ -694,13 +759,17 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
             acc = dp4a_us(a[1], w[3 * u + 1], acc);
             acc = dp4a_us(a[2], w[3 * u + 2], acc);
             const float v = __fadd_rn(__fmul_rn(magic_to_float(acc), ss[u]), bb[u]);
-            const float q = fminf(fmaxf(__fmul_rn(v, p.out_inv_scale), lo), hi);
-            code[u] = magic_rint_bits(q) + zc;
+            const float q0 = __fmul_rn(v, p.out_inv_scale);
+            code[u] = magic_rint_bits(kRound ? q0 : fminf(fmaxf(q0, lo), hi)) + zc;
+            if (kRound && p.code_lo > 0) code[u] = max(code[u], p.code_lo);
           }
-          wv[c4] = __byte_perm(__byte_perm(code[0], code[1], 0x0040), __byte_perm(code[2], code[3], 0x0040), 0x5410);
+          wv[c4] = pack_sat_u8x4(code);
         }
         *reinterpret_cast<uint4*>(dst + c16) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
       }
+      };
+      if (p.sat) channels(std::true_type{});
+      else channels(std::false_type{});
     } else {
       float in[9];
 #pragma unroll

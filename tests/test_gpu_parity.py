@@ -122,6 +122,24 @@ def two_pages(seed=7):
     return pages, np.asarray(boxes), np.asarray(page_of, np.int32)
 
 
+def decodings_without_crop_copies(blob, pages, page_of, boxes, **kw):
+    """The same run on a device that does not keep its finished crops (the crop kernel's final
+    pass then works a word at a time)."""
+    dev = native.RecDevice(blob, native.INT8, max_lines=512, max_width=1024, max_pages=4, **kw)
+    try:
+        dev.set_pages(pages)
+        return dev.recognize(page_of, boxes, 1024)
+    finally:
+        dev.close()
+
+
+def assert_same_decodings(a, la, b, lb):
+    for i in range(len(a)):
+        assert la[i] == lb[i], i
+        assert np.array_equal(a[i].ids, b[i].ids) and np.array_equal(a[i].frames, b[i].frames), i
+        assert np.array_equal(a[i].probs.view(np.int32), b[i].probs.view(np.int32)), i
+
+
 @pytest.mark.parametrize("rule", [{}, {"flip_margin": 0}])
 def test_pages_crops_and_ctc_bit_exact(rec_latin, orc, rule):
     pages, boxes, page_of = two_pages()
@@ -154,6 +172,8 @@ def test_pages_crops_and_ctc_bit_exact(rec_latin, orc, rule):
         ids, fr, pr = lines[j]
         assert np.array_equal(got[i].ids, ids) and np.array_equal(got[i].frames, fr)
         assert np.array_equal(got[i].probs.view(np.int32), pr.view(np.int32))
+    got2, lengths2 = decodings_without_crop_copies(rec_latin[0].to_blob(), pages, page_of, boxes, crop=crop_rule)
+    assert_same_decodings(got, lengths, got2, lengths2)
 
 
 def tall_pages(seed=11):
@@ -186,10 +206,12 @@ def test_tall_lines_and_odd_strides_crop_bit_exact(rec_latin, orc):
     try:
         dev.set_pages(pages)
         dev.arm_crops(1024)
-        dev.recognize(page_of, boxes, 1024)
+        got, lengths = dev.recognize(page_of, boxes, 1024)
         crops = dev.crops(len(boxes), 1024)
     finally:
         dev.close()
+    got2, lengths2 = decodings_without_crop_copies(rec_latin[0].to_blob(), pages, page_of, boxes)
+    assert_same_decodings(got, lengths, got2, lengths2)
     ocr = O.CropRule.default()
     for p in range(2):
         sel = np.nonzero(page_of == p)[0]
