@@ -21,9 +21,10 @@
 // ReLU, * inv_scale, clamped to [-zero, 255 - zero], rounded half to even, + zero.
 // FP16: A and B float16, FP32 sums; bias, residual and ReLU in FP32, stored as float16.
 //
-// Warp roles (10 warps): 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-9 epilogue: warps 2-5
-// take the CTA's even tiles, warps 6-9 its odd ones, each warp the 32 TMEM lanes (pixels) of its
-// quarter (its warp index mod 4) and all of a tile's channels.  Up to eight accumulators in TMEM
+// Warp roles (18 warps): 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-17 epilogue: a tile
+// is taken by eight warps (warps 2-5 and 10-13 the CTA's even tiles, 6-9 and 14-17 its odd ones),
+// each warp the 32 TMEM lanes (pixels) of its quarter (its warp index mod 4) and half of the
+// tile's channel groups (2-9 the first half, 10-17 the second).  Up to eight accumulators in TMEM
 // (512 columns over the tile's N rounded up to a power of two), so the MMA runs ahead of the
 // epilogue.  The epilogue is where an INT8 layer's time goes (requantizing 128 x N outputs costs
 // more CUDA-core cycles than the tensor cores' MMAs for K below ~700): the per-channel constants
@@ -80,7 +81,7 @@ struct ConvParams {
   int* err;
 };
 
-constexpr int kConvThreads = 320;
+constexpr int kConvThreads = 576;
 constexpr int kMaxAcc = 8;
 constexpr uint32_t kTmemCols = 512;
 
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     }
     for (int a = 0; a < kMaxAcc; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 4);  // the four warps of the half that takes the tile
+      mbar_init(&tmem_empty[a], 8);  // the eight warps of the half that takes the tile
     }
     fence_mbar_init();
   }
@@ -216,10 +217,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     }
   } else {
     // ---------------------------------------------------------------- epilogue
-    const int quarter = warp & 3;      // the TMEM lanes this warp may read
-    const int half = (warp - 2) >> 2;  // the CTA's even (0) or odd (1) tiles
+    const int quarter = warp & 3;           // the TMEM lanes this warp may read
+    const int half = ((warp - 2) >> 2) & 1;  // the CTA's even (0) or odd (1) tiles
+    const int part = (warp - 2) >> 3;       // the first (0) or second (1) part of a tile's channel groups
     const int row = quarter * 32 + lane;
     const int groups = p.nt / 16;
+    // the part's 16-channel groups: [g0, g1) (the first part an even count: whole 32-column loads)
+    const int gsplit = ((groups + 3) >> 2) << 1;
+    const int g0 = part ? min(gsplit, groups) : 0, g1 = part ? groups : min(gsplit, groups);
     const float lo = p.relu ? 0.0f : static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
     const int32_t zc = p.out_zero - kMagicBits, rzc = kMagicBits - p.res_zero;
     const uint32_t zb = static_cast<uint32_t>(p.out_zero) * 0x01010101u;
@@ -363,34 +368,26 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
           *reinterpret_cast<uint4*>(dst + cb * 2 + 16) = *reinterpret_cast<const uint4*>(o + 8);
         }
       };
-      // TMEM read 32 columns at a time, the next load in flight while the current is stored; the
-      // accumulator goes back to the MMA as soon as its last load has completed
+      // TMEM read 32 columns at a time (the other warps on the SM hide the loads' latency); the
+      // accumulator goes back to the MMA as soon as the part's last load has completed (a warp
+      // without groups still waits for the accumulator, so that its arrival counts for this use)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc) * acc_cols;
-      uint32_t ra[32], rb[32];
-      if (groups >= 2) tmem_ld32(taddr, ra); else tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(ra));
-      tmem_wait_ld();
-      tmem_pin(ra);
-      for (int g = 0; g < groups;) {
-        const int w = g + 1 < groups ? 2 : 1;
-        const int gn = g + w;
-        if (gn + 1 < groups) {
-          tmem_ld32(taddr + gn * 16, rb);
-        } else if (gn < groups) {
-          tmem_ld16(taddr + gn * 16, *reinterpret_cast<uint32_t(*)[16]>(rb));
-        } else {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tmem_empty[acc]);
-        }
+      auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+      };
+      if (g0 >= g1) release();
+      uint32_t ra[32];
+      for (int g = g0; g < g1; g += 2) {
+        const int w = g + 1 < g1 ? 2 : 1;
+        if (w == 2) tmem_ld32(taddr + g * 16, ra);
+        else tmem_ld16(taddr + g * 16, *reinterpret_cast<uint32_t(*)[16]>(ra));
+        tmem_wait_ld();
+        tmem_pin(ra);
+        if (g + w >= g1) release();
         store16(ra, g * 16);
         if (w == 2) store16(ra + 16, g * 16 + 16);
-        if (gn < groups) {
-          tmem_wait_ld();
-          tmem_pin(rb);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) ra[i] = rb[i];
-        }
-        g = gn;
       }
     }
   }
