@@ -230,8 +230,9 @@ __global__ void __launch_bounds__(256) dw_row_kernel(const __grid_constant__ DwP
 // A tile is 128 frames (columns of the head's input, one row); the 1x1 head runs over the
 // classes a chunk of up to 128 at a time (tcgen05.mma; A loaded once a tile, the chunks'
 // weights streamed by bulk copies), each chunk's accumulator in one of four TMEM buffers.
-// Eight epilogue warps, two for each TMEM lane quarter: the even chunks go to the first four,
-// the odd chunks to the other four, each half of the classes with two buffers of its own.
+// Sixteen epilogue warps, four for each TMEM lane quarter: the even chunks go to warps 2-5 and
+// 10-13, the odd chunks to 6-9 and 14-17 (each half of the chunks with two buffers of its own),
+// warps 2-9 a chunk's first part of its classes, 10-17 the second.
 // Per frame: the best class, ties to the lower id, and for a non-blank best its softmax
 // probability.
 // INT8: each class's logit requantized to uint8 exactly as the reference stores the head's
@@ -241,8 +242,8 @@ __global__ void __launch_bounds__(256) dw_row_kernel(const __grid_constant__ DwP
 // (carbon/src/net/net.cpp:1101-1128).  A term depends only on (q_c, q_best), so the 65,536
 // possible terms are computed once per model (ctc_terms_kernel, the same float operations) and
 // the sums only add them, in class order.
-// FP16: the FP32 logits (sum + bias); each half keeps an online maximum and sum of 2^x terms,
-// merged per frame.
+// FP16: the FP32 logits (sum + bias); each (half, part) keeps an online maximum and sum of 2^x
+// terms, the four merged per frame.
 // Only each frame's id and probability leave the kernel; the logits are never written.
 struct HeadParams {
   CUtensorMap tmap;     // the head's input: (K byte, frame column, row)
@@ -265,7 +266,7 @@ struct HeadParams {
   int* err;
 };
 
-constexpr int kHeadThreads = 320;  // warp 0 TMA, warp 1 MMA and TMEM, warps 2..9 the epilogue
+constexpr int kHeadThreads = 576;  // warp 0 TMA, warp 1 MMA and TMEM, warps 2..17 the epilogue
 constexpr int kHeadChunk = 128;    // classes a chunk (the MMA's N): four buffers in 512 TMEM columns
 constexpr uint32_t kTmemColsHead = 512;
 
@@ -277,7 +278,7 @@ __host__ __device__ constexpr int head_code_stride(int classes) {
 
 // Bytes of the head's shared memory after A, B and the codes: barriers, per-class constants,
 // the per-frame merge slots and the list of non-blank frames.
-__host__ __device__ constexpr int head_tail_bytes(int ncls) { return 128 + 12 * ncls + (3 * 256 + 3 * 128 + 2) * 4; }
+__host__ __device__ constexpr int head_tail_bytes(int ncls) { return 128 + 12 * ncls + (3 * 512 + 3 * 128 + 2) * 4; }
 
 // carbon/src/cpu/kernels.h:216-250 (exp_neg), each multiply and add rounded on its own.
 __device__ __forceinline__ float exp_neg_d(float x) {
@@ -330,10 +331,10 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
   int32_t* s_off = reinterpret_cast<int32_t*>(bars + 16);  // [ncls] per-class constants
   float* s_scale = reinterpret_cast<float*>(s_off + ncls);
   float* s_bias = s_scale + ncls;
-  int32_t* s_hmax = reinterpret_cast<int32_t*>(s_bias + ncls);  // [2][128] each half's highest code (FP16: logit)
-  int32_t* s_hbest = s_hmax + 256;                              // FP16 [2][128] each half's best class
-  float* s_hsum = reinterpret_cast<float*>(s_hbest + 256);     // FP16 [2][128] each half's sum
-  int32_t* nb_row = reinterpret_cast<int32_t*>(s_hsum + 256);  // INT8: the tile's non-blank frames' rows
+  int32_t* s_hmax = reinterpret_cast<int32_t*>(s_bias + ncls);  // [4][128] each (half, part)'s highest code (FP16: logit)
+  int32_t* s_hbest = s_hmax + 512;                              // FP16 [4][128] each (half, part)'s best class
+  float* s_hsum = reinterpret_cast<float*>(s_hbest + 512);     // FP16 [4][128] each (half, part)'s sum
+  int32_t* nb_row = reinterpret_cast<int32_t*>(s_hsum + 512);  // INT8: the tile's non-blank frames' rows
   int32_t* nb_q = nb_row + 128;                                 // and best codes
   int32_t* s_best = nb_q + 128;                                 // each row's best class
   volatile int32_t* s_count = s_best + 128;                     // [0] frames listed, [1] abort
@@ -356,7 +357,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(&t_full[i], 1);
-      mbar_init(&t_empty[i], 4);
+      mbar_init(&t_empty[i], 8);
     }
     fence_mbar_init();
   }
@@ -429,9 +430,10 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
       }
     }
   } else {
-    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int quarter = warp & 3, half = ((warp - 2) >> 2) & 1, part = (warp - 2) >> 3;
+    const int slot = 2 * half + part;  // this warp's (half, part) in the per-row partials
     const int row = quarter * 32 + lane;
-    const int e = threadIdx.x - 64;  // 0..255: this thread's place among the epilogue's
+    const int e = threadIdx.x - 64;  // 0..511: this thread's place among the epilogue's
     uint32_t t_phases = 0;  // bit i: this half's buffer i's phase
     int tsel = 0;
     const float lo = static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
@@ -533,54 +535,49 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
             for (int i = 0; i < 16; ++i) fsum += ex2_approx(fmaf(v[i], kLog2e, -fl));
           }
         };
-        // TMEM read 32 columns at a time, the next load in flight while the current is taken; the
-        // buffer goes back to the MMA as soon as its last load has completed
+        // this part's 16-class groups of the chunk, [g0, g1) (the first part an even count), read
+        // 32 columns at a time (the other warps hide the loads' latency); the buffer goes back to
+        // the MMA as soon as the part's last load has completed (a warp without groups has still
+        // waited for the buffer, so that its arrival counts for this use)
         const int groups = min(p.nchunk, (p.classes - cbase + 15) & ~15) >> 4;
+        const int gsplit = ((groups + 3) >> 2) << 1;
+        const int g0 = part ? min(gsplit, groups) : 0, g1 = part ? groups : min(gsplit, groups);
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                static_cast<uint32_t>(tb * kHeadChunk);
-        uint32_t ra[32], rb[32];
-        if (groups >= 2) tmem_ld32(taddr, ra); else tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(ra));
-        tmem_wait_ld();
-        tmem_pin(ra);
-        for (int g = 0; g < groups;) {
-          const int w = g + 1 < groups ? 2 : 1;
-          const int gn = g + w;
-          if (gn + 1 < groups) {
-            tmem_ld32(taddr + gn * 16, rb);
-          } else if (gn < groups) {
-            tmem_ld16(taddr + gn * 16, *reinterpret_cast<uint32_t(*)[16]>(rb));
-          } else {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&t_empty[tb]);
-          }
+        auto release = [&]() {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&t_empty[tb]);
+        };
+        if (g0 >= g1) release();
+        uint32_t ra[32];
+        for (int g = g0; g < g1; g += 2) {
+          const int w = g + 1 < g1 ? 2 : 1;
+          if (w == 2) tmem_ld32(taddr + g * 16, ra);
+          else tmem_ld16(taddr + g * 16, *reinterpret_cast<uint32_t(*)[16]>(ra));
+          tmem_wait_ld();
+          tmem_pin(ra);
+          if (g + w >= g1) release();
           take16(ra, cbase + g * 16);
           if (w == 2) take16(ra + 16, cbase + g * 16 + 16);
-          if (gn < groups) {
-            tmem_wait_ld();
-            tmem_pin(rb);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) ra[i] = rb[i];
-          }
-          g = gn;
         }
       }
-      // the two halves of each frame meet
+      // the four (half, part) partials of each frame meet
       if (!ok) s_count[1] = 1;
       if constexpr (kInt8) {
-        s_hmax[half * 128 + row] = mx;
+        s_hmax[slot * 128 + row] = mx;
       } else {
-        s_hmax[half * 128 + row] = __float_as_int(fm);
-        s_hbest[half * 128 + row] = fbest;
-        s_hsum[half * 128 + row] = fsum;
+        s_hmax[slot * 128 + row] = __float_as_int(fm);
+        s_hbest[slot * 128 + row] = fbest;
+        s_hsum[slot * 128 + row] = fsum;
       }
-      named_bar(1, 256);
+      named_bar(1, 512);
       if (s_count[1]) break;
       const bool valid = ox < p.ow && p.mask8[(static_cast<long long>(ox) << p.out_shift) >> 3] != 0;
-      if (half == 0) {
+      if (slot == 0) {
         if constexpr (kInt8) {
           // the first class with the highest code: for a blank frame the first 16 bytes hold it
-          const int32_t m = max(s_hmax[row], s_hmax[128 + row]);
+          const int32_t m = max(max(s_hmax[row], s_hmax[128 + row]), max(s_hmax[256 + row], s_hmax[384 + row]));
           const uint32_t m4 = static_cast<uint32_t>(m) * 0x01010101u;
           int best = 0;
           for (int j0 = 0; j0 < p.classes; j0 += 16) {
@@ -605,27 +602,35 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
             p.frame_prob[ox] = 0.0f;
           }
         } else {
-          const float m0 = __int_as_float(s_hmax[row]), m1 = __int_as_float(s_hmax[128 + row]);
-          const int b0 = s_hbest[row], b1 = s_hbest[128 + row];
-          const bool second = m1 > m0 || (m1 == m0 && b1 < b0);
-          const float top = second ? m1 : m0, other = second ? m0 : m1;
-          float sum = second ? s_hsum[128 + row] : s_hsum[row];
-          const float rest = second ? s_hsum[row] : s_hsum[128 + row];
-          if (other != -INFINITY) sum += rest * ex2_approx((other - top) * kLog2e);
-          const int best = second ? b1 : b0;
+          // the highest logit (ties: the lower class) and the partial sums rescaled to it
+          int bi = 0;
+#pragma unroll
+          for (int i = 1; i < 4; ++i) {
+            const float mi = __int_as_float(s_hmax[i * 128 + row]), mb = __int_as_float(s_hmax[bi * 128 + row]);
+            if (mi > mb || (mi == mb && s_hbest[i * 128 + row] < s_hbest[bi * 128 + row])) bi = i;
+          }
+          const float top = __int_as_float(s_hmax[bi * 128 + row]);
+          float sum = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float mi = __int_as_float(s_hmax[i * 128 + row]);
+            if (i == bi) sum += s_hsum[i * 128 + row];
+            else if (mi != -INFINITY) sum += s_hsum[i * 128 + row] * ex2_approx((mi - top) * kLog2e);
+          }
+          const int best = s_hbest[bi * 128 + row];
           if (valid) {
             p.frame_id[ox] = best;
             p.frame_prob[ox] = best != 0 ? __fdiv_rn(1.0f, sum) : 0.0f;
           }
         }
-      } else if (kInt8 && p.logits && ox < p.ow) {  // test hook: the dequantized logits
+      } else if (kInt8 && slot == 2 && p.logits && ox < p.ow) {  // test hook: the dequantized logits
         for (int j = 0; j < p.classes; ++j) p.logits[static_cast<long long>(ox) * p.classes + j] = tab[my[j]];
       }
-      named_bar(1, 256);
+      named_bar(1, 512);
       if constexpr (kInt8) {
         // the class-order sums of the listed (non-blank) frames, a thread a frame
         const int listed = s_count[0];
-        for (int k = e; k < listed; k += 256) {
+        for (int k = e; k < listed; k += 512) {
           const int r = nb_row[k];
           const uint8_t* rowc = codes + r * cstride;
           const float* trow = p.terms + nb_q[k] * 256;
@@ -645,7 +650,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
           p.frame_id[fx] = s_best[r];
           p.frame_prob[fx] = __fdiv_rn(1.0f, sum);
         }
-        named_bar(1, 256);
+        named_bar(1, 512);
         if (e == 0) s_count[0] = 0;  // read by every thread before the barrier; the next adds follow the next one
       }
     }
