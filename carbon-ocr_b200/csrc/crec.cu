@@ -823,6 +823,13 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
         const int smem = ((ncols * y.cp + 15) & ~15) + 24 * y.cp;
         CK(cudaFuncSetAttribute(dw_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         dw_row_kernel<<<static_cast<int>(tiles), 256, smem, s>>>(p);
+      } else if (!h->int8 && l.kh == 1 && xp.cp == y.cp && (l.kw == 3 || l.kw == 5 || l.kw == 7 || l.kw == 9)) {
+        // FP16, one kernel row: a CTA 2 x kDwF16Run output pixels of a row
+        const int tiles = static_cast<int>(static_cast<long long>(oh) * ((ow + 2 * kDwF16Run - 1) / (2 * kDwF16Run)));
+        if (l.kw == 3) dw_row_f16_kernel<3><<<tiles, 256, 0, s>>>(p);
+        else if (l.kw == 5) dw_row_f16_kernel<5><<<tiles, 256, 0, s>>>(p);
+        else if (l.kw == 7) dw_row_f16_kernel<7><<<tiles, 256, 0, s>>>(p);
+        else dw_row_f16_kernel<9><<<tiles, 256, 0, s>>>(p);
       } else {
         const long long total = static_cast<long long>(oh) * ow * (y.cp / 16);
         const int grid = static_cast<int>((total + 255) / 256);

@@ -225,6 +225,65 @@ __global__ void __launch_bounds__(256) dw_row_kernel(const __grid_constant__ DwP
   }
 }
 
+// The FP16 depthwise convolution of one kernel row (1 x KW): a CTA 2 x 32 output pixels of one
+// row and all channels.  A thread takes one channel pair (half2) over 32 consecutive output
+// pixels: its 2 x KW weights in registers, the pair's inputs converted to float once into a
+// window of KW registers that slides a pixel at a time; a warp's lanes are 32 consecutive
+// pairs, so a pixel's loads and stores are 128 contiguous bytes.  Each output is the generic
+// kernel's operations in the same order (an FP32 sum of fmaf over the taps in tap order from 0,
+// + bias, ReLU, rounded to FP16): the same bits.
+constexpr int kDwF16Run = 32;  // output pixels a thread
+
+template <int KW>
+__global__ void __launch_bounds__(256) dw_row_f16_kernel(const __grid_constant__ DwParams p) {
+  const int pairs = p.cp >> 1, cpw = p.cp >> 1;  // channel pairs (also the input's half2 a column)
+  const int tiles_per_row = (p.ow + 2 * kDwF16Run - 1) / (2 * kDwF16Run);
+  const int oy = blockIdx.x / tiles_per_row, ox0 = (blockIdx.x - oy * tiles_per_row) * 2 * kDwF16Run;
+  const int sh = p.in_shift;
+  const __half2* src = reinterpret_cast<const __half2*>(p.in + static_cast<long long>(oy - p.pt + p.in_ph) * p.in_pitch);
+  __half2* dst_row = reinterpret_cast<__half2*>(p.out + static_cast<long long>(oy + p.out_ph) * p.out_pitch);
+  for (int it = threadIdx.x; it < 2 * pairs; it += blockDim.x) {
+    const int seg = it / pairs, pr = it - seg * pairs;
+    const int x0 = ox0 + seg * kDwF16Run;
+    if (x0 >= p.ow) continue;
+    const int c0 = 2 * pr;
+    float w0[KW], w1[KW];
+#pragma unroll
+    for (int t = 0; t < KW; ++t) {
+      w0[t] = __ldg(p.wf + t * p.cp + c0);
+      w1[t] = __ldg(p.wf + t * p.cp + c0 + 1);
+    }
+    const float b0 = __ldg(p.bias + c0), b1 = __ldg(p.bias + c0 + 1);
+    const bool in0 = c0 < p.c, in1 = c0 + 1 < p.c;
+    auto input = [&](int ox, int t) { return __half22float2(src[static_cast<long long>((ox - p.pl + t) >> sh) * cpw + pr]); };
+    float2 win[KW];
+#pragma unroll
+    for (int t = 0; t < KW; ++t) win[t] = input(x0, t);
+#pragma unroll
+    for (int j = 0; j < kDwF16Run; ++j) {
+      const int ox = x0 + j;
+      float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+      for (int t = 0; t < KW; ++t) {
+        s0 = __fmaf_rn(win[t].x, w0[t], s0);
+        s1 = __fmaf_rn(win[t].y, w1[t], s1);
+      }
+      float v0 = __fadd_rn(s0, b0), v1 = __fadd_rn(s1, b1);
+      if (p.relu) {
+        v0 = v0 > 0.0f ? v0 : 0.0f;
+        v1 = v1 > 0.0f ? v1 : 0.0f;
+      }
+      const bool valid = p.mask8[(static_cast<long long>(ox) << p.out_shift) >> 3] != 0;
+      dst_row[static_cast<long long>(ox) * cpw + pr] =
+          __floats2half2_rn(valid && in0 ? v0 : 0.0f, valid && in1 ? v1 : 0.0f);
+      if (j + 1 == kDwF16Run || ox + 1 >= p.ow) break;
+#pragma unroll
+      for (int t = 0; t + 1 < KW; ++t) win[t] = win[t + 1];
+      win[KW - 1] = input(ox + 1, KW - 1);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- the head fused with CTC's argmax
 //
 // A tile is 128 frames (columns of the head's input, one row); the 1x1 head runs over the

@@ -99,6 +99,46 @@ def test_config1_fp16_within_tolerance(dev16, orc, rec_latin):
     assert all(lengths[i] == min(int(bws[i]) // 4, int(widths[i]) // 4) for i in range(len(crops)))
 
 
+def test_fp16_depthwise_is_its_operations(dev16, rec_latin):
+    """The FP16 depthwise layers (1x9, one at an upsample read in place) against the same
+    operations in numpy: per channel an FP32 fma chain over the taps in tap order from 0 (the
+    product exact in float64), + bias, ReLU if the layer has it, rounded to FP16; a line's
+    columns outside it read 0 (the FP16 zero point of the gap columns)."""
+    net = rec_latin[1]
+    crops, widths, bws = synth.crops(3, 6, 64, 900, bucket_step=32)
+    dev16.recognize_crops(crops, widths, bws)
+    checked = 0
+    for layer in net.layers:
+        if layer.kind != 1 or layer.kh != 1:
+            continue
+        vi, vo = layer.inp, layer.out
+        w = layer.wf.reshape(layer.cout, layer.kw).astype(np.float16).astype(np.float32)  # [c][taps]
+        b = layer.bias.astype(np.float32)
+        shapes_i = [net.shapes_for(int(bw))[vi] for bw in bws]
+        shapes_o = [net.shapes_for(int(bw))[vo] for bw in bws]
+        ci, co = net.values[vi].c, net.values[vo].c
+        xin = dev16.value(vi, sum(h * wd * ci for h, wd in shapes_i) * 2, np.float16)
+        xout = dev16.value(vo, sum(h * wd * co for h, wd in shapes_o) * 2, np.float16)
+        ai = ao = 0
+        for (hi, wi), (ho, wo) in zip(shapes_i, shapes_o):
+            assert hi == ho == 1 and wi == wo
+            a = xin[ai:ai + wi * ci].reshape(wi, ci)[:, :layer.cout].astype(np.float64)
+            got = xout[ao:ao + wo * co].reshape(wo, co)[:, :layer.cout]
+            ai += wi * ci
+            ao += wo * co
+            pad = np.zeros((wi + layer.kw - 1, layer.cout))
+            pad[layer.pl:layer.pl + wi] = a
+            s = np.zeros((wo, layer.cout), np.float32)
+            for t in range(layer.kw):
+                s = (pad[t:t + wo] * w[:, t].astype(np.float64) + s.astype(np.float64)).astype(np.float32)
+            v = (s + b).astype(np.float32)
+            if layer.relu:
+                v = np.maximum(v, np.float32(0))
+            assert np.array_equal(got.view(np.uint16), v.astype(np.float16).view(np.uint16)), layer.node
+            checked += 1
+    assert checked >= 2 * len(bws)
+
+
 def two_pages(seed=7):
     """tests/cpp/cuda_lines_test.cpp:47-109 of the reference: 1700 x 2200 and 900 x 640, one inverted."""
     rng = np.random.default_rng(seed)
