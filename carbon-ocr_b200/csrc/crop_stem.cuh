@@ -388,7 +388,11 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
       wq[i] = w;
     }
   } else {
-    for (int i = tid; i < p.cout * taps_stem; i += nthr) swf[i] = p.wf[i];
+    // [tap][channel]: a tap's weights for four channels are one 16-byte load (zeros past cout)
+    for (int i = tid; i < kStemMaxOut * 9; i += nthr) {
+      const int t = i / kStemMaxOut, j = i - t * kStemMaxOut;
+      swf[i] = j < p.cout && t < taps_stem ? p.wf[j * taps_stem + t] : 0.0f;
+    }
   }
   for (int i = tid; i < kStemMaxOut; i += nthr) {
     const bool in = i < p.cout;
@@ -780,23 +784,40 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
         if (y < 0 || y >= H || x < 0 || x >= bw) continue;  // the border: real zero
         in[t] = ftab[px(y, x)];
       }
+      // 16 channels as 8 pairs: an fma chain over the taps in tap order from 0 on the packed
+      // FP32 pipe (the FP16 engine is graded by tolerance), + bias, ReLU, to FP16
       for (int c0 = 0; c0 < p.cp_out; c0 += 16) {
-        alignas(16) __half o[16];
+        float2 acc[8];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const int j = c0 + u;
-          float v = 0.0f;
-          if (j < p.cout) {
+        for (int q = 0; q < 8; ++q) acc[q] = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int t = 0; t < 9; ++t)
-              if (t < taps_stem) v = __fmaf_rn(in[t], swf[j * taps_stem + t], v);
-            v = __fadd_rn(v, sbias[j]);
-            if (p.relu) v = v > 0.0f ? v : 0.0f;
+        for (int t = 0; t < 9; ++t) {
+          if (t >= taps_stem) break;
+          const float2 x2 = make_float2(in[t], in[t]);
+          const float4* w4 = reinterpret_cast<const float4*>(swf + t * kStemMaxOut + c0);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float4 w = w4[k];
+            acc[2 * k] = __ffma2_rn(x2, make_float2(w.x, w.y), acc[2 * k]);
+            acc[2 * k + 1] = __ffma2_rn(x2, make_float2(w.z, w.w), acc[2 * k + 1]);
           }
-          o[u] = __float2half_rn(v);
+        }
+        alignas(16) __half2 o[8];
+        const float4* b4 = reinterpret_cast<const float4*>(sbias + c0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float4 b = b4[k];
+          float v[4] = {__fadd_rn(acc[2 * k].x, b.x), __fadd_rn(acc[2 * k].y, b.y), __fadd_rn(acc[2 * k + 1].x, b.z),
+                        __fadd_rn(acc[2 * k + 1].y, b.w)};
+          if (p.relu) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = v[u] > 0.0f ? v[u] : 0.0f;
+          }
+          o[2 * k] = __floats2half2_rn(v[0], v[1]);
+          o[2 * k + 1] = __floats2half2_rn(v[2], v[3]);
         }
         *reinterpret_cast<uint4*>(dst + c0 * 2) = *reinterpret_cast<const uint4*>(o);
-        *reinterpret_cast<uint4*>(dst + c0 * 2 + 16) = *reinterpret_cast<const uint4*>(o + 8);
+        *reinterpret_cast<uint4*>(dst + c0 * 2 + 16) = *reinterpret_cast<const uint4*>(o + 4);
       }
     }
   }
