@@ -55,8 +55,10 @@ struct ConvParams {
   const uint8_t* wimg;  // [n tile][ky][kb][nt rows][128 bytes], each block in the 128-byte swizzle
   int krows, nkb, last_steps;  // input rows; K blocks of 128 bytes a row; 32-byte K steps in a row's last block
   int q_rows, cq;              // output rows a tile; its channels an output row (cq = nt when q_rows is 1)
+  int cq_inv;                  // ceil(65536 / (cq / 16)): a group g's output row is (g * cq_inv) >> 16 (exact for g < 16)
   int nt, n_tiles;          // output channels a tile (multiple of 16, <= 256), tiles across the channels
   int oh, ow, m_per_row, num_tiles;
+  uint32_t nt_magic, mpr_magic;  // div_magic(n_tiles), div_magic(m_per_row): the tile decode without divisions
   int stages;
   uint32_t stage_bytes, a_bytes, b_bytes;
   // epilogue
@@ -141,8 +143,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     uint32_t phase = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-      const int n = t % p.n_tiles, m = t / p.n_tiles;
-      const int oy = m / p.m_per_row, ox0 = (m % p.m_per_row) * 128;
+      const int m = fast_div(t, p.n_tiles, p.nt_magic), n = t - m * p.n_tiles;
+      const int oy = fast_div(m, p.m_per_row, p.mpr_magic), ox0 = (m - oy * p.m_per_row) * 128;
       for (int ky = 0; ky < p.krows && ok; ++ky) {
         for (int kb = 0; kb < p.nkb; ++kb) {
           if (!mbar_wait_warp(&empty[stage], phase ^ 1, p.err, kErrTimeoutEmpty)) {
@@ -231,8 +233,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     // the line mask byte of this thread's pixel in tile t (0 past the output's width)
     auto mask_of = [&](int t) -> int {
       if (t >= p.num_tiles) return 0;
-      const int m = t / p.n_tiles;
-      const int ox = (m % p.m_per_row) * 128 + row;
+      const int m = fast_div(t, p.n_tiles, p.nt_magic);
+      const int ox = (m - fast_div(m, p.m_per_row, p.mpr_magic) * p.m_per_row) * 128 + row;
       return ox < p.ow ? __ldg(p.mask8 + ((static_cast<long long>(ox) << p.out_shift) >> 3)) : 0;
     };
     int iter = half;
@@ -244,8 +246,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       const uint32_t acc_phase = (iter / p.n_acc) & 1;
       if (!mbar_wait(&tmem_full[acc], acc_phase, p.err, kErrTimeoutTmemFull)) break;
       tc_fence_after();
-      const int n = t % p.n_tiles, m = t / p.n_tiles;
-      const int oy = (m / p.m_per_row) * p.q_rows, ox = (m % p.m_per_row) * 128 + row;
+      const int m = fast_div(t, p.n_tiles, p.nt_magic), n = t - m * p.n_tiles;
+      const int mr = fast_div(m, p.m_per_row, p.mpr_magic);
+      const int oy = mr * p.q_rows, ox = (m - mr * p.m_per_row) * 128 + row;
       const bool inside = ox < p.ow;
       const bool valid = inside && mk != 0;
       mk = mk_next;
@@ -256,7 +259,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       const int c0 = n * p.nt;
       // 16 of the tile's columns from r[0..16), starting at tile column tc: output row oy + q, channel cb
       auto store16 = [&](const uint32_t* r, int tc) {
-        const int q = p.q_rows > 1 ? tc / p.cq : 0;
+        const int q = p.q_rows > 1 ? ((tc >> 4) * p.cq_inv) >> 16 : 0;
         const int cb = c0 + tc - q * p.cq;
         if (!inside || cb >= p.cp_out || oy + q >= p.oh) return;
         uint8_t* dst = dst0 + q * p.out_pitch;

@@ -855,6 +855,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.krows = l.krows;
     p.q_rows = l.q_rows;
     p.cq = l.cq;
+    p.cq_inv = (65536 + l.cq / 16 - 1) / (l.cq / 16);
     p.nkb = l.nkb;
     p.last_steps = l.last_steps;
     p.nt = l.nt;
@@ -863,6 +864,11 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.ow = static_cast<int>(ow);
     p.m_per_row = static_cast<int>((ow + 127) / 128);
     p.num_tiles = (oh / l.q_rows) * p.m_per_row * l.n_tiles;
+    p.nt_magic = div_magic(static_cast<uint32_t>(l.n_tiles));
+    p.mpr_magic = div_magic(static_cast<uint32_t>(p.m_per_row));
+    // the multiply-high divisions are exact for x * d < 2^32 (x a tile or column-block index)
+    if (static_cast<unsigned long long>(p.num_tiles) * static_cast<unsigned>(std::max(l.n_tiles, p.m_per_row)) >= (1ull << 32))
+      return set_error(h, CREC_E_RANGE, "a run with too many conv tiles");
     p.stages = l.stages;
     p.stage_bytes = l.stage_bytes;
     p.a_bytes = l.a_bytes;

@@ -85,6 +85,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// x / d by a multiply-high: magic = div_magic(d) = floor(2^32 / d) + 1 (d >= 2); exact whenever
+// x * d < 2^32 (the error of magic * d over 2^32 is at most d).  d = 1 passes x through.
+__host__ __device__ inline uint32_t div_magic(uint32_t d) {
+  return d <= 1 ? 0u : static_cast<uint32_t>(0x100000000ull / d + 1);
+}
+__device__ __forceinline__ int fast_div(int x, int d, uint32_t magic) {
+  return d <= 1 ? x : static_cast<int>(__umulhi(static_cast<uint32_t>(x), magic));
+}
+
 // One lane of a converged warp (the same lane each call while the whole warp is active).
 __device__ __forceinline__ bool elect_one() {
   uint32_t e;
