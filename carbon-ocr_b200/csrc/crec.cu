@@ -816,6 +816,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.out_shift = y.shift;
       p.wt = l.dwt;
       p.dwc = l.dwc;
+      p.g_magic = div_magic(static_cast<uint32_t>(y.cp / 16));
       ProfScope prof(h, kProfDw, static_cast<int>(li));
       if (h->int8 && l.dwt) {
         const long long tiles = static_cast<long long>(oh) * ((ow + kDwTile - 1) / kDwTile);

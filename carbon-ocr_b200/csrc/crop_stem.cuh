@@ -712,8 +712,14 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
   const float lo = p.relu ? 0.0f : static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
   const int32_t zc = p.out_zero - kMagicBits;
   const bool windows = kInt8 && p.kh <= 3 && p.kw <= 4 && p.pt >= 0 && p.pt <= 2 && p.pl >= 0 && p.pl <= 4;
-  for (int i = tid; i < oh * ow; i += nthr) {
-    const int oy = i / ow, ox = i - oy * ow;
+  // pixel i = tid + k * nthr as (oy, ox), advanced without a division a step
+  const int step_y = nthr / ow, step_x = nthr - step_y * ow;
+  int oy = tid / ow, ox = tid - oy * ow;
+  for (int i = tid; i < oh * ow; i += nthr, oy += step_y, ox += step_x) {
+    if (ox >= ow) {
+      ox -= ow;
+      ++oy;
+    }
     uint8_t* dst = p.out + (oy + p.out_ph) * p.out_pitch + (col0 + ox) * p.cp_out * eb;
     if constexpr (kInt8) {
       // a kernel row's taps, 4 bytes a word (past kw: anything, the weights there are 0); the

@@ -42,6 +42,7 @@ struct DwParams {
   // threads read 16 consecutive 16-byte words
   const uint32_t* wt;   // [3 slots]: channel c's taps 4j .. 4j+3 in slot j (zeros past kw)
   const uint32_t* dwc;  // [3 slots]: kMagicBits - in_zero * (the channel's weight sum), scale, bias (bits)
+  uint32_t g_magic;     // div_magic(cp / 16): an item's pixel without a division (item * groups < 2^32)
 };
 
 // The row kernel's interleaved index of channel c (of cp) in slot `slot`.
@@ -157,7 +158,7 @@ __global__ void __launch_bounds__(256) dw_row_kernel(const __grid_constant__ DwP
   const int32_t zc = p.out_zero - kMagicBits;
   const uint32_t zb = static_cast<uint32_t>(p.out_zero) * 0x01010101u;
   for (int it = threadIdx.x; it < kDwTile * G; it += blockDim.x) {
-    const int px = it / G, g = it - px * G;
+    const int px = fast_div(it, G, p.g_magic), g = it - px * G;
     const int ox = ox0 + px;
     if (ox >= p.ow) continue;
     uint8_t* dst = p.out + static_cast<long long>(oy + p.out_ph) * p.out_pitch + static_cast<long long>(ox) * cp + g * 16;
