@@ -53,8 +53,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--max-columns", type=int, default=1 << 21)
-    ap.add_argument("--max-lines", type=int, default=8192)
+    ap.add_argument("--max-columns", type=int, default=1 << 23, help="input columns a device run at most (the scheduler's run size)")
+    ap.add_argument("--max-lines", type=int, default=32768)
     ap.add_argument("--pages", type=int, default=PAGES_TOTAL, help="page slots of the whole job (1024: config 5)")
     ap.add_argument("--no-fp16", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
