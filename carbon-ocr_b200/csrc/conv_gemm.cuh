@@ -70,8 +70,8 @@ struct ConvParams {
   const float* scale;     // [cp_out] input scale * weight scale (int8)
   const float* bias;      // [cp_out]
   int out_zero, relu;
-  int sat;      // INT8: |v * inv_scale| < 2^21 for every output, so it may be rounded before the clamp
-  int code_lo;  // the lowest code: the zero point after a ReLU, else 0
+  int sat;  // INT8: |v * inv_scale| < 2^21 for every output and no ReLU above a zero point, so the code
+           // may be rounded first and clamped to [0, 255] by the saturating pack
   int n_acc;              // TMEM accumulators (a power of two, <= kMaxAcc), each 512 / n_acc columns
   float out_inv_scale;
   const uint8_t* res;  // residual tensor's first row, or null
@@ -303,10 +303,6 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
                 code[4 * k + u] = t0 + zc;
                 code[4 * k + u + 1] = t1 + zc;
               }
-            }
-            if (p.sat && p.code_lo > 0) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) code[i] = max(code[i], p.code_lo);
             }
             if (cb + 16 > p.c_out) {
 #pragma unroll

@@ -462,7 +462,8 @@ bool round_first(const crec_handle* h, const Layer& l, const Value& x, const Val
     for (size_t k = 0; k < per; ++k) a += std::abs(static_cast<int>(l.w8[j * per + k]));
     worst = std::max(worst, a * reach * std::fabs(scale[j]) + std::fabs(bias[j]) + rs);
   }
-  return worst * 1.01 * std::fabs(1.0 / y.scale) < static_cast<double>(1 << 21);
+  // a ReLU above a zero point clamps at the zero point, not at 0: left to the float clamp
+  return worst * 1.01 * std::fabs(1.0 / y.scale) < static_cast<double>(1 << 21) && !(l.relu && y.zero > 0);
 }
 
 int setup_layer(crec_handle* h, size_t li) {
@@ -712,7 +713,6 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.out_zero = s0.zero;
     p.relu = stem.relu;
     p.sat = stem.sat;
-    p.code_lo = stem.relu ? s0.zero : 0;
     p.out_inv_scale = h->int8 ? 1.0f / s0.scale : 1.0f;
     p.out = s0.base;
     p.out_ph = s0.ph;
@@ -886,7 +886,6 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.out_zero = y.zero;
     p.relu = l.relu;
     p.sat = l.sat;
-    p.code_lo = l.relu ? y.zero : 0;
     p.n_acc = conv_accumulators(l.nt);
     p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
     if (l.residual >= 0) {

@@ -67,8 +67,8 @@ struct CropParams {
   const int32_t* colsum;  // [cout] sum of each output channel's int8 weights
   const uint8_t* in_table;  // [256] the INT8 input table
   int in_zero, out_zero, relu;
-  int sat;      // INT8: |v * inv_scale| < 2^21 for every output (round, then clamp while packing)
-  int code_lo;  // the lowest code: the zero point after a ReLU, else 0
+  int sat;  // INT8: |v * inv_scale| < 2^21 for every output and no ReLU above a zero point (round,
+           // then clamp to [0, 255] while packing)
   float out_inv_scale;
   uint8_t* out;  // stem tensor's first row
   int out_ph;
@@ -771,7 +771,6 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
             const float v = __fadd_rn(__fmul_rn(magic_to_float(acc), ss[u]), bb[u]);
             const float q0 = __fmul_rn(v, p.out_inv_scale);
             code[u] = magic_rint_bits(kRound ? q0 : fminf(fmaxf(q0, lo), hi)) + zc;
-            if (kRound && p.code_lo > 0) code[u] = max(code[u], p.code_lo);
           }
           wv[c4] = pack_sat_u8x4(code);
         }
