@@ -164,17 +164,20 @@ def two_pages(seed=7):
 
 def decodings_without_crop_copies(blob, pages, page_of, boxes, **kw):
     """The same run on a device that does not keep its finished crops (the crop kernel's final
-    pass then works a word at a time)."""
+    pass then works a word at a time): decodings, lengths and every line's logits."""
     dev = native.RecDevice(blob, native.INT8, max_lines=512, max_width=1024, max_pages=4, **kw)
     try:
         dev.set_pages(pages)
-        return dev.recognize(page_of, boxes, 1024)
+        dev.arm_logits()
+        got, lengths = dev.recognize(page_of, boxes, 1024)
+        return got, lengths, dev.logits([1024] * len(boxes), 800)
     finally:
         dev.close()
 
 
-def assert_same_decodings(a, la, b, lb):
+def assert_same_decodings(a, la, b, lb, logits_a, logits_b):
     for i in range(len(a)):
+        assert np.array_equal(logits_a[i], logits_b[i]), i
         assert la[i] == lb[i], i
         assert np.array_equal(a[i].ids, b[i].ids) and np.array_equal(a[i].frames, b[i].frames), i
         assert np.array_equal(a[i].probs.view(np.int32), b[i].probs.view(np.int32)), i
@@ -189,8 +192,10 @@ def test_pages_crops_and_ctc_bit_exact(rec_latin, orc, rule):
     try:
         dev.set_pages(pages)
         dev.arm_crops(1024)
+        dev.arm_logits()
         got, lengths = dev.recognize(page_of, boxes, 1024)
         crops = dev.crops(len(boxes), 1024)
+        dev_logits = dev.logits([1024] * len(boxes), 800)
     finally:
         dev.close()
     ocr = O.CropRule.default(**rule)
@@ -208,12 +213,14 @@ def test_pages_crops_and_ctc_bit_exact(rec_latin, orc, rule):
     logits = m.run(want_crops[sample])
     lines, _, _ = orc.ctc_greedy(logits, np.minimum(256, widths[sample] // 4))
     for j, i in enumerate(sample):
+        # every logit: with random weights these page crops decode mostly to blanks
+        assert np.array_equal(dev_logits[i], logits[j]), int(i)
         assert lengths[i] == min(256, widths[i] // 4)
         ids, fr, pr = lines[j]
         assert np.array_equal(got[i].ids, ids) and np.array_equal(got[i].frames, fr)
         assert np.array_equal(got[i].probs.view(np.int32), pr.view(np.int32))
-    got2, lengths2 = decodings_without_crop_copies(rec_latin[0].to_blob(), pages, page_of, boxes, crop=crop_rule)
-    assert_same_decodings(got, lengths, got2, lengths2)
+    got2, lengths2, logits2 = decodings_without_crop_copies(rec_latin[0].to_blob(), pages, page_of, boxes, crop=crop_rule)
+    assert_same_decodings(got, lengths, got2, lengths2, dev_logits, logits2)
 
 
 def tall_pages(seed=11):
@@ -246,12 +253,14 @@ def test_tall_lines_and_odd_strides_crop_bit_exact(rec_latin, orc):
     try:
         dev.set_pages(pages)
         dev.arm_crops(1024)
+        dev.arm_logits()
         got, lengths = dev.recognize(page_of, boxes, 1024)
         crops = dev.crops(len(boxes), 1024)
+        dev_logits = dev.logits([1024] * len(boxes), 800)
     finally:
         dev.close()
-    got2, lengths2 = decodings_without_crop_copies(rec_latin[0].to_blob(), pages, page_of, boxes)
-    assert_same_decodings(got, lengths, got2, lengths2)
+    got2, lengths2, logits2 = decodings_without_crop_copies(rec_latin[0].to_blob(), pages, page_of, boxes)
+    assert_same_decodings(got, lengths, got2, lengths2, dev_logits, logits2)
     ocr = O.CropRule.default()
     for p in range(2):
         sel = np.nonzero(page_of == p)[0]
