@@ -32,21 +32,23 @@ def page_lines(rng: np.random.Generator, width: int, height: int, n: int, hmin=1
         y0 = rng.uniform(margin, max(margin + 1.0, height - margin - span))
         base = y0 + (abs(rise) if rise < 0 else 0.0)  # the line's top at its left end
         boxes[i] = (x0, y0, x0 + w, y0 + span)
-        # glyph strokes along the line: a few per glyph width
+        # glyph strokes along the line, 2-5 a glyph, as dense as config 1's crops: the random-weight
+        # recognizer then reads about a quarter of a line's frames as characters (sparser strokes
+        # decoded almost all blank, which would leave the fused head's per-frame sums idle)
         x = x0 + rng.uniform(0, 3)
         while x < x0 + w - 2:
-            gw = rng.uniform(0.35, 0.75) * h  # a glyph
-            k = int(rng.integers(1, 4))
+            gw = rng.uniform(0.35, 0.6) * h  # a glyph
+            k = int(rng.integers(2, 6))
             for _ in range(k):
                 sx = x + rng.uniform(0, gw)
-                sw = rng.uniform(2, max(2.5, 0.12 * h))
-                top = base + (sx - x0) * math.tan(ang) + rng.uniform(0.1, 0.4) * h
-                sh = rng.uniform(0.3, 0.6) * h
-                if rng.random() < 0.4:  # a horizontal bar instead
-                    sw, sh = rng.uniform(0.3, 0.6) * h, rng.uniform(2, max(2.5, 0.1 * h))
+                sw = rng.uniform(0.08 * h, max(0.08 * h + 0.5, 0.16 * h))
+                top = base + (sx - x0) * math.tan(ang) + rng.uniform(0.05, 0.3) * h
+                sh = rng.uniform(0.45, 0.8) * h
+                if rng.random() < 0.35:  # a horizontal bar instead
+                    sw, sh = rng.uniform(0.3, 0.6) * h, rng.uniform(0.08 * h, max(0.08 * h + 0.5, 0.16 * h))
                 v = int(np.clip(rng.normal(40, 15), 0, 255))
                 strokes.append((int(sx), int(top), int(min(sx + sw, x0 + w)) + 1, int(top + sh) + 1, v))
-            x += gw + rng.uniform(0.1, 0.5) * h * (3.0 if rng.random() < 0.15 else 1.0)
+            x += gw + rng.uniform(0.05, 0.25) * h * (3.0 if rng.random() < 0.15 else 1.0)
     return boxes, np.asarray(strokes, np.int32).reshape(-1, 5)
 
 

@@ -391,25 +391,35 @@ def test_config3_scale_int8(dev8, orc, rec_latin):
                     assert np.array_equal(got[i].probs.view(np.int32), lines[j][2].view(np.int32))
 
 
-def test_fp16_pages_agree_with_fp32(dev16, orc, rec_latin):
-    pages, boxes = synth.pages(2, 2, 2480, 3508, 32)
-    page_of = np.repeat(np.arange(2), 32).astype(np.int32)
+def test_fp16_pages_agree_with_fp32(orc, rec_latin):
+    """Crops of text-like pages through the FP16 engine against the FP32 recognizer on the same
+    crops: the logits within FP16_LOGIT_TOL and, over the frames the decoder reads (within each
+    line's length), at least 99.9% of frame ids agreeing.  With random weights the ids that differ
+    are near ties, so the share is measured over many frames: 256 lines, ~18,000 frames."""
+    pages, boxes = synth.pages(2, 4, 2480, 3508, 64)
+    page_of = np.repeat(np.arange(4), 64).astype(np.int32)
     allb = np.concatenate(boxes)
-    dev16.set_pages(pages)
-    dev16.arm_logits()
-    widths = np.array([native.crop_region(b)[1] for b in allb])
-    bws = ((widths + 31) // 32 * 32).astype(np.int32)
-    got, lengths = dev16.recognize_lines(page_of, allb, bws)
-    logits = dev16.logits(bws, 800)
+    dev = native.RecDevice(rec_latin[1].to_blob(), native.FP16, max_lines=512, max_width=2048, max_pages=8,
+                           max_page_bytes=4 * 2480 * 3508)
+    try:
+        dev.set_pages(pages)
+        dev.arm_logits()
+        widths = np.array([native.crop_region(b)[1] for b in allb])
+        bws = ((widths + 31) // 32 * 32).astype(np.int32)
+        got, lengths = dev.recognize_lines(page_of, allb, bws)
+        logits = dev.logits(bws, 800)
+    finally:
+        dev.close()
     m32 = orc.model(rec_latin[1].to_blob())
     agree = total = 0
     worst = 0.0
-    for i in range(0, len(allb), 4):
+    for i in range(len(allb)):
         crop, _ = orc.crop_lines(pages[page_of[i]], allb[i:i + 1], int(bws[i]))
         ref = m32.run(crop)[0]
         worst = max(worst, float(np.abs(logits[i] - ref).max()))
-        agree += int((logits[i].argmax(0) == ref.argmax(0)).sum())
-        total += ref.shape[1]
+        n = int(lengths[i])
+        agree += int((logits[i].argmax(0)[:n] == ref.argmax(0)[:n]).sum())
+        total += n
     assert worst <= FP16_LOGIT_TOL and agree / total >= FP16_ID_AGREEMENT, (worst, agree, total)
 
 
