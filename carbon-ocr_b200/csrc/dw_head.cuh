@@ -694,16 +694,30 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
           const int r = nb_row[k];
           const uint8_t* rowc = codes + r * cstride;
           const float* trow = p.terms + nb_q[k] * 256;
-          float sum = 0.0f;
-          int j0 = 0;
-          for (; j0 + 16 <= p.classes; j0 += 16) {
+          // batches of 16 terms, the next batch's loads in flight while the current is added
+          // (the adds stay in class order)
+          auto load16 = [&](int j0, float (&dst)[16]) {
             const uint4 w = *reinterpret_cast<const uint4*>(rowc + j0);
             const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-            float term[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) term[i] = __ldg(trow + ((ww[i >> 2] >> (8 * (i & 3))) & 0xff));
+            for (int i = 0; i < 16; ++i) dst[i] = __ldg(trow + ((ww[i >> 2] >> (8 * (i & 3))) & 0xff));
+          };
+          const int full = p.classes & ~15;
+          float sum = 0.0f, cur[16], nxt[16];
+          int j0 = 0;
+          if (full >= 16) load16(0, cur);
+          for (; j0 + 32 <= full; j0 += 32) {
+            load16(j0 + 16, nxt);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, term[i]);
+            for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, cur[i]);
+            if (j0 + 48 <= full) load16(j0 + 32, cur);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, nxt[i]);
+          }
+          if (j0 + 16 <= full) {  // one batch left, in cur
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, cur[i]);
+            j0 += 16;
           }
           for (; j0 < p.classes; ++j0) sum = __fadd_rn(sum, __ldg(trow + rowc[j0]));
           const int fx = t * 128 + r;
