@@ -6,8 +6,9 @@
 Workload (the 1/2/4/8-GPU one; config 2 is its 16-page slice):
 1024 synthetic 2480 x 3508 pages x 64 lines (65,536 lines), sharded by page over the N
 ranks (strong scaling: the total is fixed).  The pages are 32 distinct seeded pages
-(seed 5000: background ~N(235, 8), lines 18-60 px high, aspect 4-40, +-5 degrees), page
-slot s using page s % 32 and its 64 boxes; each line is read at its 32-px bucket (up to
+(seed 5000: background ~N(235, 8), lines 18-60 px high, aspect 4-40, +-5 degrees, glyph strokes
+dense enough that about a quarter of the frames decode to characters), page slot s using page
+s % 32 and its 64 boxes; each line is read at its 32-px bucket (up to
 1024).  A step is every line of the rank's shard: cropped from its page, recognized,
 decoded; only ids, frames and probabilities leave the GPU.
 
@@ -44,7 +45,8 @@ METRIC = "text lines/sec (rec-latin INT8 & FP16, crop+CTC fused) at 1/2/4/8 B200
 PAGES_TOTAL, LINES_PER_PAGE, DISTINCT, SEED = 1024, 64, 32, 5000
 PAGE_W, PAGE_H = 2480, 3508
 WORKLOAD = ("config5: 1024 synthetic 2480x3508 pages x 64 lines (65,536 lines), rec-latin crop+trunk+fused CTC, "
-            "32-px buckets to 1024, sharded by page; 32 distinct seeded pages (seed 5000) resident before timing")
+            "32-px buckets to 1024, sharded by page; 32 distinct seeded pages (seed 5000, text-like glyphs: ~25% of "
+            "frames decode to characters) resident before timing")
 
 
 def parse():
