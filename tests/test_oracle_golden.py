@@ -148,3 +148,21 @@ def test_mini_int8_golden(orc, mini, golden):
     crops, widths, bws = synth.crops(21, 6, 40, 200, bucket_step=8)
     for i, want in enumerate(golden["mini_int8"]["lines"]):
         assert sha(m.run(crops[i:i + 1, :, :want["bw"]])) == want["logits_sha256"]
+
+
+def test_synth_page_lines_read_as_text(orc, rec_latin):
+    """The bench's synthetic pages draw glyphs dense enough that the random-weight recognizer
+    reads a share of each line's frames as characters (21% on these 32 lines; 20% on config 1's
+    crops): with near-blank lines the fused head's per-frame class-order sums would hardly run
+    and the bench would not measure them."""
+    pages, boxes = synth.pages(5000, 1, 2480, 3508, 32)
+    m = orc.model(rec_latin[0].to_blob())
+    crops, widths = orc.crop_lines(pages[0], boxes[0], 1024)
+    chars = frames = 0
+    for i in range(len(boxes[0])):
+        bw = int((widths[i] + 31) // 32 * 32)
+        logits = m.run(crops[i:i + 1, :, :bw])
+        n = min(bw // 4, int(widths[i]) // 4)
+        chars += int((logits[0].argmax(0)[:n] != 0).sum())
+        frames += n
+    assert 0.1 <= chars / frames <= 0.5, (chars, frames)
