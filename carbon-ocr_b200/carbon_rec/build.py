@@ -21,7 +21,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "carbon_rec.h"]
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [INCLUDE / "carbon_rec.h"]
 
 
 def needs_build() -> bool:
@@ -34,7 +34,7 @@ def needs_build() -> bool:
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not needs_build():
         return LIB
-    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-fmad=false", "--expt-relaxed-constexpr",
+    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++20", "-fmad=false", "--expt-relaxed-constexpr",
            "-Xcompiler", "-fPIC,-ffp-contract=off,-fvisibility=hidden", "-shared",
            f"-I{INCLUDE}", str(CSRC / "crec.cu"), "-o", str(LIB)]
     if verbose:

@@ -19,6 +19,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libcarbon_rec.so"
 
 OK, E_INVALID, E_NOMEM, E_CUDA, E_STICKY, E_TIMEOUT, E_MODEL, E_RANGE = range(8)
 INT8, FP16 = 0, 1
+INJECT_TIMEOUT, INJECT_STICKY = 1, 2
 _NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA error", E_STICKY: "sticky CUDA error",
           E_TIMEOUT: "kernel wait timed out", E_MODEL: "model not supported", E_RANGE: "out of range"}
 
@@ -26,7 +27,7 @@ _NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA
 EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec_set_pages", "crec_prefetch_pages",
            "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_ctc_greedy", "crec_ctc_greedy_noalloc", "crec_width_bucket", "crec_crop_region",
            "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats",
-           "crec_profile", "crec_profile_layers", "crec_mma_peak"]
+           "crec_profile", "crec_profile_layers", "crec_mma_peak", "crec_debug_inject"]
 
 
 class CrecError(RuntimeError):
@@ -66,7 +67,8 @@ class Box(C.Structure):
 
 
 class Stats(C.Structure):
-    _fields_ = [("runs", C.c_int64), ("launches", C.c_int64), ("h2d_bytes", C.c_int64), ("d2h_bytes", C.c_int64)]
+    _fields_ = [("runs", C.c_int64), ("launches", C.c_int64), ("h2d_bytes", C.c_int64), ("d2h_bytes", C.c_int64),
+                ("h2d_total", C.c_int64), ("d2h_total", C.c_int64)]
 
 
 class ProfileEntry(C.Structure):
@@ -113,6 +115,7 @@ def lib() -> C.CDLL:
         L.crec_profile.argtypes = [p, i, C.POINTER(ProfileEntry), i]
         L.crec_profile_layers.argtypes = [p, C.POINTER(ProfileEntry), i]
         L.crec_mma_peak.argtypes = [i, i, i, i, C.POINTER(C.c_double)]
+        L.crec_debug_inject.argtypes = [p, i]
         _lib = L
     return _lib
 
@@ -197,6 +200,15 @@ class CtcLine:
     probs: np.ndarray
 
 
+def _page_array(p) -> np.ndarray:
+    """A page as the C ABI takes it: uint8 rows, each row's bytes contiguous (rows may be further
+    apart, a view into a wider image); other arrays are copied."""
+    a = np.asarray(p)
+    if a.dtype == np.uint8 and a.ndim == 2 and a.strides[1] == 1 and a.strides[0] >= a.shape[1]:
+        return a
+    return np.ascontiguousarray(a, np.uint8)
+
+
 def _boxes(boxes) -> np.ndarray:
     b = np.ascontiguousarray(np.asarray(boxes, np.float64).reshape(-1, 4))
     return b
@@ -263,7 +275,7 @@ class RecDevice:
     def set_pages(self, pages, rows=None) -> None:
         """pages: list of 2-d uint8 arrays (paper 255); rows: per page a list of (first, last) row runs or None.
         The arrays are kept alive here until the next set_pages or prefetch_pages call returns."""
-        arr = [np.ascontiguousarray(p, np.uint8) for p in pages]
+        arr = [_page_array(p) for p in pages]
         descs = (Page * max(1, len(arr)))(*[Page(a.ctypes.data, a.shape[1], a.shape[0], a.strides[0]) for a in arr])
         keep: list = []
         runs = self._runs(rows, keep)
@@ -278,7 +290,7 @@ class RecDevice:
     def prefetch_pages(self, pages, rows=None) -> None:
         """The next group's pages, uploaded beside the current group's work; a set_pages with the same
         arrays then takes them.  Kept alive here until the next set_pages or prefetch_pages call returns."""
-        arr = [np.ascontiguousarray(p, np.uint8) for p in pages]
+        arr = [_page_array(p) for p in pages]
         descs = (Page * max(1, len(arr)))(*[Page(a.ctypes.data, a.shape[1], a.shape[0], a.strides[0]) for a in arr])
         keep: list = []
         runs = self._runs(rows, keep)
@@ -349,7 +361,8 @@ class RecDevice:
     def last_stats(self) -> dict:
         st = Stats()
         self._check(lib().crec_last_stats(self._h, C.byref(st)))
-        return {"runs": st.runs, "launches": st.launches, "h2d_bytes": st.h2d_bytes, "d2h_bytes": st.d2h_bytes}
+        return {"runs": st.runs, "launches": st.launches, "h2d_bytes": st.h2d_bytes, "d2h_bytes": st.d2h_bytes,
+                "h2d_total": st.h2d_total, "d2h_total": st.d2h_total}
 
     def profile(self, enable: int = -1) -> dict:
         """Per-kernel totals {name: (launches, ms, ops)} since profiling was (re)started; enable 1 (re)starts."""
@@ -364,6 +377,10 @@ class RecDevice:
         if n < 0:
             self._check(-n)
         return [(ent[i].kernel.decode(), ent[i].launches, ent[i].ms, ent[i].ops) for i in range(n)]
+
+    def inject(self, what: int) -> None:
+        """Test hook: INJECT_TIMEOUT or INJECT_STICKY for the next device run (crec_debug_inject)."""
+        self._check(lib().crec_debug_inject(self._h, int(what)))
 
     def arm_logits(self) -> None:
         self._check(lib().crec_debug_logits(self._h, None, 0))

@@ -81,6 +81,8 @@ struct ConvParams {
   const uint8_t* mask8;  // one byte per 8 input columns: 1 where a line is
   int out_shift;         // log2 of input columns per output column
   int* err;
+  unsigned long long wait_ns;  // every wait's limit (kWaitNs; shorter only for a test's injected timeout)
+  int idle_producer;           // test hook: the producer issues nothing, so the waits run out
 };
 
 constexpr int kConvThreads = 576;
@@ -141,13 +143,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     const bool leader = elect_one();
     int stage = 0;
     uint32_t phase = 0;
-    bool ok = true;
+    bool ok = p.idle_producer == 0;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
       const int m = fast_div(t, p.n_tiles, p.nt_magic), n = t - m * p.n_tiles;
       const int oy = fast_div(m, p.m_per_row, p.mpr_magic), ox0 = (m - oy * p.m_per_row) * 128;
       for (int ky = 0; ky < p.krows && ok; ++ky) {
         for (int kb = 0; kb < p.nkb; ++kb) {
-          if (!mbar_wait_warp(&empty[stage], phase ^ 1, p.err, kErrTimeoutEmpty)) {
+          if (!mbar_wait_warp(&empty[stage], phase ^ 1, p.err, kErrTimeoutEmpty, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -186,13 +188,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++iter) {
       const int acc = iter & (p.n_acc - 1);
       const uint32_t acc_phase = (iter / p.n_acc) & 1;
-      if (!mbar_wait_warp(&tmem_empty[acc], acc_phase ^ 1, p.err, kErrTimeoutTmemEmpty)) break;
+      if (!mbar_wait_warp(&tmem_empty[acc], acc_phase ^ 1, p.err, kErrTimeoutTmemEmpty, p.wait_ns)) break;
       tc_fence_after();
       const uint32_t d = tmem + static_cast<uint32_t>(acc) * acc_cols;
       uint32_t accumulate = 0;
       int kb = 0;
       for (int ks = 0; ks < ksteps_per_tile; ++ks) {
-        if (!mbar_wait_warp(&full[stage], phase, p.err, kErrTimeoutFull)) {
+        if (!mbar_wait_warp(&full[stage], phase, p.err, kErrTimeoutFull, p.wait_ns)) {
           ok = false;
           break;
         }
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       const int mk_next = mask_of(t + 2 * gridDim.x);  // in flight during this tile
       const int acc = iter & (p.n_acc - 1);
       const uint32_t acc_phase = (iter / p.n_acc) & 1;
-      if (!mbar_wait(&tmem_full[acc], acc_phase, p.err, kErrTimeoutTmemFull)) break;
+      if (!mbar_wait(&tmem_full[acc], acc_phase, p.err, kErrTimeoutTmemFull, p.wait_ns)) break;
       tc_fence_after();
       const int m = fast_div(t, p.n_tiles, p.nt_magic), n = t - m * p.n_tiles;
       const int mr = fast_div(m, p.m_per_row, p.mpr_magic);

@@ -14,12 +14,14 @@
 
 #include <algorithm>
 #include <cmath>
+#include <condition_variable>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/carbon_rec.h"
@@ -29,6 +31,7 @@
 #include "dw_head.cuh"
 #include "peak.cuh"
 #include "sm100.cuh"
+#include "stager.h"
 
 using namespace crec;
 
@@ -145,11 +148,26 @@ struct crec_handle {
     cudaEvent_t unused = nullptr;    // the last recognize work that read it, on the recognize stream
     bool ready = false;              // a prefetch's upload set_pages has not taken yet
     bool recorded = false;           // `unused` recorded
+    long long bytes = 0;             // what its last upload sent
   };
   PageSlot slot[2];
   int cur = 0;
   cudaEvent_t last_upload = nullptr;  // the previous set_pages / prefetch_pages call's upload
   cudaStream_t copy_stream = nullptr;
+  // pageable pages go through the stager's pinned chunks (made on first use); prefetch_pages hands
+  // its upload to the uploader thread and returns, as the reference's CudaModels does
+  // (carbon/src/cuda/pipeline_cuda.cpp:422-437, 654-672)
+  std::unique_ptr<crec::Stager> stager;
+  std::thread up_thread;
+  std::mutex up_m;
+  std::condition_variable up_cv;
+  bool up_stop = false, up_busy = false;
+  struct UpJob {
+    PageSlot* slot = nullptr;
+    std::vector<crec_page> pages;
+    std::vector<std::vector<int32_t>> runs;  // copies of the caller's row runs
+    bool has_rows = false;
+  } up_job;
   PageDesc* d_ext_pages = nullptr;  // set_pages_device's descriptors
   std::vector<PageDesc> pages;      // the current group's, device pointers
   PageDesc* d_pages = nullptr;      // and their descriptors on the device
@@ -192,6 +210,8 @@ struct crec_handle {
   const int* run_bw = nullptr;         // this run's bucket widths (host)
   // the last call's statistics, and the optional per-launch profile (CUDA events on the stream)
   long long st_runs = 0, st_launches = 0, st_h2d = 0, st_d2h = 0;
+  long long tot_h2d = 0, tot_d2h = 0;  // since open, the calls' own
+  long long up_h2d = 0;                // since open, the uploader's (under up_m)
   bool profile = false;
   std::vector<cudaEvent_t> ev_pool;  // pairs
   std::vector<int> ev_kind;          // a pair's kernel kind
@@ -201,6 +221,8 @@ struct crec_handle {
   long long prof_count[8] = {0};
   std::vector<double> lprof_ms, lprof_ops;  // by layer (and the collapse after the last)
   std::vector<long long> lprof_count;
+  // test hooks (crec_debug_inject), armed for the next run
+  bool inject_timeout = false, inject_sticky = false;
   // the last run
   int last_n = 0;
   long long last_cols = 0;
@@ -902,6 +924,12 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.mask8 = h->d_mask;
     p.out_shift = y.shift;
     p.err = h->d_err;
+    p.wait_ns = kWaitNs;
+    if (h->inject_timeout) {  // test hook: this launch's loads never come, its waits end after 1 ms
+      h->inject_timeout = false;
+      p.wait_ns = 1000000ull;
+      p.idle_producer = 1;
+    }
     const int grid = std::min(p.num_tiles, h->sms);
     ProfScope prof(h, kProfConv, static_cast<int>(li));
     if (h->int8 && l.fast) {
@@ -1102,6 +1130,10 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
   CK(cudaMemcpyAsync(out->counts, h->dp_counts, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(out->offsets, h->dp_offsets, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
+  if (h->inject_sticky) {  // test hook: the completion check fails as after a faulted kernel
+    h->inject_sticky = false;
+    CK(cudaErrorLaunchFailure);
+  }
   if (h->profile) collect_profile(h);
   if (*h->h_err)
     return set_error(h, CREC_E_TIMEOUT, "a kernel's bounded wait ran out (device error " + std::to_string(*h->h_err) + ")");
@@ -1114,6 +1146,8 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
     CK(cudaStreamSynchronize(s));
   }
   h->st_d2h += static_cast<long long>(8 * n + 12 * total);
+  h->tot_h2d += h->st_h2d;
+  h->tot_d2h += h->st_d2h;
   std::memcpy(out->lengths, h->hs_length, sizeof(int32_t) * n);
   out->total = total;
   const Run& last = runs.back();
@@ -1341,6 +1375,15 @@ int crec_open(const crec_config* config, crec_handle** out) {
 
 int crec_close(crec_handle* h) {
   if (!h) return CREC_OK;
+  if (h->up_thread.joinable()) {
+    {
+      std::lock_guard<std::mutex> lk(h->up_m);
+      h->up_stop = true;
+    }
+    h->up_cv.notify_all();
+    h->up_thread.join();
+  }
+  h->stager.reset();
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
   if (h->copy_stream) cudaStreamSynchronize(h->copy_stream);
@@ -1355,63 +1398,135 @@ void* crec_stream(crec_handle* h) { return h ? static_cast<void*>(h->stream) : n
 
 namespace {
 
+// Whether host memory is page-locked (cudaHostAlloc'd or registered): the copy engine reads it as it is.
+bool page_locked(const void* p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
 // The pages (only rows[i]'s runs where given) into a slot, queued on the copy stream once the
-// recognize work that last read the slot is done; its `done` event follows them.
-int upload_slot(crec_handle* h, crec_handle::PageSlot& sl, const crec_page* pages, int n, const crec_row_runs* rows) {
+// recognize work that last read the slot is done; its `done` event follows them.  Page-locked
+// pages are copied from where they are; pageable ones through the stager's pinned chunks.  Runs
+// on the caller's thread (set_pages) or the uploader's (prefetch_pages); it touches the slot, the
+// copy stream and the stager only (the handle's error message is the caller's to set).
+int upload_slot(crec_handle* h, crec_handle::PageSlot& sl, const crec_page* pages, int n, const crec_row_runs* rows,
+                std::string* msg) {
+  auto fail = [&](int code, const std::string& m) {
+    *msg = m;
+    return code;
+  };
+  auto cuda = [&](cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return CREC_OK;
+    cudaGetLastError();
+    return fail(e == cudaErrorMemoryAllocation ? CREC_E_NOMEM : CREC_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  };
+  int rc;
   size_t need = 0;
   for (int i = 0; i < n; ++i) need += (static_cast<size_t>(pages[i].height) * pages[i].width + 255) / 256 * 256;
   if (need > sl.cap) {
     const size_t limit = h->cfg.max_page_bytes > 0 ? static_cast<size_t>(h->cfg.max_page_bytes)
                                                    : static_cast<size_t>(h->max_pages) * 1700 * 2200;
     if (need > std::max(limit + static_cast<size_t>(n) * 256, sl.cap))
-      return set_error(h, CREC_E_RANGE, "set_pages: more page bytes than configured");
-    CK(cudaStreamSynchronize(h->stream));  // nothing queued may still read the old memory
-    CK(cudaStreamSynchronize(h->copy_stream));
+      return fail(CREC_E_RANGE, "set_pages: more page bytes than configured");
+    // nothing queued may still read the old memory
+    if ((rc = cuda(cudaStreamSynchronize(h->stream), "cudaStreamSynchronize")) ||
+        (rc = cuda(cudaStreamSynchronize(h->copy_stream), "cudaStreamSynchronize")))
+      return rc;
     cudaFree(sl.mem);
     sl.mem = nullptr;
     sl.cap = 0;
-    CK(cudaMalloc(&sl.mem, need));
+    if ((rc = cuda(cudaMalloc(&sl.mem, need), "cudaMalloc (pages)"))) return rc;
     sl.cap = need;
   }
-  if (sl.recorded) CK(cudaStreamWaitEvent(h->copy_stream, sl.unused, 0));
+  if (sl.recorded && (rc = cuda(cudaStreamWaitEvent(h->copy_stream, sl.unused, 0), "cudaStreamWaitEvent"))) return rc;
   sl.pages.resize(n);
   sl.views.assign(pages, pages + n);
+  sl.bytes = 0;
+  std::vector<RowPiece> staged;
   size_t at = 0;
-  auto rows_of = [&](const crec_page& pg, uint8_t* d, int y0, int y1) -> int {
-    if (pg.stride == pg.width) {  // contiguous rows: one copy
-      CK(cudaMemcpyAsync(d + static_cast<size_t>(y0) * pg.width, pg.data + static_cast<size_t>(y0) * pg.stride,
-                         static_cast<size_t>(y1 - y0) * pg.width, cudaMemcpyHostToDevice, h->copy_stream));
-    } else {
-      CK(cudaMemcpy2DAsync(d + static_cast<size_t>(y0) * pg.width, pg.width, pg.data + static_cast<size_t>(y0) * pg.stride,
-                           pg.stride, pg.width, y1 - y0, cudaMemcpyHostToDevice, h->copy_stream));
-    }
-    h->st_h2d += static_cast<long long>(y1 - y0) * pg.width;
-    return CREC_OK;
-  };
   for (int i = 0; i < n; ++i) {
     const crec_page& pg = pages[i];
     uint8_t* d = sl.mem + at;
     sl.pages[i] = {d, pg.width, pg.height, static_cast<long long>(pg.width)};
-    int rc;
+    const bool locked = page_locked(pg.data);
+    auto rows_of = [&](int y0, int y1) -> int {
+      const uint8_t* src = pg.data + static_cast<long long>(y0) * pg.stride;
+      uint8_t* dst = d + static_cast<size_t>(y0) * pg.width;
+      sl.bytes += static_cast<long long>(y1 - y0) * pg.width;
+      if (!locked) {
+        staged.push_back({src, pg.stride, pg.width, y1 - y0, dst});
+        return CREC_OK;
+      }
+      if (pg.stride == pg.width)  // contiguous rows: one copy
+        return cuda(cudaMemcpyAsync(dst, src, static_cast<size_t>(y1 - y0) * pg.width, cudaMemcpyHostToDevice, h->copy_stream),
+                    "cudaMemcpyAsync (pages)");
+      return cuda(cudaMemcpy2DAsync(dst, pg.width, src, pg.stride, pg.width, y1 - y0, cudaMemcpyHostToDevice, h->copy_stream),
+                  "cudaMemcpy2DAsync (pages)");
+    };
     if (rows && rows[i].count > 0 && rows[i].runs) {
       for (int r = 0; r < rows[i].count; ++r) {
         const int y0 = std::max(0, rows[i].runs[2 * r]), y1 = std::min(pg.height, rows[i].runs[2 * r + 1]);
-        if (y1 > y0 && (rc = rows_of(pg, d, y0, y1))) return rc;
+        if (y1 > y0 && (rc = rows_of(y0, y1))) return rc;
       }
-    } else if ((rc = rows_of(pg, d, 0, pg.height))) {
+    } else if ((rc = rows_of(0, pg.height))) {
       return rc;
     }
     at += (static_cast<size_t>(pg.height) * pg.width + 255) / 256 * 256;
   }
-  if (n > 0) CK(cudaMemcpyAsync(sl.d_pages, sl.pages.data(), sizeof(PageDesc) * n, cudaMemcpyHostToDevice, h->copy_stream));
-  CK(cudaEventRecord(sl.done, h->copy_stream));
-  h->last_upload = sl.done;
-  return CREC_OK;
+  if (!staged.empty()) {
+    if (!h->stager) h->stager = std::make_unique<crec::Stager>(h->device, 4);
+    if ((rc = cuda(h->stager->send(staged, h->copy_stream), "staged page upload"))) return rc;
+  }
+  if (n > 0 &&
+      (rc = cuda(cudaMemcpyAsync(sl.d_pages, sl.pages.data(), sizeof(PageDesc) * n, cudaMemcpyHostToDevice, h->copy_stream),
+                 "cudaMemcpyAsync (page descriptors)")))
+    return rc;
+  sl.bytes += static_cast<long long>(sizeof(PageDesc)) * n;
+  return cuda(cudaEventRecord(sl.done, h->copy_stream), "cudaEventRecord");
+}
+
+// The uploader thread: one prefetch's upload at a time.  A failed prefetch leaves its slot not
+// ready; the set_pages of those pages uploads them again and meets the error itself if it lasts.
+void uploader(crec_handle* h) {
+  cudaSetDevice(h->device);
+  std::unique_lock<std::mutex> lk(h->up_m);
+  for (;;) {
+    h->up_cv.wait(lk, [&] { return h->up_stop || (h->up_busy && h->up_job.slot); });
+    if (h->up_stop) return;
+    crec_handle::UpJob job = std::move(h->up_job);
+    h->up_job = {};
+    lk.unlock();
+    std::vector<crec_row_runs> rr(job.runs.size());
+    for (size_t i = 0; i < rr.size(); ++i) rr[i] = {job.runs[i].data(), static_cast<int>(job.runs[i].size() / 2)};
+    std::string msg;
+    const int rc = upload_slot(h, *job.slot, job.pages.data(), static_cast<int>(job.pages.size()),
+                               job.has_rows ? rr.data() : nullptr, &msg);
+    lk.lock();
+    if (rc) {
+      job.slot->ready = false;
+    } else {
+      h->last_upload = job.slot->done;
+      h->up_h2d += job.slot->bytes;
+    }
+    h->up_busy = false;
+    h->up_cv.notify_all();
+  }
+}
+
+// Until the uploader holds no prefetch (its copies queued, or its error met).
+void wait_uploader(crec_handle* h) {
+  std::unique_lock<std::mutex> lk(h->up_m);
+  h->up_cv.wait(lk, [&] { return !h->up_busy; });
 }
 
 // The previous call's pages are the caller's again once its upload is done (the pages of a
 // set_pages or prefetch_pages call stay alive until the next such call returns).
 int release_previous(crec_handle* h) {
+  wait_uploader(h);
   if (h->last_upload) CK(cudaEventSynchronize(h->last_upload));
   h->last_upload = nullptr;
   return CREC_OK;
@@ -1435,10 +1550,16 @@ int crec_set_pages(crec_handle* h, const crec_page* pages, int n, const crec_row
   h->st_d2h = 0;
   h->st_launches = 0;
   h->st_runs = 0;
+  if ((rc = release_previous(h))) return rc;  // a taken prefetch's upload too: done by now when it ran beside a group
   crec_handle::PageSlot& next = h->slot[1 - h->cur];
   const bool taken = next.ready && same_pages(next.views, pages, n);
-  if ((rc = release_previous(h))) return rc;  // a taken prefetch's upload too: done by now when it ran beside a group
-  if (!taken && (rc = upload_slot(h, next, pages, n, rows))) return rc;
+  if (!taken) {
+    std::string msg;
+    if ((rc = upload_slot(h, next, pages, n, rows, &msg))) return set_error(h, rc, msg);
+    h->last_upload = next.done;
+    h->tot_h2d += next.bytes;
+  }
+  h->st_h2d = next.bytes;
   next.ready = false;
   // the slot left behind is free once the recognize work queued so far is done
   crec_handle::PageSlot& old = h->slot[h->cur];
@@ -1457,9 +1578,24 @@ int crec_prefetch_pages(crec_handle* h, const crec_page* pages, int n, const cre
   CK(cudaSetDevice(h->device));
   if ((rc = release_previous(h))) return rc;
   crec_handle::PageSlot& next = h->slot[1 - h->cur];
-  next.ready = false;
-  if ((rc = upload_slot(h, next, pages, n, rows))) return rc;
+  crec_handle::UpJob job;
+  job.slot = &next;
+  job.pages.assign(pages, pages + n);
+  job.has_rows = rows != nullptr;
+  if (rows) {
+    job.runs.resize(n);
+    for (int i = 0; i < n; ++i)
+      if (rows[i].count > 0 && rows[i].runs) job.runs[i].assign(rows[i].runs, rows[i].runs + 2 * rows[i].count);
+  }
+  next.views = job.pages;  // what set_pages compares; the upload writes the same
   next.ready = true;
+  if (!h->up_thread.joinable()) h->up_thread = std::thread(uploader, h);
+  {
+    std::lock_guard<std::mutex> lk(h->up_m);
+    h->up_job = std::move(job);
+    h->up_busy = true;
+  }
+  h->up_cv.notify_all();
   return CREC_OK;
 }
 
@@ -1640,8 +1776,10 @@ int crec_ctc_greedy_noalloc(const float* logits, int n, int classes, int frames,
     if (error && error_size) std::snprintf(error, error_size, "%s", msg);
     return code;
   };
-  if (n < 0 || classes <= 0 || frames < 0 ||
-      (n > 0 && frames > 0 && (!logits || !lengths || !counts || !ids || !starts || !probs)))
+  // every line gets a count (and reads its length), so those two are needed whenever there are
+  // lines; the logits and the character arrays only when there are frames to read
+  if (n < 0 || classes <= 0 || frames < 0 || (n > 0 && (!lengths || !counts)) ||
+      (n > 0 && frames > 0 && (!logits || !ids || !starts || !probs)))
     return fail(CREC_E_INVALID, "ctc_greedy_noalloc: arguments");
   const size_t cells = static_cast<size_t>(n) * static_cast<size_t>(frames);
   if (cells > kNoAllocFrames) {
@@ -1651,17 +1789,30 @@ int crec_ctc_greedy_noalloc(const float* logits, int n, int classes, int frames,
     return fail(CREC_E_RANGE, msg);
   }
   if (n == 0) return CREC_OK;
-  void* scratch = nullptr;
-  cudaError_t e = noalloc_scratch(&scratch);
-  if (e != cudaSuccess) return fail(CREC_E_CUDA, cudaGetErrorString(e));
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (frames == 0) {  // no frames: every line has no characters; no kernel, no scratch
+    e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * static_cast<size_t>(n), s);
+    return e == cudaSuccess ? CREC_OK : fail(CREC_E_CUDA, cudaGetErrorString(e));
+  }
+  void* scratch = nullptr;
+  e = noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return fail(CREC_E_CUDA, cudaGetErrorString(e));
   int32_t* arg = static_cast<int32_t*>(scratch);
   float* prob = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kNoAllocFrames * 4);
   // nothing in the scratch needs to start at zero: the argmax writes every frame the collapse reads
-  if (frames > 0) ctc_argmax_kernel<<<n, 256, 0, s>>>(logits, classes, frames, lengths, arg, prob);
+  ctc_argmax_kernel<<<n, 256, 0, s>>>(logits, classes, frames, lengths, arg, prob);
   ctc_collapse_lines_kernel<<<(n + 127) / 128, 128, 0, s>>>(n, frames, lengths, arg, prob, ids, starts, probs, counts);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(CREC_E_CUDA, cudaGetErrorString(e));
+  return CREC_OK;
+}
+
+int crec_debug_inject(crec_handle* h, int what) {
+  if (!h) return CREC_E_INVALID;
+  if (what == CREC_INJECT_TIMEOUT) h->inject_timeout = true;
+  else if (what == CREC_INJECT_STICKY) h->inject_sticky = true;
+  else return set_error(h, CREC_E_INVALID, "debug_inject: what");
   return CREC_OK;
 }
 
@@ -1671,6 +1822,11 @@ int crec_last_stats(const crec_handle* h, crec_stats* out) {
   out->launches = h->st_launches;
   out->h2d_bytes = h->st_h2d;
   out->d2h_bytes = h->st_d2h;
+  {
+    std::lock_guard<std::mutex> lk(const_cast<crec_handle*>(h)->up_m);
+    out->h2d_total = h->tot_h2d + h->up_h2d;
+  }
+  out->d2h_total = h->tot_d2h;
   return CREC_OK;
 }
 

@@ -72,14 +72,15 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Waits for the phase of `parity` to complete, at most kWaitNs.  False on a timeout, after
+// Waits for the phase of `parity` to complete, at most limit_ns.  False on a timeout, after
 // recording `code` in *err (the first error wins).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 15) == 0 && global_ns() - t0 > kWaitNs) break;
+    if ((i & 15) == 0 && global_ns() - t0 > limit_ns) break;
   }
   if (err) atomicCAS(err, 0, code);
   return false;
@@ -104,9 +105,10 @@ __device__ __forceinline__ bool elect_one() {
 // mbar_wait by every lane of a converged warp; the vote makes the result warp-uniform, so a
 // loop that leaves on a timeout keeps its counters uniform (and the MMA and TMA operands
 // derived from them in uniform registers).
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code,
+                                               uint64_t limit_ns = kWaitNs) {
   if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code));
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code, limit_ns));
 }
 
 // TMA: a tiled box of a 3-d tensor map into shared memory, completing on `bar`.

@@ -157,7 +157,9 @@ CREC_API int crec_ctc_greedy(const float* logits, int n, int classes, int frames
  * it started.  No counterpart in the reference.  Everything is in device memory and queued on
  * `stream` without waiting: logits [n][classes][frames] (float32), lengths [n], and the outputs
  * counts [n] and ids, starts, probs [n][frames] (line i's characters at [i * frames, i * frames +
- * counts[i])), the same values as crec_ctc_greedy's.  The per-frame scratch is a 4 MiB device
+ * counts[i])), the same values as crec_ctc_greedy's.  With n > 0, lengths and counts are always
+ * required; logits, ids, starts and probs when frames > 0 (CREC_E_INVALID otherwise).  With
+ * frames == 0 no kernel runs: counts is cleared on `stream`.  The per-frame scratch is a 4 MiB device
  * array inside this library: n x frames may be at most 524,288 (CREC_E_RANGE beyond, nothing
  * queued).  Each call on a device uses the same array, so calls whose work overlaps on the GPU
  * (two streams, two threads) race: order them on one stream.  The first call on each device looks
@@ -172,9 +174,13 @@ CREC_API int crec_width_bucket(int crop_width);
  * the crop's width. */
 CREC_API int crec_crop_region(const crec_box* box, const crec_crop_rule* rule, double* region, int* width);
 
-/* What the last call did: device runs, kernel launches, bytes copied host -> device and back. */
+/* What the last call did: device runs, kernel launches, bytes copied host -> device and back
+ * (for crec_set_pages, the upload of the pages it took, whether it made that upload itself or a
+ * crec_prefetch_pages made it); and the bytes copied each way since the handle was opened (every
+ * page upload, prefetched or not, and every call's own copies). */
 typedef struct crec_stats {
   int64_t runs, launches, h2d_bytes, d2h_bytes;
+  int64_t h2d_total, d2h_total;
 } crec_stats;
 CREC_API int crec_last_stats(const crec_handle* h, crec_stats* out);
 
@@ -203,6 +209,17 @@ CREC_API int crec_profile_layers(crec_handle* h, crec_profile_entry* out, int ca
  * multiply-adds a second / 1e12. The roofline's denominator for this build's tensor kernels.
  * No counterpart in the reference (a measurement). */
 CREC_API int crec_mma_peak(int device, int precision, int n, int iters, double* tera_ops);
+
+/* Test hooks for the failure paths, armed for the next device run (no counterpart in the
+ * reference).  CREC_INJECT_TIMEOUT: the run's first dense convolution loads nothing and every
+ * wait of that launch gives up after 1 ms instead of 2 s, so its bounded waits run out: the
+ * kernel ends, the run reports CREC_E_TIMEOUT, and the handle stays usable.  CREC_INJECT_STICKY:
+ * once the run has completed, its completion check reports cudaErrorLaunchFailure (the error a
+ * faulted kernel leaves), so the handle takes the sticky-error path: CREC_E_STICKY, then
+ * crec_is_broken and CREC_E_STICKY from every later call. */
+#define CREC_INJECT_TIMEOUT 1
+#define CREC_INJECT_STICKY 2
+CREC_API int crec_debug_inject(crec_handle* h, int what);
 
 /* The CUDA stream (a cudaStream_t) the handle's work runs on, for device-side timing. */
 CREC_API void* crec_stream(crec_handle* h);

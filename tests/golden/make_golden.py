@@ -130,7 +130,7 @@ def main() -> None:
     g["rec_latin_config1"] = recs
 
     # the reference's own miniature INT8 recognizer fixture, on inputs made of bytes
-    fixture = Path("/root/reference/tests/data/native-rec.int8.onnx")
+    fixture = O.REFERENCE_ROOT / "tests" / "data" / "native-rec.int8.onnx"
     if fixture.exists():
         rng = np.random.default_rng(9)
         b = rng.integers(0, 256, (3, 32, 72)).astype(np.uint8)

@@ -447,3 +447,44 @@ def test_errors_are_reported_and_the_device_goes_on(dev8, rec_latin):
     assert len(got) == 2 and lengths.shape == (2,)
     empty, el = dev8.recognize([], np.zeros((0, 4)), 256)
     assert empty == [] and el.shape == (0,)
+
+
+def test_pageable_pinned_and_strided_pages_upload_alike(rec_latin):
+    """The same pages handed as pageable arrays (staged through the library's pinned chunks), as
+    page-locked memory (copied from where they are) and as views into wider images (rows further
+    apart than their width), with and without row runs, by set_pages and by prefetch_pages:
+    the same decodings."""
+    import torch
+    pages, boxes = synth.pages(41, 2, 1500, 1100, 10)
+    page_of = np.repeat(np.arange(2), 10).astype(np.int32)
+    allb = np.concatenate(boxes)
+    rows = [native.rows_read(b, 1100) for b in boxes]
+    pinned = []
+    for p in pages:
+        t = torch.empty(p.shape, dtype=torch.uint8, pin_memory=True)
+        t.numpy()[:] = p
+        pinned.append(t)
+    wide = []
+    for p in pages:
+        w = np.full((p.shape[0], p.shape[1] + 37), 255, np.uint8)
+        w[:, :p.shape[1]] = p
+        wide.append(w[:, :p.shape[1]])
+    dev = native.RecDevice(rec_latin[0].to_blob(), native.INT8, max_lines=64, max_width=2048, max_pages=2)
+    try:
+        dev.set_pages(pages)
+        want = dev.recognize_lines(page_of, allb)
+        for variant in ([t.numpy() for t in pinned], wide, pages):
+            for r in (None, rows):
+                dev.set_pages(variant, r)
+                got = dev.recognize_lines(page_of, allb)
+                assert np.array_equal(got[1], want[1])
+                for x, y in zip(got[0], want[0]):
+                    assert np.array_equal(x.ids, y.ids) and np.array_equal(x.probs.view(np.int32), y.probs.view(np.int32))
+                dev.prefetch_pages(variant, r)
+                dev.set_pages(variant, r)  # takes the prefetch
+                assert dev.last_stats()["h2d_bytes"] > 0
+                got = dev.recognize_lines(page_of, allb)
+                for x, y in zip(got[0], want[0]):
+                    assert np.array_equal(x.ids, y.ids) and np.array_equal(x.probs.view(np.int32), y.probs.view(np.int32))
+    finally:
+        dev.close()

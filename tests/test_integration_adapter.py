@@ -10,7 +10,9 @@ from pathlib import Path
 import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
-REF_INCLUDE = Path("/root/reference/carbon/include")
+from oracle import oracle as O  # noqa: E402
+
+REF_INCLUDE = O.REFERENCE_ROOT / "carbon" / "include"
 
 
 @pytest.mark.skipif(not (REF_INCLUDE / "carbon" / "pipeline.h").exists() or shutil.which("g++") is None,

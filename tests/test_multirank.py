@@ -19,6 +19,15 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _shard_lines(bench, rank: int, world: int, pages_total: int):
+    """The rank's lines as bench.py lays them out, page indices made global (slot numbers)."""
+    from carbon_rec import native
+    _, boxes, bws = bench.content(lambda b: native.crop_region(b)[1])
+    slots = bench.shard(rank, world, pages_total)
+    page_of, allb, bw = bench.lines_of(slots, boxes, bws)
+    return page_of + slots[0], allb, bw
+
+
 def _rank_main(rank: int, world: int, port: int, pages_total: int, out_dir: str) -> None:
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "carbon-ocr_b200"))
@@ -31,7 +40,7 @@ def _rank_main(rank: int, world: int, port: int, pages_total: int, out_dir: str)
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        _, _, page_of, boxes, bws = bench.workload(rank, world, pages_total)
+        page_of, boxes, bws = _shard_lines(bench, rank, world, pages_total)
         # each rank's own step time; the job's is the slowest rank's
         t = bench.reduce_max(0.5 + rank, world, "cpu")
         total = bench.reduce_sum(10 + rank, world, "cpu")
@@ -50,7 +59,7 @@ def test_two_ranks_shard_pages_and_take_the_max(tmp_path):
     sys.path.insert(0, str(ROOT / "carbon-ocr_b200"))
     import bench
 
-    _, _, page_of1, boxes1, bws1 = bench.workload(0, 1, pages_total)
+    page_of1, boxes1, bws1 = _shard_lines(bench, 0, 1, pages_total)
     parts = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     # every slot's lines exactly once, in slot order: rank 0 takes the first half of the slots
     assert np.array_equal(np.concatenate([p["page_of"] for p in parts]), page_of1)
@@ -59,6 +68,25 @@ def test_two_ranks_shard_pages_and_take_the_max(tmp_path):
     assert [len(p["page_of"]) for p in parts] == [pages_total // world * bench.LINES_PER_PAGE] * world
     assert all(float(p["t"]) == 0.5 + (world - 1) for p in parts)
     assert all(float(p["total"]) == 10 * world + world * (world - 1) // 2 for p in parts)
+
+
+def test_reference_arm_leaves_the_cuda_library_unloaded():
+    """The reference arm times the reference's own code: its process never maps this
+    repository's CUDA library (crop widths come from the reference's crop_region)."""
+    import subprocess
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    if not O.Reference.available():
+        pytest.skip("the reference's compiled code (oracle/_ref) is not here")
+    code = ("import sys, json; sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '0']; "
+            "import bench; bench.main(); maps = open('/proc/self/maps').read(); "
+            "print('MAPS', 'libcarbon_rec' in maps, 'libcarbon_ref' in maps)")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("{")][0]
+    out = __import__("json").loads(line)
+    assert out["impl"] == "reference" and out["value"] > 0 and out["config"]["lines"] == 65536
+    assert "MAPS False True" in r.stdout, r.stdout[-500:]
 
 
 def test_reference_arm_runs_on_rank_zero_only():

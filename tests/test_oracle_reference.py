@@ -88,7 +88,7 @@ def test_reference_fixture_through_the_compile(orc, ref):
     # package's ONNX compile and the restated executor
     from pathlib import Path
     from carbon_rec import netdef
-    f = Path("/root/reference/tests/data/native-rec.int8.onnx")
+    f = O.REFERENCE_ROOT / "tests" / "data" / "native-rec.int8.onnx"
     if not f.exists():
         pytest.skip("the reference's test data is not here")
     net = netdef.load(f)

@@ -50,3 +50,14 @@ def test_no_alloc_refuses_sizes_beyond_its_scratch():
     with pytest.raises(native.CrecError) as e:
         native.ctc_greedy_noalloc(1, 4096, 800, 256, 1, 1, 1, 1, 1)
     assert e.value.code == native.E_RANGE and "524288" in str(e.value)
+
+
+def test_no_alloc_without_frames_clears_the_counts():
+    """frames == 0: every line's count is 0 (a memset on the caller's array; no kernel)."""
+    import torch
+    n = 6
+    d_len = torch.zeros(n, dtype=torch.int32, device="cuda")
+    counts = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+    native.ctc_greedy_noalloc(0, n, 800, 0, d_len.data_ptr(), counts.data_ptr(), 0, 0, 0)
+    torch.cuda.synchronize()
+    assert counts.cpu().numpy().tolist() == [0] * n
