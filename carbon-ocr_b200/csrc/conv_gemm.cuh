@@ -286,22 +286,22 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
               const float ss[4] = {s4.x, s4.y, s4.z, s4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
               for (int u = 0; u < 4; u += 2) {
+                // two channels at a time on the packed FP32 pipe (the same roundings as scalar)
                 const int32_t a0 = static_cast<int32_t>(r[4 * k + u]), a1 = static_cast<int32_t>(r[4 * k + u + 1]);
-                float2 v;
-                v.x = __fadd_rn(__fmul_rn(magic_to_float(a0 + oo[u]), ss[u]), bb[u]);
-                v.y = __fadd_rn(__fmul_rn(magic_to_float(a1 + oo[u + 1]), ss[u + 1]), bb[u + 1]);
+                float2 v = fadd2_rn(fmul_pair_rn(magic_to_float2(a0 + oo[u], a1 + oo[u + 1]), make_float2(ss[u], ss[u + 1])),
+                                    make_float2(bb[u], bb[u + 1]));
                 if (res) {
                   const int32_t r0 = static_cast<int32_t>((rw[k] >> (8 * u)) & 0xffu);
                   const int32_t r1 = static_cast<int32_t>((rw[k] >> (8 * u + 8)) & 0xffu);
-                  v.x = __fadd_rn(v.x, __fmul_rn(magic_to_float(r0 + rzc), p.res_scale));
-                  v.y = __fadd_rn(v.y, __fmul_rn(magic_to_float(r1 + rzc), p.res_scale));
+                  v = fadd2_rn(v, fmul_pair_rn(magic_to_float2(r0 + rzc, r1 + rzc), make_float2(p.res_scale, p.res_scale)));
                 }
-                float2 q = make_float2(__fmul_rn(v.x, p.out_inv_scale), __fmul_rn(v.y, p.out_inv_scale));
+                float2 q = fmul_pair_rn(v, make_float2(p.out_inv_scale, p.out_inv_scale));
                 if (!p.sat) {
                   q.x = fminf(fmaxf(q.x, lo), hi);
                   q.y = fminf(fmaxf(q.y, lo), hi);
                 }
-                const int32_t t0 = magic_rint_bits(q.x), t1 = magic_rint_bits(q.y);
+                int32_t t0, t1;
+                magic_rint_bits2(q, t0, t1);
                 code[4 * k + u] = t0 + zc;
                 code[4 * k + u + 1] = t1 + zc;
               }
@@ -325,16 +325,26 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
               const int32_t oo[4] = {o4.x, o4.y, o4.z, o4.w};
               const float ss[4] = {s4.x, s4.y, s4.z, s4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int32_t a = static_cast<int32_t>(r[4 * k + u]);
-                const float f = static_cast<float>(a - oo[u]);
-                float v = __fadd_rn(__fmul_rn(f, ss[u]), bb[u]);
+              for (int u = 0; u < 4; u += 2) {
+                // sums past 2^22: float(s) exactly (round to nearest even) by the split conversion,
+                // two channels at a time on the packed FP32 pipe
+                const int32_t a0 = static_cast<int32_t>(r[4 * k + u]), a1 = static_cast<int32_t>(r[4 * k + u + 1]);
+                float2 v = fadd2_rn(fmul_pair_rn(exact_i2f2(a0 - oo[u], a1 - oo[u + 1]), make_float2(ss[u], ss[u + 1])),
+                                    make_float2(bb[u], bb[u + 1]));
                 if (res) {
-                  const int32_t rb = static_cast<int32_t>((rw[k] >> (8 * u)) & 0xffu);
-                  v = __fadd_rn(v, __fmul_rn(magic_to_float(rb + rzc), p.res_scale));
+                  const int32_t r0 = static_cast<int32_t>((rw[k] >> (8 * u)) & 0xffu);
+                  const int32_t r1 = static_cast<int32_t>((rw[k] >> (8 * u + 8)) & 0xffu);
+                  v = fadd2_rn(v, fmul_pair_rn(magic_to_float2(r0 + rzc, r1 + rzc), make_float2(p.res_scale, p.res_scale)));
                 }
-                const float q = fminf(fmaxf(__fmul_rn(v, p.out_inv_scale), lo), hi);
-                code[4 * k + u] = magic_rint_bits(q) + zc;
+                float2 q = fmul_pair_rn(v, make_float2(p.out_inv_scale, p.out_inv_scale));
+                if (!p.sat) {
+                  q.x = fminf(fmaxf(q.x, lo), hi);
+                  q.y = fminf(fmaxf(q.y, lo), hi);
+                }
+                int32_t t0, t1;
+                magic_rint_bits2(q, t0, t1);
+                code[4 * k + u] = t0 + zc;
+                code[4 * k + u + 1] = t1 + zc;
               }
             }
             if (cb + 16 > p.c_out) {

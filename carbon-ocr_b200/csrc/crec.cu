@@ -135,6 +135,12 @@ struct crec_handle {
   uint8_t* in_table = nullptr;
   float* head_table = nullptr;
   float* ctc_terms = nullptr;  // INT8: [256][256] exp_neg(table[q] - table[best])
+  // INT8: a run's non-blank frames for the class-order sums (the head lists them, ctc_sums_kernel adds)
+  uint8_t* d_nb_codes = nullptr;  // [frames][nb_row_bytes]
+  int32_t* d_nb_frame = nullptr;
+  int32_t* d_nb_best = nullptr;
+  int* d_nb_count = nullptr;  // [CTA][2]: listed, 255 - least best code
+  int nb_row_bytes = 0;
   // pages: two slots, the group being read and the next group's upload (prefetch_pages, on the
   // copy stream while the current group's runs go on), as the reference's CUDA device keeps them
   // (carbon/src/cuda/pipeline_cuda.cpp:407-437); or the caller's own device pages
@@ -596,7 +602,7 @@ int setup_layer(crec_handle* h, size_t li) {
     l.stages = std::min<int>(8, (200 * 1024) / l.stage_bytes);
     l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 2 * kMaxAcc) * 8 + 16 + 12 * y.cp + 64;
     if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, y.cp))) return rc;
-    if (h->int8 && l.fast) l.sat = round_first(h, l, x, y, scale, bias);
+    if (h->int8) l.sat = round_first(h, l, x, y, scale, bias);
   }
   const std::vector<uint8_t> img = weight_image(h, l, x.cp, l.nt, l.n_tiles, l.nkb);
   if ((rc = upload(h, &l.wimg, img))) return rc;
@@ -699,6 +705,98 @@ void add_run_ops(crec_handle* h, const int* bw, int a, int b) {
   }
 }
 
+// One dense convolution (layer li) over a run of `cols` input columns: its tensor maps, the
+// conv_gemm_kernel launch on the handle's stream.
+int launch_conv(crec_handle* h, size_t li, long long cols) {
+  cudaStream_t s = h->stream;
+  const Layer& l = h->l[li];
+  const Value& x = h->v[l.in];
+  const Value& y = h->v[l.out];
+  const Value& xp = h->v[x.phys];
+  const int oh = y.h;
+  const long long ow = cols >> y.shift;
+  ConvParams p{};
+  const long long in_pitch = xp.pitch;
+  const uint64_t px = static_cast<uint64_t>(x.cp) * h->eb;
+  for (int i = 0; i < l.krows; ++i) {  // input row i of a tile's group of q_rows output rows
+    const uint8_t* base = xp.base + static_cast<long long>(i - l.pt + xp.ph) * in_pitch - static_cast<long long>(l.pl) * px;
+    int rc = encode_map(h, &p.tmap[i], base, static_cast<uint64_t>(l.nkb) * 128, static_cast<uint64_t>(ow),
+                        static_cast<uint64_t>(oh / l.q_rows), static_cast<uint64_t>(l.sw) * px,
+                        static_cast<uint64_t>(l.q_rows) * l.sh * in_pitch);
+    if (rc) return rc;
+  }
+  p.wimg = l.wimg;
+  p.krows = l.krows;
+  p.q_rows = l.q_rows;
+  p.cq = l.cq;
+  p.cq_inv = (65536 + l.cq / 16 - 1) / (l.cq / 16);
+  p.nkb = l.nkb;
+  p.last_steps = l.last_steps;
+  p.nt = l.nt;
+  p.n_tiles = l.n_tiles;
+  p.oh = oh;
+  p.ow = static_cast<int>(ow);
+  p.m_per_row = static_cast<int>((ow + 127) / 128);
+  p.num_tiles = (oh / l.q_rows) * p.m_per_row * l.n_tiles;
+  p.nt_magic = div_magic(static_cast<uint32_t>(l.n_tiles));
+  p.mpr_magic = div_magic(static_cast<uint32_t>(p.m_per_row));
+  // the multiply-high divisions are exact for x * d < 2^32 (x a tile or column-block index)
+  if (static_cast<unsigned long long>(p.num_tiles) * static_cast<unsigned>(std::max(l.n_tiles, p.m_per_row)) >= (1ull << 32))
+    return set_error(h, CREC_E_RANGE, "a run with too many conv tiles");
+  p.stages = l.stages;
+  p.stage_bytes = l.stage_bytes;
+  p.a_bytes = l.a_bytes;
+  p.b_bytes = l.b_bytes;
+  p.out = y.base;
+  p.out_ph = y.ph;
+  p.out_pitch = y.pitch;
+  p.cp_out = y.cp;
+  p.c_out = l.cout;
+  p.ebytes = h->eb;
+  p.off = l.hoff;
+  p.scale = l.scale;
+  p.bias = l.dbias;
+  p.out_zero = y.zero;
+  p.relu = l.relu;
+  p.sat = l.sat;
+  p.n_acc = conv_accumulators(l.nt);
+  p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
+  if (l.residual >= 0) {
+    const Value& r = h->v[l.residual];
+    const Value& rp = h->v[r.phys];
+    p.res = rp.base;
+    p.res_ph = rp.ph;
+    p.res_cp = rp.cp;
+    p.res_shift = rp.shift - y.shift;
+    p.res_zero = r.zero;
+    p.res_pitch = rp.pitch;
+    p.res_scale = r.scale;
+  }
+  p.mask8 = h->d_mask;
+  p.out_shift = y.shift;
+  p.err = h->d_err;
+  p.wait_ns = kWaitNs;
+  if (h->inject_timeout) {  // test hook: this launch's loads never come, its waits end after 1 ms
+    h->inject_timeout = false;
+    p.wait_ns = 1000000ull;
+    p.idle_producer = 1;
+  }
+  const int grid = std::min(p.num_tiles, h->sms);
+  ProfScope prof(h, kProfConv, static_cast<int>(li));
+  if (h->int8 && l.fast) {
+    CK(cudaFuncSetAttribute(conv_gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+    conv_gemm_kernel<true, true><<<grid, kConvThreads, l.smem, s>>>(p);
+  } else if (h->int8) {
+    CK(cudaFuncSetAttribute(conv_gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+    conv_gemm_kernel<true, false><<<grid, kConvThreads, l.smem, s>>>(p);
+  } else {
+    CK(cudaFuncSetAttribute(conv_gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+    conv_gemm_kernel<false, false><<<grid, kConvThreads, l.smem, s>>>(p);
+  }
+  CK(cudaGetLastError());
+  return CREC_OK;
+}
+
 // Launches every layer for the lines laid out in h_lines (already on the device), `cols` input columns.
 int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
   cudaStream_t s = h->stream;
@@ -786,7 +884,11 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.out_zero = y.zero;
       p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
       p.table = h->head_table;
-      p.terms = h->ctc_terms;
+      p.nb_codes = h->d_nb_codes;
+      p.nb_row_bytes = h->nb_row_bytes;
+      p.nb_frame = h->d_nb_frame;
+      p.nb_best = h->d_nb_best;
+      p.nb_count = h->d_nb_count;
       p.mask8 = h->d_mask;
       p.out_shift = y.shift;
       p.frame_id = h->d_frame_id;
@@ -794,6 +896,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.logits = h->d_logits;
       p.err = h->d_err;
       const int grid = std::min(p.num_tiles, h->sms);
+      p.nb_region = (p.num_tiles + grid - 1) / grid * 128;
       ProfScope prof(h, kProfHead, static_cast<int>(li));
       if (h->int8 && l.fast) {
         CK(cudaFuncSetAttribute(head_ctc_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
@@ -806,6 +909,14 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
         head_ctc_kernel<false, false><<<grid, kHeadThreads, l.smem, s>>>(p);
       }
       CK(cudaGetLastError());
+      if (h->int8) {  // the listed frames' class-order sums
+        ProfScope sums(h, kProfHead, static_cast<int>(li));
+        const int smem = kSumRows * 256 * static_cast<int>(sizeof(float));
+        CK(cudaFuncSetAttribute(ctc_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        ctc_sums_kernel<<<grid, kSumThreads, smem, s>>>(h->d_nb_codes, h->nb_row_bytes, h->d_nb_frame, h->d_nb_best,
+                                                        h->d_nb_count, p.nb_region, h->ctc_terms, l.cout, h->d_frame_prob);
+        CK(cudaGetLastError());
+      }
       continue;
     }
     if (l.kind == kKindDw) {
@@ -864,85 +975,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       CK(cudaGetLastError());
       continue;
     }
-    ConvParams p{};
-    const long long in_pitch = xp.pitch;
-    const uint64_t px = static_cast<uint64_t>(x.cp) * h->eb;
-    for (int i = 0; i < l.krows; ++i) {  // input row i of a tile's group of q_rows output rows
-      const uint8_t* base = xp.base + static_cast<long long>(i - l.pt + xp.ph) * in_pitch - static_cast<long long>(l.pl) * px;
-      int rc = encode_map(h, &p.tmap[i], base, static_cast<uint64_t>(l.nkb) * 128, static_cast<uint64_t>(ow),
-                          static_cast<uint64_t>(oh / l.q_rows), static_cast<uint64_t>(l.sw) * px,
-                          static_cast<uint64_t>(l.q_rows) * l.sh * in_pitch);
-      if (rc) return rc;
-    }
-    p.wimg = l.wimg;
-    p.krows = l.krows;
-    p.q_rows = l.q_rows;
-    p.cq = l.cq;
-    p.cq_inv = (65536 + l.cq / 16 - 1) / (l.cq / 16);
-    p.nkb = l.nkb;
-    p.last_steps = l.last_steps;
-    p.nt = l.nt;
-    p.n_tiles = l.n_tiles;
-    p.oh = oh;
-    p.ow = static_cast<int>(ow);
-    p.m_per_row = static_cast<int>((ow + 127) / 128);
-    p.num_tiles = (oh / l.q_rows) * p.m_per_row * l.n_tiles;
-    p.nt_magic = div_magic(static_cast<uint32_t>(l.n_tiles));
-    p.mpr_magic = div_magic(static_cast<uint32_t>(p.m_per_row));
-    // the multiply-high divisions are exact for x * d < 2^32 (x a tile or column-block index)
-    if (static_cast<unsigned long long>(p.num_tiles) * static_cast<unsigned>(std::max(l.n_tiles, p.m_per_row)) >= (1ull << 32))
-      return set_error(h, CREC_E_RANGE, "a run with too many conv tiles");
-    p.stages = l.stages;
-    p.stage_bytes = l.stage_bytes;
-    p.a_bytes = l.a_bytes;
-    p.b_bytes = l.b_bytes;
-    p.out = y.base;
-    p.out_ph = y.ph;
-    p.out_pitch = y.pitch;
-    p.cp_out = y.cp;
-    p.c_out = l.cout;
-    p.ebytes = h->eb;
-    p.off = l.hoff;
-    p.scale = l.scale;
-    p.bias = l.dbias;
-    p.out_zero = y.zero;
-    p.relu = l.relu;
-    p.sat = l.sat;
-    p.n_acc = conv_accumulators(l.nt);
-    p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
-    if (l.residual >= 0) {
-      const Value& r = h->v[l.residual];
-      const Value& rp = h->v[r.phys];
-      p.res = rp.base;
-      p.res_ph = rp.ph;
-      p.res_cp = rp.cp;
-      p.res_shift = rp.shift - y.shift;
-      p.res_zero = r.zero;
-      p.res_pitch = rp.pitch;
-      p.res_scale = r.scale;
-    }
-    p.mask8 = h->d_mask;
-    p.out_shift = y.shift;
-    p.err = h->d_err;
-    p.wait_ns = kWaitNs;
-    if (h->inject_timeout) {  // test hook: this launch's loads never come, its waits end after 1 ms
-      h->inject_timeout = false;
-      p.wait_ns = 1000000ull;
-      p.idle_producer = 1;
-    }
-    const int grid = std::min(p.num_tiles, h->sms);
-    ProfScope prof(h, kProfConv, static_cast<int>(li));
-    if (h->int8 && l.fast) {
-      CK(cudaFuncSetAttribute(conv_gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-      conv_gemm_kernel<true, true><<<grid, kConvThreads, l.smem, s>>>(p);
-    } else if (h->int8) {
-      CK(cudaFuncSetAttribute(conv_gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-      conv_gemm_kernel<true, false><<<grid, kConvThreads, l.smem, s>>>(p);
-    } else {
-      CK(cudaFuncSetAttribute(conv_gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-      conv_gemm_kernel<false, false><<<grid, kConvThreads, l.smem, s>>>(p);
-    }
-    CK(cudaGetLastError());
+    if (int rc = launch_conv(h, li, cols)) return rc;
   }
   CollapseParams c{};
   c.frame_id = h->d_frame_id;
@@ -1178,6 +1211,10 @@ void free_all(crec_handle* h) {
   cudaFree(h->in_table);
   cudaFree(h->head_table);
   cudaFree(h->ctc_terms);
+  cudaFree(h->d_nb_codes);
+  cudaFree(h->d_nb_frame);
+  cudaFree(h->d_nb_best);
+  cudaFree(h->d_nb_count);
   for (auto& sl : h->slot) {
     cudaFree(sl.mem);
     cudaFree(sl.d_pages);
@@ -1285,6 +1322,15 @@ int open_impl(crec_handle* h, const crec_config* c) {
   if ((rc = host_alloc(h, &h->h_err, 1)) || (rc = host_alloc(h, &h->h_total, 1)) ||
       (rc = dev_alloc(h, &h->d_total, 1)))
     return rc;
+  if (h->int8) {
+    // the head's list: CTA b's part from b * region on, region = ceil(tiles / grid) x 128 entries
+    h->nb_row_bytes = round16(h->v[h->outv].c);
+    const size_t tiles = (frames + 127) / 128, entries = (tiles + h->sms - 1) / h->sms * h->sms * 128;
+    if ((rc = dev_alloc(h, &h->d_nb_codes, entries * static_cast<size_t>(h->nb_row_bytes))) ||
+        (rc = dev_alloc(h, &h->d_nb_frame, entries)) || (rc = dev_alloc(h, &h->d_nb_best, entries)) ||
+        (rc = dev_alloc(h, &h->d_nb_count, 2 * static_cast<size_t>(h->sms))))
+      return rc;
+  }
   if (crop_smem_bytes(h, c->max_width) > 232448) return set_error(h, CREC_E_INVALID, "max_width: the crop kernel's shared memory");
   return CREC_OK;
 }

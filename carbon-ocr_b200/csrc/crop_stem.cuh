@@ -762,15 +762,25 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
           const float4 b4 = *reinterpret_cast<const float4*>(sbias + j);
           const int32_t oo[4] = {o4.x, o4.y, o4.z, o4.w};
           const float ss[4] = {s4.x, s4.y, s4.z, s4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
-          int32_t code[4];
+          int32_t code[4], acc[4];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            int32_t acc = dp4a_us(a[0], w[3 * u], oo[u]);
-            acc = dp4a_us(a[1], w[3 * u + 1], acc);
-            acc = dp4a_us(a[2], w[3 * u + 2], acc);
-            const float v = __fadd_rn(__fmul_rn(magic_to_float(acc), ss[u]), bb[u]);
-            const float q0 = __fmul_rn(v, p.out_inv_scale);
-            code[u] = magic_rint_bits(kRound ? q0 : fminf(fmaxf(q0, lo), hi)) + zc;
+            acc[u] = dp4a_us(a[0], w[3 * u], oo[u]);
+            acc[u] = dp4a_us(a[1], w[3 * u + 1], acc[u]);
+            acc[u] = dp4a_us(a[2], w[3 * u + 2], acc[u]);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; u += 2) {  // two channels at a time on the packed FP32 pipe
+            float2 q = out_stage2(acc[u], acc[u + 1], make_float2(ss[u], ss[u + 1]), make_float2(bb[u], bb[u + 1]),
+                                  p.out_inv_scale);
+            if (!kRound) {
+              q.x = fminf(fmaxf(q.x, lo), hi);
+              q.y = fminf(fmaxf(q.y, lo), hi);
+            }
+            int32_t t0, t1;
+            magic_rint_bits2(q, t0, t1);
+            code[u] = t0 + zc;
+            code[u + 1] = t1 + zc;
           }
           wv[c4] = pack_sat_u8x4(code);
         }

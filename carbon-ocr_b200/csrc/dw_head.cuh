@@ -215,10 +215,15 @@ __global__ void __launch_bounds__(256) dw_row_kernel(const __grid_constant__ DwP
       const float ss[4] = {s4.x, s4.y, s4.z, s4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
       int32_t code[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float v = __fadd_rn(__fmul_rn(magic_to_float(acc[4 * k + u]), ss[u]), bb[u]);
-        const float q = fminf(fmaxf(__fmul_rn(v, p.out_inv_scale), lo), hi);
-        code[u] = c0 + 4 * k + u < p.c ? magic_rint_bits(q) + zc : p.out_zero;
+      for (int u = 0; u < 4; u += 2) {  // two channels at a time on the packed FP32 pipe
+        float2 q = out_stage2(acc[4 * k + u], acc[4 * k + u + 1], make_float2(ss[u], ss[u + 1]),
+                              make_float2(bb[u], bb[u + 1]), p.out_inv_scale);
+        q.x = fminf(fmaxf(q.x, lo), hi);
+        q.y = fminf(fmaxf(q.y, lo), hi);
+        int32_t t0, t1;
+        magic_rint_bits2(q, t0, t1);
+        code[u] = c0 + 4 * k + u < p.c ? t0 + zc : p.out_zero;
+        code[u + 1] = c0 + 4 * k + u + 1 < p.c ? t1 + zc : p.out_zero;
       }
       wv[k] = __byte_perm(__byte_perm(code[0], code[1], 0x0040), __byte_perm(code[2], code[3], 0x0040), 0x5410);
     }
@@ -301,7 +306,10 @@ __global__ void __launch_bounds__(256) dw_row_f16_kernel(const __grid_constant__
 // exp_neg(table[q_c] - table[q_best])), table[q] = (q - zero) * scale
 // (carbon/src/net/net.cpp:1101-1128).  A term depends only on (q_c, q_best), so the 65,536
 // possible terms are computed once per model (ctc_terms_kernel, the same float operations) and
-// the sums only add them, in class order.
+// the sums only add them, in class order.  A sum is a chain of `classes` dependent adds, so it
+// is not done here, where a tile's few non-blank frames would hold up its 16 epilogue warps:
+// each non-blank frame's codes go out to the run's list (nb_codes), and ctc_sums_kernel adds
+// them up over the whole GPU.
 // FP16: the FP32 logits (sum + bias); each (half, part) keeps an online maximum and sum of 2^x
 // terms, the four merged per frame.
 // Only each frame's id and probability leave the kernel; the logits are never written.
@@ -317,7 +325,12 @@ struct HeadParams {
   int out_zero;
   float out_inv_scale;
   const float* table;  // INT8 [256]: the u8 logits' values
-  const float* terms;  // INT8 [256 best][256 q]: exp_neg(table[q] - table[best])
+  uint8_t* nb_codes;   // INT8: the run's non-blank frames' class codes, row k at k * nb_row_bytes
+  int nb_row_bytes;    // classes rounded up to 16
+  int32_t* nb_frame;   // INT8 [listed]: the frame column of list entry k
+  int32_t* nb_best;    // INT8 [listed]: its best code
+  int nb_region;       // INT8: list entries a CTA owns (CTA b's from b * nb_region on)
+  int* nb_count;       // INT8 [grid][2]: each CTA's frames listed and 255 - its smallest best code listed
   const uint8_t* mask8;
   int out_shift;
   int32_t* frame_id;   // [ow]
@@ -338,7 +351,7 @@ __host__ __device__ constexpr int head_code_stride(int classes) {
 
 // Bytes of the head's shared memory after A, B and the codes: barriers, per-class constants,
 // the per-frame merge slots and the list of non-blank frames.
-__host__ __device__ constexpr int head_tail_bytes(int ncls) { return 128 + 12 * ncls + (3 * 512 + 3 * 128 + 2) * 4; }
+__host__ __device__ constexpr int head_tail_bytes(int ncls) { return 128 + 12 * ncls + (3 * 512 + 3 * 128 + 4) * 4; }
 
 // carbon/src/cpu/kernels.h:216-250 (exp_neg), each multiply and add rounded on its own.
 __device__ __forceinline__ float exp_neg_d(float x) {
@@ -397,7 +410,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
   int32_t* nb_row = reinterpret_cast<int32_t*>(s_hsum + 512);  // INT8: the tile's non-blank frames' rows
   int32_t* nb_q = nb_row + 128;                                 // and best codes
   int32_t* s_best = nb_q + 128;                                 // each row's best class
-  volatile int32_t* s_count = s_best + 128;                     // [0] frames listed, [1] abort
+  volatile int32_t* s_count = s_best + 128;  // [0] frames listed, [1] abort, [2] their place in the run's list, [3] 255 - least best
   __shared__ float tab[256];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -406,7 +419,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
     s_scale[j] = kInt8 ? p.scale[j] : 0.0f;
     s_bias[j] = p.bias[j];
   }
-  if (threadIdx.x < 2) s_count[threadIdx.x] = 0;
+  if (threadIdx.x < 4) s_count[threadIdx.x] = 0;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) tab[i] = kInt8 ? p.table[i] : 0.0f;
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
@@ -503,7 +516,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       const int ox = t * 128 + row;
-      int32_t mx = 0;                                   // INT8: this half's highest code
+      int32_t mx = -1;                                  // INT8: this part's highest code
+      int fi = 0;                                       // INT8: the first class holding it
       float fm = -INFINITY, fsum = 0.0f;                // FP16: this half's highest logit and sum
       int fbest = 0;
       for (int c = half; c < p.chunks && ok; c += 2) {
@@ -528,14 +542,19 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
               const int32_t oo[4] = {o.x, o.y, o.z, o.w};
               const float ss[4] = {sc.x, sc.y, sc.z, sc.w}, bv[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int32_t acc = static_cast<int32_t>(r[4 * k + u]);
-                // carbon/src/net/net.cpp:703-720: (acc - zero * colsum) * scale + bias, requantized
-                const float f = kFast ? magic_to_float(acc + oo[u]) : static_cast<float>(acc - oo[u]);
-                const float v = __fadd_rn(__fmul_rn(f, ss[u]), bv[u]);
-                float q = __fmul_rn(v, p.out_inv_scale);
-                q = fminf(fmaxf(q, lo), hi);
-                code[4 * k + u] = magic_rint_bits(q) + zc;  // in [0, 255]
+              for (int u = 0; u < 4; u += 2) {
+                // carbon/src/net/net.cpp:703-720: (acc - zero * colsum) * scale + bias, requantized;
+                // two classes at a time on the packed FP32 pipe (the same roundings)
+                const int32_t a0 = static_cast<int32_t>(r[4 * k + u]), a1 = static_cast<int32_t>(r[4 * k + u + 1]);
+                const float2 f = kFast ? magic_to_float2(a0 + oo[u], a1 + oo[u + 1]) : exact_i2f2(a0 - oo[u], a1 - oo[u + 1]);
+                float2 q = fmul_pair_rn(fadd2_rn(fmul_pair_rn(f, make_float2(ss[u], ss[u + 1])), make_float2(bv[u], bv[u + 1])),
+                                    make_float2(p.out_inv_scale, p.out_inv_scale));
+                q.x = fminf(fmaxf(q.x, lo), hi);
+                q.y = fminf(fmaxf(q.y, lo), hi);
+                int32_t t0, t1;
+                magic_rint_bits2(q, t0, t1);
+                code[4 * k + u] = t0 + zc;  // in [0, 255]
+                code[4 * k + u + 1] = t1 + zc;
               }
             }
             uint4 packed;
@@ -555,7 +574,19 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
             for (int i = 0; i < 8; ++i) m8[i] = max(code[i], code[i + 8]);
 #pragma unroll
             for (int i = 0; i < 4; ++i) m8[i] = max(m8[i], m8[i + 4]);
-            mx = max(mx, max(max(m8[0], m8[1]), max(m8[2], m8[3])));
+            const int32_t m16 = max(max(m8[0], m8[1]), max(m8[2], m8[3]));
+            if (m16 > mx) {  // a new highest code: the first of this group's classes holding it (the
+                             // classes come in increasing order, so the earlier holder is kept on a tie;
+                             // bytes past `classes` follow the real ones and never come first)
+              mx = m16;
+              const uint32_t m4 = static_cast<uint32_t>(m16) * 0x01010101u;
+              const uint32_t f0 = first_byte_eq(pw[0], m4), f1 = first_byte_eq(pw[1], m4);
+              const uint32_t f2 = first_byte_eq(pw[2], m4), f3 = first_byte_eq(pw[3], m4);
+              fi = j0 + (f0   ? (__ffs(f0) - 1) >> 3
+                         : f1 ? 4 + ((__ffs(f1) - 1) >> 3)
+                         : f2 ? 8 + ((__ffs(f2) - 1) >> 3)
+                              : 12 + ((__ffs(f3) - 1) >> 3));
+            }
           } else {
             float v[16];
 #pragma unroll
@@ -626,6 +657,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
       if (!ok) s_count[1] = 1;
       if constexpr (kInt8) {
         s_hmax[slot * 128 + row] = mx;
+        s_hbest[slot * 128 + row] = fi;
       } else {
         s_hmax[slot * 128 + row] = __float_as_int(fm);
         s_hbest[slot * 128 + row] = fbest;
@@ -636,27 +668,20 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
       const bool valid = ox < p.ow && p.mask8[(static_cast<long long>(ox) << p.out_shift) >> 3] != 0;
       if (slot == 0) {
         if constexpr (kInt8) {
-          // the first class with the highest code: for a blank frame the first 16 bytes hold it
+          // the highest code and the first class holding it (ties: the lower class, as
+          // carbon/src/cpu/kernels.cpp:799-828 takes it): the lowest first class among the parts
+          // whose highest code it is
           const int32_t m = max(max(s_hmax[row], s_hmax[128 + row]), max(s_hmax[256 + row], s_hmax[384 + row]));
-          const uint32_t m4 = static_cast<uint32_t>(m) * 0x01010101u;
-          int best = 0;
-          for (int j0 = 0; j0 < p.classes; j0 += 16) {
-            const uint4 w = *reinterpret_cast<const uint4*>(my + j0);
-            const uint32_t f0 = first_byte_eq(w.x, m4), f1 = first_byte_eq(w.y, m4);
-            const uint32_t f2 = first_byte_eq(w.z, m4), f3 = first_byte_eq(w.w, m4);
-            if (f0 | f1 | f2 | f3) {
-              best = j0 + (f0   ? (__ffs(f0) - 1) >> 3
-                           : f1 ? 4 + ((__ffs(f1) - 1) >> 3)
-                           : f2 ? 8 + ((__ffs(f2) - 1) >> 3)
-                                : 12 + ((__ffs(f3) - 1) >> 3));
-              break;
-            }
-          }
+          int best = 0x7fffffff;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (s_hmax[i * 128 + row] == m) best = min(best, s_hbest[i * 128 + row]);
           s_best[row] = best;
           if (valid && best != 0) {
             const int k = atomicAdd(const_cast<int32_t*>(&s_count[0]), 1);
             nb_row[k] = row;
             nb_q[k] = m;
+            atomicMax(const_cast<int32_t*>(&s_count[3]), 255 - m);
           } else if (valid) {
             p.frame_id[ox] = 0;
             p.frame_prob[ox] = 0.0f;
@@ -688,51 +713,95 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
       }
       named_bar(1, 512);
       if constexpr (kInt8) {
-        // the class-order sums of the listed (non-blank) frames, a thread a frame
-        const int listed = s_count[0];
+        // the listed (non-blank) frames to this CTA's part of the run's list: their ids now,
+        // their codes for the class-order sums (ctc_sums_kernel)
+        const int listed = s_count[0], base = blockIdx.x * p.nb_region + s_count[2];
+        const int w16 = p.nb_row_bytes >> 4;
+        for (int i = e; i < listed * w16; i += 512) {
+          const int k = i / w16, j = i - k * w16;
+          *reinterpret_cast<uint4*>(p.nb_codes + static_cast<long long>(base + k) * p.nb_row_bytes + 16 * j) =
+              *reinterpret_cast<const uint4*>(codes + nb_row[k] * cstride + 16 * j);
+        }
         for (int k = e; k < listed; k += 512) {
-          const int r = nb_row[k];
-          const uint8_t* rowc = codes + r * cstride;
-          const float* trow = p.terms + nb_q[k] * 256;
-          // batches of 16 terms, the next batch's loads in flight while the current is added
-          // (the adds stay in class order)
-          auto load16 = [&](int j0, float (&dst)[16]) {
-            const uint4 w = *reinterpret_cast<const uint4*>(rowc + j0);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int i = 0; i < 16; ++i) dst[i] = __ldg(trow + ((ww[i >> 2] >> (8 * (i & 3))) & 0xff));
-          };
-          const int full = p.classes & ~15;
-          float sum = 0.0f, cur[16], nxt[16];
-          int j0 = 0;
-          if (full >= 16) load16(0, cur);
-          for (; j0 + 32 <= full; j0 += 32) {
-            load16(j0 + 16, nxt);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, cur[i]);
-            if (j0 + 48 <= full) load16(j0 + 32, cur);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, nxt[i]);
-          }
-          if (j0 + 16 <= full) {  // one batch left, in cur
-#pragma unroll
-            for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, cur[i]);
-            j0 += 16;
-          }
-          for (; j0 < p.classes; ++j0) sum = __fadd_rn(sum, __ldg(trow + rowc[j0]));
-          const int fx = t * 128 + r;
-          p.frame_id[fx] = s_best[r];
-          p.frame_prob[fx] = __fdiv_rn(1.0f, sum);
+          const int fx = t * 128 + nb_row[k];
+          p.nb_frame[base + k] = fx;
+          p.nb_best[base + k] = nb_q[k];
+          p.frame_id[fx] = s_best[nb_row[k]];
         }
         named_bar(1, 512);
-        if (e == 0) s_count[0] = 0;  // read by every thread before the barrier; the next adds follow the next one
+        if (e == 0) {  // read by every thread before the barrier; the next list follows the next one
+          s_count[2] += listed;
+          s_count[0] = 0;
+        }
       }
+    }
+    if (kInt8 && e == 0) {  // this CTA's list for the sums
+      p.nb_count[2 * blockIdx.x] = s_count[2];
+      p.nb_count[2 * blockIdx.x + 1] = s_count[3];
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, kTmemColsHead);
+}
+
+// ---------------------------------------------------------------- class-order sums
+//
+// The probability of each listed (non-blank) frame: 1 / (the sum over classes, in class order, of
+// terms[best][q_c]) (carbon/src/cpu/kernels.cpp:799-828), a thread a frame.  The terms rows of
+// the best codes a run lists (codes from the least listed one up, at most kSumRows rows) are
+// staged in shared memory, so the chain of dependent adds reads its terms there; a frame whose
+// best code is below them reads its row from global memory.
+constexpr int kSumRows = 192;
+constexpr int kSumThreads = 512;
+
+template <bool kShared>
+__device__ __forceinline__ float class_sum(const uint8_t* row, int classes, const float* trow) {
+  float sum = 0.0f;
+  const uint4* r4 = reinterpret_cast<const uint4*>(row);
+  const int full = classes & ~15;
+  uint4 w = full ? __ldg(r4) : make_uint4(0, 0, 0, 0);
+  for (int j0 = 0; j0 < full; j0 += 16) {
+    const uint4 cur = w;
+    if (j0 + 16 < full) w = __ldg(r4 + (j0 >> 4) + 1);  // the next 16 codes in flight
+    const uint32_t ww[4] = {cur.x, cur.y, cur.z, cur.w};
+    float t[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t q = (ww[i >> 2] >> (8 * (i & 3))) & 0xffu;
+      t[i] = kShared ? trow[q] : __ldg(trow + q);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, t[i]);
+  }
+  for (int j = full; j < classes; ++j) {
+    const uint32_t q = row[j];
+    sum = __fadd_rn(sum, kShared ? trow[q] : __ldg(trow + q));
+  }
+  return sum;
+}
+
+// CTA b takes the list part the head's CTA b wrote (the same grid).
+__global__ void __launch_bounds__(kSumThreads) ctc_sums_kernel(const uint8_t* nb_codes, int row_bytes,
+                                                               const int32_t* nb_frame, const int32_t* nb_best,
+                                                               const int* nb_count, int nb_region, const float* terms,
+                                                               int classes, float* frame_prob) {
+  extern __shared__ __align__(16) float srows[];  // [rows][256]: terms rows lo .. 255
+  const int count = nb_count[2 * blockIdx.x];
+  if (count == 0) return;
+  const int lo = max(255 - nb_count[2 * blockIdx.x + 1], 256 - kSumRows);
+  const long long first = static_cast<long long>(blockIdx.x) * nb_region;
+  const float4* src = reinterpret_cast<const float4*>(terms + static_cast<size_t>(lo) * 256);
+  for (int i = threadIdx.x; i < (256 - lo) * 64; i += blockDim.x) reinterpret_cast<float4*>(srows)[i] = __ldg(src + i);
+  __syncthreads();
+  for (long long k = first + threadIdx.x; k < first + count; k += blockDim.x) {
+    const int b = nb_best[k];
+    const uint8_t* row = nb_codes + k * row_bytes;
+    const float sum = b >= lo ? class_sum<true>(row, classes, srows + (b - lo) * 256)
+                              : class_sum<false>(row, classes, terms + static_cast<size_t>(b) * 256);
+    frame_prob[nb_frame[k]] = __fdiv_rn(1.0f, sum);
+  }
 }
 
 // ---------------------------------------------------------------- collapse

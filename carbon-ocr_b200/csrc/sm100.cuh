@@ -247,6 +247,49 @@ __device__ __forceinline__ float magic_to_float(int32_t biased) { return __fsub_
 // rint(x) + kMagicBits for |x| <= 2^22 (round to nearest, ties to even, as __float2int_rn).
 __device__ __forceinline__ int32_t magic_rint_bits(float x) { return __float_as_int(__fadd_rn(x, kMagic)); }
 
+// Packed FP32 pairs (PTX add.rn.f32x2, sm_100): each half rounded to nearest even on its own,
+// the same bits as __fadd_rn on each half (checked on 2^33 random pairs and on exact ties: no
+// difference), one instruction for two.  Only the adds are packed: a packed product
+// (mul.rn.f32x2) whose one use is a packed add is fused with it into one fused multiply-add by the
+// assembler, despite the explicit rounding (measured: a quarter of such chains lose the product's
+// rounding), while products from the scalar pipe feeding a packed add keep both roundings
+// (measured: none differ).  So every product here is a __fmul_rn.
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 a, b, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n add.rn.f32x2 d, a, b;\n"
+      " mov.b64 {%0, %1}, d;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fmul_pair_rn(float2 a, float2 b) {
+  return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
+}
+// Two biased sums (s + kMagicBits each, |s| < 2^22) as floats.
+__device__ __forceinline__ float2 magic_to_float2(int32_t b0, int32_t b1) {
+  return fadd2_rn(make_float2(__int_as_float(b0), __int_as_float(b1)), make_float2(-kMagic, -kMagic));
+}
+// The INT8 output stage of two sums (given biased, + kMagicBits) up to the code's rounding:
+// (s * scale + bias) * inv_scale, each operation rounded on its own (the reference's
+// epilogue_scalar, carbon/src/cpu/kernels.h:354-380, without residual or ReLU).
+__device__ __forceinline__ float2 out_stage2(int32_t b0, int32_t b1, float2 scale, float2 bias, float inv) {
+  return fmul_pair_rn(fadd2_rn(fmul_pair_rn(magic_to_float2(b0, b1), scale), bias), make_float2(inv, inv));
+}
+// float(s) rounded to nearest even for any int32 s, both halves, without the conversion unit:
+// s = hi + lo with lo = s & 0xfff and hi = (s >> 12) * 4096; both are exact floats (lo below 2^12,
+// hi / 4096 below 2^19 in magnitude, through kMagic), so their one rounded sum is float(s).
+__device__ __forceinline__ float2 exact_i2f2(int32_t s0, int32_t s1) {
+  const float2 hi = fmul_pair_rn(magic_to_float2(kMagicBits + (s0 >> 12), kMagicBits + (s1 >> 12)), make_float2(4096.0f, 4096.0f));
+  const float2 lo = magic_to_float2((s0 & 0xfff) | kMagicBits, (s1 & 0xfff) | kMagicBits);
+  return fadd2_rn(hi, lo);
+}
+// rint of both halves + kMagicBits (|x| <= 2^22).
+__device__ __forceinline__ void magic_rint_bits2(float2 x, int32_t& r0, int32_t& r1) {
+  const float2 t = fadd2_rn(x, make_float2(kMagic, kMagic));
+  r0 = __float_as_int(t.x);
+  r1 = __float_as_int(t.y);
+}
+
 // Bytes hi and lo, each saturated to [0, 255], above them the low 16 bits of `upper`:
 // upper << 16 | sat(hi) << 8 | sat(lo) (PTX cvt.pack.sat.u8.s32.b32).
 __device__ __forceinline__ uint32_t pack_sat_u8x2(int32_t hi, int32_t lo, uint32_t upper) {
