@@ -67,6 +67,7 @@ def parse(argv=None):
     ap.add_argument("--no-fp16", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="config 4's kernel sweep instead (one GPU)")
     return ap.parse_args(argv)
 
 
@@ -283,8 +284,44 @@ def run_reference(args, rank: int, world: int):
     return 0
 
 
+def run_sweep(args) -> int:
+    """3x3 stride-1 convolutions C -> C for N = 256 lines of [H][W][C],
+    C in {32, 64, 128, 256}, H in {8, 16, 32}, W in {128, 512, 1024}, INT8 and FP16, through the
+    recognizer's implicit-GEMM kernel (crec_conv_sweep, inputs resident, the mean of `steps` launches
+    after one warm-up, CUDA events): TOPS and the fraction of this GPU's measured tcgen05 rate."""
+    import torch  # noqa: F401  (the CUDA context)
+    from carbon_rec import model, native, netdef
+    peaks = {native.INT8: native.mma_peak(0, native.INT8, 256), native.FP16: native.mma_peak(0, native.FP16, 256)}
+    rng = np.random.default_rng(4)
+    n = 256
+    base8 = rng.integers(0, 256, n * 32 * 1024 * 256, dtype=np.uint8)
+    base16 = (base8[: n * 32 * 1024 * 256].view(np.int8).astype(np.float16) / np.float16(40.0))
+    rows = []
+    for prec, name in ((native.INT8, "int8"), (native.FP16, "fp16")):
+        for c in (32, 64, 128, 256):
+            for h in (8, 16, 32):
+                for w in (128, 512, 1024):
+                    fp, i8, _ = model.make_conv(c, c, h, seed=c + h + w)
+                    blob = netdef.compile_model(i8 if prec == native.INT8 else fp).to_blob()
+                    size = n * h * w * c
+                    x = (base8 if prec == native.INT8 else base16)[:size].reshape(n, h, w, c)
+                    _, ms = native.conv_sweep(blob, prec, x, c, repeat=max(1, args.steps))
+                    ops = 2.0 * n * h * w * c * c * 9
+                    tops = ops / (ms * 1e-3) / 1e12
+                    rows.append({"precision": name, "c": c, "h": h, "w": w, "ms": round(ms, 4), "tops": round(tops, 1),
+                                 "frac": round(tops / peaks[prec], 4)})
+    out = {"metric": "config 4 kernel sweep: 3x3 s1 implicit-GEMM conv TOPS (N=256 lines)", "unit": "TOP/s",
+           "peaks_measured": {"int8_n256_tops": peaks[native.INT8], "fp16_n256_tflops": peaks[native.FP16]},
+           "timing": f"CUDA events, mean of {max(1, args.steps)} launches after a warm-up, inputs resident",
+           "shapes": rows}
+    print(json.dumps(out))
+    return 0
+
+
 def main() -> int:
     args = parse()
+    if args.sweep:
+        return run_sweep(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -295,3 +295,44 @@ def make_rec_latin(seed: int = 0, calib_lines: int = 24):
     crops = synthetic_crops(rng, calib_lines, 256, 256)
     quant = calibrate(w, np.stack(crops))
     return w, quant, build_onnx(w, None), build_onnx(w, quant)
+
+
+# ----------------------------------------------------------------------------- kernel sweep layers
+
+def make_conv(c_in: int, c_out: int, height: int, seed: int = 0, stride: int = 1, relu: bool = False,
+              calib_width: int = 64):
+    """BASELINE.json config 4's layer: one 3x3 convolution, pad 1, stride (stride, stride), c_in -> c_out
+    (He-normal weights and small biases from `seed`; a ReLU when asked), on inputs [N, c_in, height, W]:
+    (fp32 ONNX, int8 Q/DQ ONNX, (input scale, input zero point)).  The INT8 file quantizes the
+    input ~N(0, 1) per tensor and the output by MinMax over a float run on a seeded sample."""
+    rng = np.random.default_rng(seed)
+    std = np.sqrt(2.0 / (c_in * 9))
+    w = {"conv.w": rng.normal(0.0, std, (c_out, c_in, 3, 3)).astype(np.float32),
+         "conv.b": rng.normal(0.0, 0.05, c_out).astype(np.float32)}
+
+    def build(quant):
+        b = _Builder(quant, w)
+        x = b.qdq("x")
+        y = b.conv("conv", x, 3, 3, stride, stride, (1, 1, 1, 1), relu)
+        out = y
+        if quant is not None:
+            # quantized inside the graph, then an Identity and the output's Q/DQ (as rec-latin's head
+            # ends: its codes leave the network, not a float)
+            b.node("Identity", [b.qdq(y)], ["y"])
+            out = b.qdq("y", params_of=y)
+        b.g.inputs = [pb.ValueInfo("x", pb.FLOAT, ["N", c_in, height, "W"])]
+        b.g.outputs = [pb.ValueInfo(out, pb.FLOAT, ["N", c_out, "H", "W"])]
+        return pb.Model(b.g, 17, {})
+
+    fp = build(None)
+    sample = rng.normal(0.0, 1.0, (2, c_in, height, calib_width)).astype(np.float32)
+    out = forward_float(netdef.compile_model(fp), sample)
+
+    def params(lo, hi):
+        lo, hi = min(lo, 0.0), max(hi, 0.0)
+        s = np.float32((hi - lo) / 255.0)
+        return float(s), int(np.clip(np.rint(-lo / float(s)), 0, 255))
+
+    yname = "conv.relu" if relu else "conv.out"
+    quant = {"x": params(float(sample.min()), float(sample.max())), yname: params(float(out.min()), float(out.max()))}
+    return fp, build(quant), quant["x"]

@@ -27,7 +27,7 @@ _NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA
 EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec_set_pages", "crec_prefetch_pages",
            "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_ctc_greedy", "crec_ctc_greedy_noalloc", "crec_width_bucket", "crec_crop_region",
            "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats",
-           "crec_profile", "crec_profile_layers", "crec_mma_peak", "crec_debug_inject"]
+           "crec_profile", "crec_profile_layers", "crec_mma_peak", "crec_debug_inject", "crec_conv_sweep"]
 
 
 class CrecError(RuntimeError):
@@ -116,6 +116,7 @@ def lib() -> C.CDLL:
         L.crec_profile_layers.argtypes = [p, C.POINTER(ProfileEntry), i]
         L.crec_mma_peak.argtypes = [i, i, i, i, C.POINTER(C.c_double)]
         L.crec_debug_inject.argtypes = [p, i]
+        L.crec_conv_sweep.argtypes = [i, i, p, C.c_size_t, i, i, i, p, p, i, C.POINTER(C.c_double)]
         _lib = L
     return _lib
 
@@ -152,6 +153,23 @@ def ctc_greedy_noalloc(logits_ptr: int, n: int, classes: int, frames: int, lengt
                                        int(ids_ptr), int(starts_ptr), int(probs_ptr), stream or None, err, 256)
     if rc != OK:
         raise CrecError(rc, err.value.decode())
+
+
+def conv_sweep(blob: bytes, precision: int, x: np.ndarray, c_out: int, repeat: int = 3, device: int = 0,
+               stride: int = 1):
+    """crec_conv_sweep: x [n, h, w, c_in] (uint8 codes for INT8, float16 for FP16) through the blob's one
+    convolution (3x3, pad 1, stride `stride`): (y [n, oh, w / stride, c_out], ms a launch)."""
+    x = np.ascontiguousarray(x)
+    n, h, w, _ = x.shape
+    oh = (h + 2 - 3) // stride + 1
+    y = np.zeros((n, oh, w // stride, c_out), x.dtype)
+    ms = C.c_double(0.0)
+    b = C.create_string_buffer(bytes(blob), len(blob))
+    rc = lib().crec_conv_sweep(device, precision, C.cast(b, C.c_void_p), len(blob), n, h, w, x.ctypes.data, y.ctypes.data,
+                               repeat, C.byref(ms))
+    if rc != OK:
+        raise CrecError(rc, "crec_conv_sweep")
+    return y, ms.value
 
 
 def width_bucket(crop_width: int) -> int:

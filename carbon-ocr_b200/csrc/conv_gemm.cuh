@@ -94,7 +94,10 @@ __host__ __device__ constexpr int conv_accumulators(int nt) {
   return nt <= 32 ? 8 : nt <= 64 ? 8 : nt <= 128 ? 4 : 2;
 }
 
-template <bool kInt8, bool kFast>
+// Compile-time forms of a layer, so the epilogue's per-16-channel code carries no run-time
+// branches: kRes a residual input, kSat the round-first output stage (p.sat), kStack row stacking
+// (p.q_rows > 1).
+template <bool kInt8, bool kFast, bool kRes, bool kSat, bool kStack>
 __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid_constant__ ConvParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-aligned base for the swizzled stages
@@ -256,12 +259,12 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       mk = mk_next;
       uint8_t* dst0 = p.out + (oy + p.out_ph) * p.out_pitch + static_cast<long long>(ox) * p.cp_out * p.ebytes;
       const uint8_t* res = nullptr;
-      if (p.res && valid)
+      if (kRes && valid)
         res = p.res + (oy + p.res_ph) * p.res_pitch + static_cast<long long>(ox >> p.res_shift) * p.res_cp * p.ebytes;
       const int c0 = n * p.nt;
       // 16 of the tile's columns from r[0..16), starting at tile column tc: output row oy + q, channel cb
       auto store16 = [&](const uint32_t* r, int tc) {
-        const int q = p.q_rows > 1 ? ((tc >> 4) * p.cq_inv) >> 16 : 0;
+        const int q = kStack ? ((tc >> 4) * p.cq_inv) >> 16 : 0;
         const int cb = c0 + tc - q * p.cq;
         if (!inside || cb >= p.cp_out || oy + q >= p.oh) return;
         uint8_t* dst = dst0 + q * p.out_pitch;
@@ -275,7 +278,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
             // integer bounds)
             int32_t code[16];
             uint4 rv = make_uint4(0, 0, 0, 0);
-            if (res) rv = *reinterpret_cast<const uint4*>(res + cb);
+            if constexpr (kRes) rv = *reinterpret_cast<const uint4*>(res + cb);
             const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -290,13 +293,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
                 const int32_t a0 = static_cast<int32_t>(r[4 * k + u]), a1 = static_cast<int32_t>(r[4 * k + u + 1]);
                 float2 v = fadd2_rn(fmul_pair_rn(magic_to_float2(a0 + oo[u], a1 + oo[u + 1]), make_float2(ss[u], ss[u + 1])),
                                     make_float2(bb[u], bb[u + 1]));
-                if (res) {
+                if constexpr (kRes) {
                   const int32_t r0 = static_cast<int32_t>((rw[k] >> (8 * u)) & 0xffu);
                   const int32_t r1 = static_cast<int32_t>((rw[k] >> (8 * u + 8)) & 0xffu);
                   v = fadd2_rn(v, fmul_pair_rn(magic_to_float2(r0 + rzc, r1 + rzc), make_float2(p.res_scale, p.res_scale)));
                 }
                 float2 q = fmul_pair_rn(v, make_float2(p.out_inv_scale, p.out_inv_scale));
-                if (!p.sat) {
+                if constexpr (!kSat) {
                   q.x = fminf(fmaxf(q.x, lo), hi);
                   q.y = fminf(fmaxf(q.y, lo), hi);
                 }
@@ -315,7 +318,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
           } else {
             int32_t code[16];
             uint4 rv = make_uint4(0, 0, 0, 0);
-            if (res) rv = *reinterpret_cast<const uint4*>(res + cb);
+            if constexpr (kRes) rv = *reinterpret_cast<const uint4*>(res + cb);
             const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -331,13 +334,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
                 const int32_t a0 = static_cast<int32_t>(r[4 * k + u]), a1 = static_cast<int32_t>(r[4 * k + u + 1]);
                 float2 v = fadd2_rn(fmul_pair_rn(exact_i2f2(a0 - oo[u], a1 - oo[u + 1]), make_float2(ss[u], ss[u + 1])),
                                     make_float2(bb[u], bb[u + 1]));
-                if (res) {
+                if constexpr (kRes) {
                   const int32_t r0 = static_cast<int32_t>((rw[k] >> (8 * u)) & 0xffu);
                   const int32_t r1 = static_cast<int32_t>((rw[k] >> (8 * u + 8)) & 0xffu);
                   v = fadd2_rn(v, fmul_pair_rn(magic_to_float2(r0 + rzc, r1 + rzc), make_float2(p.res_scale, p.res_scale)));
                 }
                 float2 q = fmul_pair_rn(v, make_float2(p.out_inv_scale, p.out_inv_scale));
-                if (!p.sat) {
+                if constexpr (!kSat) {
                   q.x = fminf(fmaxf(q.x, lo), hi);
                   q.y = fminf(fmaxf(q.y, lo), hi);
                 }
@@ -362,7 +365,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
             for (int i = 0; i < 16; ++i) o[i] = __float2half_rn(0.0f);
           } else {
             alignas(16) __half rh[16];
-            if (res) {
+            if constexpr (kRes) {
               *reinterpret_cast<uint4*>(rh) = *reinterpret_cast<const uint4*>(res + cb * 2);
               *reinterpret_cast<uint4*>(rh + 8) = *reinterpret_cast<const uint4*>(res + cb * 2 + 16);
             }
@@ -370,7 +373,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
             for (int i = 0; i < 16; ++i) {
               const int j = cb + i;
               float v = __fadd_rn(__uint_as_float(r[i]), s_bias[j]);
-              if (res) v = __fadd_rn(v, __half2float(rh[i]));
+              if constexpr (kRes) v = __fadd_rn(v, __half2float(rh[i]));
               if (p.relu) v = v > 0.0f ? v : 0.0f;
               o[i] = __float2half_rn(j < p.c_out ? v : 0.0f);
             }

@@ -22,6 +22,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/carbon_rec.h"
@@ -783,16 +784,30 @@ int launch_conv(crec_handle* h, size_t li, long long cols) {
   }
   const int grid = std::min(p.num_tiles, h->sms);
   ProfScope prof(h, kProfConv, static_cast<int>(li));
-  if (h->int8 && l.fast) {
-    CK(cudaFuncSetAttribute(conv_gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-    conv_gemm_kernel<true, true><<<grid, kConvThreads, l.smem, s>>>(p);
-  } else if (h->int8) {
-    CK(cudaFuncSetAttribute(conv_gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-    conv_gemm_kernel<true, false><<<grid, kConvThreads, l.smem, s>>>(p);
-  } else {
-    CK(cudaFuncSetAttribute(conv_gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-    conv_gemm_kernel<false, false><<<grid, kConvThreads, l.smem, s>>>(p);
-  }
+  // the layer's compile-time form
+  auto run = [&](auto int8, auto fast, auto res, auto sat, auto stack) -> int {
+    auto* k = conv_gemm_kernel<decltype(int8)::value, decltype(fast)::value, decltype(res)::value, decltype(sat)::value,
+                               decltype(stack)::value>;
+    CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+    k<<<grid, kConvThreads, l.smem, s>>>(p);
+    return CREC_OK;
+  };
+  using T = std::true_type;
+  using F = std::false_type;
+  auto by_stack = [&](auto int8, auto fast, auto res, auto sat) {
+    return l.q_rows > 1 ? run(int8, fast, res, sat, T{}) : run(int8, fast, res, sat, F{});
+  };
+  auto by_sat = [&](auto int8, auto fast, auto res) {
+    return l.sat ? by_stack(int8, fast, res, T{}) : by_stack(int8, fast, res, F{});
+  };
+  auto by_res = [&](auto int8, auto fast) {
+    return l.residual >= 0 ? by_sat(int8, fast, T{}) : by_sat(int8, fast, F{});
+  };
+  int rc;
+  if (h->int8 && l.fast) rc = by_res(T{}, T{});
+  else if (h->int8) rc = by_res(T{}, F{});
+  else rc = l.residual >= 0 ? by_stack(F{}, F{}, T{}, F{}) : by_stack(F{}, F{}, F{}, F{});
+  if (rc) return rc;
   CK(cudaGetLastError());
   return CREC_OK;
 }
@@ -1979,6 +1994,119 @@ int crec_debug_value(crec_handle* h, int value, void* out, int64_t capacity) {
 }
 
 }  // extern "C"
+
+namespace {
+
+// Opens `h` as a layer-only device (no crop, no head): the blob's one dense convolution between
+// its input value (h_in rows) and output value, each input line bw columns wide, n of them laid
+// out as a run is; the layer set up exactly as in a recognizer (setup_layer, the same tensors).
+int open_layer(crec_handle* h, int device, int precision, const void* model, size_t model_bytes, int n, int h_in,
+               int bw, long long* cols_out) {
+  h->int8 = precision == CREC_INT8;
+  h->eb = h->int8 ? 1 : 2;
+  h->device = device;
+  CK(cudaSetDevice(device));
+  cudaDeviceProp prop{};
+  CK(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) return set_error(h, CREC_E_INVALID, "this build runs on sm_100 (B200)");
+  h->sms = prop.multiProcessorCount;
+  cudaDriverEntryPointQueryResult q{};
+  void* fn = nullptr;
+  CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (!fn || q != cudaDriverEntryPointSuccess) return set_error(h, CREC_E_CUDA, "cuTensorMapEncodeTiled is not available");
+  h->encode = reinterpret_cast<EncodeTiled>(fn);
+  CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+  int rc = read_model(h, static_cast<const uint8_t*>(model), model_bytes);
+  if (rc) return rc;
+  if (h->l.size() != 1 || h->l[0].kind != kKindConv || h->l[0].residual >= 0)
+    return set_error(h, CREC_E_MODEL, "a blob of one dense convolution");
+  const Layer conv = h->l[0];
+  Value& x = h->v[conv.in];
+  Value& y = h->v[conv.out];
+  const int s = log2i(conv.sw);
+  if (s < 0 || conv.kh > 3 || x.c % 16 || y.c % 16) return set_error(h, CREC_E_MODEL, "a convolution this sweep does not run");
+  x.h = h_in;
+  x.shift = 0;
+  x.phys = conv.in;
+  x.real = true;
+  x.cp = x.c;
+  y.h = (h_in + conv.pt + conv.pb - conv.kh) / conv.sh + 1;
+  y.shift = s;
+  y.phys = conv.out;
+  y.real = true;
+  y.cp = y.c;
+  if (y.h <= 0 || bw % (8 << s)) return set_error(h, CREC_E_INVALID, "layer sweep: shape");
+  h->max_shift = s;
+  h->head_shift = s;
+  h->gap = static_cast<int>(round_up(std::max({1, conv.pl, conv.pr}), std::max(8, 1 << s)));
+  Layer stub{};
+  stub.kind = kKindResize;
+  h->l = {stub, conv, stub};  // setup_layer's view: neither the first layer (the stem) nor the last (the head)
+  const long long cols = round_up(static_cast<long long>(n) * (bw + h->gap) + h->gap, 128LL << s);
+  h->max_cols = cols;
+  if ((rc = setup_layer(h, 1)) || (rc = alloc_values(h))) return rc;
+  if ((rc = dev_alloc(h, &h->d_mask, static_cast<size_t>(cols / 8))) || (rc = dev_alloc(h, &h->d_err, 1))) return rc;
+  std::vector<uint8_t> mask(static_cast<size_t>(cols / 8), 0);
+  for (int i = 0; i < n; ++i) std::memset(mask.data() + (h->gap + static_cast<long long>(i) * (bw + h->gap)) / 8, 1, bw / 8);
+  CK(cudaMemcpy(h->d_mask, mask.data(), mask.size(), cudaMemcpyHostToDevice));
+  CK(cudaMemset(h->d_err, 0, sizeof(int)));
+  *cols_out = cols;
+  return CREC_OK;
+}
+
+}  // namespace
+
+int crec_conv_sweep(int device, int precision, const void* model, size_t model_bytes, int n, int h_in, int w,
+                    const void* x, void* y, int repeat, double* ms) {
+  if (!model || !x || !y || !ms || n <= 0 || h_in <= 0 || h_in > 64 || w <= 0 || repeat < 1 ||
+      (precision != CREC_INT8 && precision != CREC_FP16))
+    return CREC_E_INVALID;
+  std::unique_ptr<crec_handle, void (*)(crec_handle*)> hold(new crec_handle(), [](crec_handle* p) {
+    free_all(p);
+    delete p;
+  });
+  crec_handle* h = hold.get();
+  long long cols = 0;
+  int rc = open_layer(h, device, precision, model, model_bytes, n, h_in, w, &cols);
+  if (rc) return rc;
+  const Layer& l = h->l[1];
+  const Value& xv = h->v[l.in];
+  const Value& yv = h->v[l.out];
+  const size_t xrow = static_cast<size_t>(w) * xv.c * h->eb;
+  for (int i = 0; i < n; ++i) {  // line i at input columns [gap + i (w + gap), + w)
+    const long long seg = h->gap + static_cast<long long>(i) * (w + h->gap);
+    CK(cudaMemcpy2D(xv.base + static_cast<long long>(xv.ph) * xv.pitch + seg * xv.cp * h->eb, xv.pitch,
+                    static_cast<const uint8_t*>(x) + static_cast<size_t>(i) * h_in * xrow, xrow, xrow, h_in,
+                    cudaMemcpyHostToDevice));
+  }
+  if ((rc = launch_conv(h, 1, cols))) return rc;  // warm-up
+  CK(cudaStreamSynchronize(h->stream));
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventCreate(&e1));
+  CK(cudaEventRecord(e0, h->stream));
+  for (int r = 0; r < repeat && rc == CREC_OK; ++r) rc = launch_conv(h, 1, cols);
+  CK(cudaEventRecord(e1, h->stream));
+  CK(cudaEventSynchronize(e1));
+  float t = 0.0f;
+  cudaEventElapsedTime(&t, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc) return rc;
+  int err = 0;
+  CK(cudaMemcpy(&err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) return CREC_E_TIMEOUT;
+  *ms = static_cast<double>(t) / repeat;
+  const int ow = w >> yv.shift;
+  const size_t yrow = static_cast<size_t>(ow) * yv.c * h->eb;
+  for (int i = 0; i < n; ++i) {
+    const long long seg = (h->gap + static_cast<long long>(i) * (w + h->gap)) >> yv.shift;
+    CK(cudaMemcpy2D(static_cast<uint8_t*>(y) + static_cast<size_t>(i) * yv.h * yrow, yrow,
+                    yv.base + static_cast<long long>(yv.ph) * yv.pitch + seg * yv.cp * h->eb, yv.pitch, yrow, yv.h,
+                    cudaMemcpyDeviceToHost));
+  }
+  return CREC_OK;
+}
 
 int crec_mma_peak(int device, int precision, int n, int iters, double* tera_ops) {
   if (!tera_ops || n < 16 || n > 256 || n % 16 || iters < 1 || (precision != CREC_INT8 && precision != CREC_FP16))

@@ -221,6 +221,17 @@ CREC_API int crec_mma_peak(int device, int precision, int n, int iters, double* 
 #define CREC_INJECT_STICKY 2
 CREC_API int crec_debug_inject(crec_handle* h, int what);
 
+/* The kernel sweep (on the CPU the reference measures its GEMMs with
+ * cli/main.cpp's bench_gemm): a blob's one dense convolution (its input value, the layer, its
+ * output value; carbon_rec/model.py make_conv) run by this build's tcgen05 implicit-GEMM kernel,
+ * set up as in a recognizer, on n inputs [h][w][c_in] (NHWC, each its own line with the zero
+ * point -- a real 0 -- around it, as the reference's executor borders a batch): uint8 codes for
+ * CREC_INT8, float16 for CREC_FP16; y gets [n][oh][ow][c_out] the same way.  *ms: the kernel's
+ * mean device time over `repeat` launches after one warm-up (CUDA events).  Channel counts must
+ * be multiples of 16.  No counterpart in the reference (a measurement and parity hook). */
+CREC_API int crec_conv_sweep(int device, int precision, const void* model, size_t model_bytes, int n, int h, int w,
+                             const void* x, void* y, int repeat, double* ms);
+
 /* The CUDA stream (a cudaStream_t) the handle's work runs on, for device-side timing. */
 CREC_API void* crec_stream(crec_handle* h);
 
