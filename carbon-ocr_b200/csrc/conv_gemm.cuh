@@ -83,6 +83,18 @@ struct ConvParams {
   int* err;
   unsigned long long wait_ns;  // every wait's limit (kWaitNs; shorter only for a test's injected timeout)
   int idle_producer;           // test hook: the producer issues nothing, so the waits run out
+  // band mode (conv_gemm_kernel<..., kBand = true>): see the comment above the kernel
+  int num_bands;               // 128-column bands of the output
+  int band_rows;               // input rows a band reads: (oh - 1) * sh + kh
+  int kh, kw, sh, pairs, sw;   // kernel, vertical stride, 32-byte channel pairs, horizontal stride
+  int plane_px;                // pixel rows a channel plane holds
+  int gx0;                     // the first plane row's pixel group, relative to the band's first output column
+  int kx_parity[3], kx_off[3]; // per kernel column: its plane's parity and its first row in the plane
+  uint32_t slot_bytes;         // a ring slot: one input row, (2 * pairs) x sw planes of plane_px x 16 bytes
+  uint32_t load_bytes;         // the bytes a slot's loads bring (the real chunks only)
+  int chunks;                  // 16-byte channel chunks of the input (the rest of 2 * pairs stay zero)
+  uint32_t w_bytes;            // the resident weight image
+  int row0;                    // the input's border rows less the layer's top padding: band row i is map row i + row0
 };
 
 constexpr int kConvThreads = 576;
@@ -94,19 +106,34 @@ __host__ __device__ constexpr int conv_accumulators(int nt) {
   return nt <= 32 ? 8 : nt <= 64 ? 8 : nt <= 128 ? 4 : 2;
 }
 
+// Band mode, for narrow layers (few channels, so a tile's K is short and the 128-byte im2col boxes
+// would re-read every input row kh x kw times through L2): a CTA takes a band of 128 output
+// columns from the first output row to the last.  Each input row the band reads is loaded once,
+// into a ring slot of shared memory, as channel planes: for each 16-byte chunk of the channels
+// (and, with stride 2, for each pixel parity) the band's pixels one after another, 16 bytes
+// each.  That is the tensor cores' K-major layout without swizzle (8-row core matrices of 16
+// bytes), so the MMA for kernel tap (ky, kx) and a 32-byte channel pair reads its A operand in
+// place: the planes of input row oy * sh + ky, starting kx's row offset in, the next chunk one
+// plane further (the descriptor's leading byte offset), the next 8 pixels 128 bytes further
+// (its stride byte offset).  The weights stay resident, [ky][kx][pair][N / 8][2][8 rows][16 bytes]
+// (the same layout).  The epilogue is the other mode's.
+//
 // Compile-time forms of a layer, so the epilogue's per-16-channel code carries no run-time
 // branches: kRes a residual input, kSat the round-first output stage (p.sat), kStack row stacking
-// (p.q_rows > 1).
-template <bool kInt8, bool kFast, bool kRes, bool kSat, bool kStack>
+// (p.q_rows > 1), kBand the band mode.
+template <bool kInt8, bool kFast, bool kRes, bool kSat, bool kStack, bool kBand>
 __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid_constant__ ConvParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-aligned base for the swizzled stages
+  // 1024-aligned base for the swizzled stages (band mode: the resident weights, then the ring)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
+  const uint32_t data_bytes = kBand ? p.w_bytes + p.stages * p.slot_bytes : p.stages * p.stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + data_bytes);
   uint64_t* empty = full + p.stages;
   uint64_t* tmem_full = empty + p.stages;      // [kMaxAcc]
   uint64_t* tmem_empty = tmem_full + kMaxAcc;  // [kMaxAcc]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + kMaxAcc);
+  uint64_t* w_full = tmem_empty + kMaxAcc;     // band mode: the resident weights (16 bytes kept, so
+                                               // the per-channel tables below stay 16-byte aligned)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(w_full + 2);
   int32_t* s_off = reinterpret_cast<int32_t*>(tmem_slot + 4);  // [cp_out] per-channel constants
   float* s_scale = reinterpret_cast<float*>(s_off + p.cp_out);
   float* s_bias = s_scale + p.cp_out;
@@ -126,7 +153,18 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       mbar_init(&tmem_full[a], 1);
       mbar_init(&tmem_empty[a], 8);  // the eight warps of the half that takes the tile
     }
+    mbar_init(w_full, 1);
     fence_mbar_init();
+  }
+  if constexpr (kBand) {
+    // the ring's planes past the input's chunks (a channel pair's missing half) hold zeros: the
+    // loads never write them, and zero times a zero weight is zero (float16 too)
+    const int planes = 2 * p.pairs * p.sw, real = p.chunks * p.sw;
+    const uint32_t plane_bytes = static_cast<uint32_t>(p.plane_px) * 16;
+    for (int s = 0; s < p.stages; ++s)
+      for (uint32_t i = threadIdx.x * 16; i < (planes - real) * plane_bytes; i += blockDim.x * 16)
+        *reinterpret_cast<uint4*>(smem + p.w_bytes + s * p.slot_bytes + real * plane_bytes + i) = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   if (warp == 0 && lane == 0) {
@@ -139,7 +177,101 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
   const int ksteps_per_tile = p.krows * p.nkb;
   const uint32_t acc_cols = kTmemCols / static_cast<uint32_t>(p.n_acc);
 
-  if (warp == 0) {
+  if (kBand && warp == 0) {
+    // ---------------------------------------------------------------- band producer
+    // the weights once, then each band's input rows into the ring, in order
+    const bool leader = elect_one();
+    if (leader) {
+      mbar_expect_tx(w_full, p.w_bytes);
+      for (uint32_t off = 0; off < p.w_bytes; off += 32768)
+        bulk_load(smem + off, p.wimg + off, min(32768u, p.w_bytes - off), w_full);
+    }
+    __syncwarp();
+    uint32_t g = 0;  // rows loaded so far
+    bool ok = p.idle_producer == 0;
+    for (int band = blockIdx.x; band < p.num_bands && ok; band += gridDim.x) {
+      const int c = band * 128 + p.gx0;
+      for (int i = 0; i < p.band_rows; ++i, ++g) {
+        const int slot = static_cast<int>(g % static_cast<uint32_t>(p.stages));
+        const uint32_t phase = (g / static_cast<uint32_t>(p.stages)) & 1;
+        if (!mbar_wait_warp(&empty[slot], phase ^ 1, p.err, kErrTimeoutEmpty, p.wait_ns)) {
+          ok = false;
+          break;
+        }
+        if (leader) {
+          uint8_t* dst = smem + p.w_bytes + slot * p.slot_bytes;
+          mbar_expect_tx(&full[slot], p.load_bytes);
+          for (int j = 0; j < p.chunks; ++j)
+            for (int par = 0; par < p.sw; ++par)
+              tma_load_4d(dst + (j * p.sw + par) * p.plane_px * 16, &p.tmap[0], 16 * j, par, c, i + p.row0, &full[slot]);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (kBand && warp == 1) {
+    // ---------------------------------------------------------------- band MMA issuer
+    const bool leader = elect_one();
+    const uint32_t tmem = __shfl_sync(0xffffffffu, tmem_base, 0);
+    const uint32_t ring = smem_u32(smem) + p.w_bytes, plane_bytes = static_cast<uint32_t>(p.plane_px) * 16;
+    const uint32_t lbo = static_cast<uint32_t>(p.sw) * plane_bytes;  // the next 16-byte chunk, same parity
+    const uint32_t w_step = static_cast<uint32_t>(p.cq) * 32;
+    const uint64_t a_desc0 = umma_desc_none(ring, lbo, 128), b_desc0 = umma_desc_none(smem_u32(smem), 128, 256);
+    bool ok = mbar_wait_warp(w_full, 0, p.err, kErrTimeoutFull, p.wait_ns);
+    tc_fence_after();
+    uint32_t g = 0;  // the ring counter of the band's first row
+    int s = 0;       // this CTA's tile sequence
+    const int groups = p.oh / p.q_rows;
+    const uint32_t idesc_row = kInt8 ? idesc_i8(p.cq) : idesc_f16(p.cq);  // one output row's channels
+    for (int band = blockIdx.x; band < p.num_bands && ok; band += gridDim.x) {
+      for (int grp = 0; grp < groups && ok; ++grp, ++s) {
+        const int acc = s & (p.n_acc - 1);
+        if (!mbar_wait_warp(&tmem_empty[acc], ((s / p.n_acc) & 1) ^ 1, p.err, kErrTimeoutTmemEmpty, p.wait_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // output row oy = grp * q_rows + q of the tile into accumulator columns [q * cq, (q + 1) * cq)
+        for (int q = 0; q < p.q_rows && ok; ++q) {
+          const int oy = grp * p.q_rows + q;
+          const uint32_t d = tmem + static_cast<uint32_t>(acc) * acc_cols + static_cast<uint32_t>(q * p.cq);
+          uint32_t accumulate = 0;
+          for (int ky = 0; ky < p.kh && ok; ++ky) {
+            const uint32_t r = g + static_cast<uint32_t>(oy * p.sh + ky);
+            const uint32_t slot = r % static_cast<uint32_t>(p.stages);
+            if (!mbar_wait_warp(&full[slot], (r / static_cast<uint32_t>(p.stages)) & 1, p.err, kErrTimeoutFull, p.wait_ns)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            // every lane computes the descriptors (warp-uniform values); one lane issues.  A tap's
+            // descriptors differ from the row's (and the weights' first) only in the start address
+            // field (address >> 4, no carry: shared memory is below 256 KB)
+            const uint64_t row_desc = a_desc0 + ((slot * p.slot_bytes) >> 4);
+            uint64_t bd = b_desc0 + static_cast<uint64_t>((ky * p.kw * p.pairs * w_step) >> 4);
+            for (int kx = 0; kx < p.kw; ++kx) {
+              uint64_t ad = row_desc + ((static_cast<uint32_t>(p.kx_parity[kx]) * plane_bytes + static_cast<uint32_t>(p.kx_off[kx]) * 16) >> 4);
+              for (int pr = 0; pr < p.pairs; ++pr) {
+                if (leader) umma<kInt8>(d, ad, bd, idesc_row, accumulate);
+                accumulate = 1;
+                ad += (2 * lbo) >> 4;
+                bd += w_step >> 4;
+              }
+            }
+            __syncwarp();
+          }
+        }
+        if (!ok) break;
+        if (leader) {
+          umma_commit(&tmem_full[acc]);
+          // the rows no later tile of the band reads go back to the producer
+          const int first = grp * p.q_rows * p.sh, last = grp + 1 == groups ? p.band_rows : (grp + 1) * p.q_rows * p.sh;
+          for (int i = first; i < last; ++i) umma_commit(&empty[(g + static_cast<uint32_t>(i)) % static_cast<uint32_t>(p.stages)]);
+        }
+        __syncwarp();
+      }
+      g += static_cast<uint32_t>(p.band_rows);
+    }
+  } else if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     // The whole warp runs the loop (its counters, coordinates and addresses warp-uniform), one
     // elected lane issues the copies.
@@ -235,25 +367,45 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     const float lo = p.relu ? 0.0f : static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
     const int32_t zc = p.out_zero - kMagicBits, rzc = kMagicBits - p.res_zero;
     const uint32_t zb = static_cast<uint32_t>(p.out_zero) * 0x01010101u;
-    // the line mask byte of this thread's pixel in tile t (0 past the output's width)
-    auto mask_of = [&](int t) -> int {
-      if (t >= p.num_tiles) return 0;
-      const int m = fast_div(t, p.n_tiles, p.nt_magic);
-      const int ox = (m - fast_div(m, p.m_per_row, p.mpr_magic) * p.m_per_row) * 128 + row;
+    // this CTA's tile s: its first output row, its first output column, its channel tile (false
+    // past the last one).  Tiles go round the CTAs (tile blockIdx.x + s * gridDim.x), or in band
+    // mode band by band, each band's output rows in order
+    auto tile_of = [&](int s, int& oy, int& ox0, int& n) -> bool {
+      if constexpr (kBand) {
+        const int groups = p.oh / p.q_rows;
+        const int band = blockIdx.x + (s / groups) * gridDim.x;
+        if (band >= p.num_bands) return false;
+        oy = (s % groups) * p.q_rows;
+        ox0 = band * 128;
+        n = 0;
+      } else {
+        const int t = blockIdx.x + s * gridDim.x;
+        if (t >= p.num_tiles) return false;
+        const int m = fast_div(t, p.n_tiles, p.nt_magic);
+        n = t - m * p.n_tiles;
+        const int mr = fast_div(m, p.m_per_row, p.mpr_magic);
+        oy = mr * p.q_rows;
+        ox0 = (m - mr * p.m_per_row) * 128;
+      }
+      return true;
+    };
+    // the line mask byte of this thread's pixel in tile s (0 past the output's width)
+    auto mask_of = [&](int s) -> int {
+      int oy, ox0, n;
+      if (!tile_of(s, oy, ox0, n)) return 0;
+      const int ox = ox0 + row;
       return ox < p.ow ? __ldg(p.mask8 + ((static_cast<long long>(ox) << p.out_shift) >> 3)) : 0;
     };
     int iter = half;
-    int t = blockIdx.x + half * gridDim.x;
-    int mk = mask_of(t);
-    for (; t < p.num_tiles; t += 2 * gridDim.x, iter += 2) {
-      const int mk_next = mask_of(t + 2 * gridDim.x);  // in flight during this tile
+    int mk = mask_of(iter);
+    int oy, ox0, n;
+    for (; tile_of(iter, oy, ox0, n); iter += 2) {
+      const int mk_next = mask_of(iter + 2);  // in flight during this tile
       const int acc = iter & (p.n_acc - 1);
       const uint32_t acc_phase = (iter / p.n_acc) & 1;
       if (!mbar_wait(&tmem_full[acc], acc_phase, p.err, kErrTimeoutTmemFull, p.wait_ns)) break;
       tc_fence_after();
-      const int m = fast_div(t, p.n_tiles, p.nt_magic), n = t - m * p.n_tiles;
-      const int mr = fast_div(m, p.m_per_row, p.mpr_magic);
-      const int oy = mr * p.q_rows, ox = (m - mr * p.m_per_row) * 128 + row;
+      const int ox = ox0 + row;
       const bool inside = ox < p.ow;
       const bool valid = inside && mk != 0;
       mk = mk_next;

@@ -39,6 +39,11 @@ using namespace crec;
 namespace {
 
 constexpr int kKindConv = 0, kKindDw = 1, kKindResize = 2;
+// Band mode (conv_gemm.cuh) is bit-exact but off: it gathers its channel planes 16 bytes at a time
+// from NHWC rows, which from L2 was 1.6x faster than the im2col windows (s1b of a 524,288-column
+// run, 46 against 76 us) but from DRAM, at full run size, 2x slower (s1b 5.1 against 2.6 ms a
+// step).  It needs its input written chunk-planar by the layer before.
+constexpr bool kNoBand = true;
 constexpr size_t kGuard = 64 << 10;
 
 struct Value {
@@ -76,6 +81,11 @@ struct Layer {
   int nkb = 0, last_steps = 0, nt = 0, n_tiles = 0, stages = 0, nchunk = 0, chunks = 0;
   int krows = 0, q_rows = 1, cq = 0;  // dense convs: input rows a tile reads, output rows it stacks, channels a row
   uint32_t stage_bytes = 0, a_bytes = 0, b_bytes = 0, smem = 0;
+  // band mode (conv_gemm.cuh): channel-plane ring slots, resident weights
+  bool band = false;
+  int pairs = 0, band_chunks = 0, plane_px = 0, band_rows = 0, gx0 = 0;
+  int kx_parity[3] = {0, 0, 0}, kx_off[3] = {0, 0, 0};
+  uint32_t slot_bytes = 0, load_bytes = 0, w_bytes = 0;
 };
 
 template <class T>
@@ -455,6 +465,35 @@ std::vector<uint8_t> weight_image(const crec_handle* h, const Layer& l, int cp_i
   return img;
 }
 
+// A dense layer's weights in band mode: [ky][kx][32-byte channel pair][nt / 8][2 chunks][8 rows][16
+// bytes], the tensor cores' K-major layout without swizzle (zeros past the input's channels and
+// past cout).
+std::vector<uint8_t> band_weight_image(const crec_handle* h, const Layer& l, int nt) {
+  const int eb = h->eb, taps = l.kh * l.kw;
+  std::vector<uint8_t> img(static_cast<size_t>(taps) * l.pairs * nt * 32, 0);
+  for (int ky = 0; ky < l.kh; ++ky)
+    for (int kx = 0; kx < l.kw; ++kx)
+      for (int pr = 0; pr < l.pairs; ++pr) {
+        uint8_t* blk = img.data() + static_cast<size_t>((ky * l.kw + kx) * l.pairs + pr) * nt * 32;
+        for (int n = 0; n < nt && n < l.cout; ++n)
+          for (int c = 0; c < 2; ++c)
+            for (int b = 0; b < 16; ++b) {
+              const int byte = ((2 * pr + c) * 16 + b), ch = byte / eb;
+              if (ch >= l.cin) continue;
+              const size_t wi = (static_cast<size_t>(n) * l.cin + ch) * taps + ky * l.kw + kx;
+              uint8_t v;
+              if (h->int8) {
+                v = static_cast<uint8_t>(l.w8[wi]);
+              } else {
+                const uint16_t hb = half_bits(l.wf[wi]);
+                v = static_cast<uint8_t>(byte % 2 ? hb >> 8 : hb & 0xff);
+              }
+              blk[(n / 8) * 256 + c * 128 + (n % 8) * 16 + b] = v;
+            }
+      }
+  return img;
+}
+
 // The INT8 epilogue's per-channel offsets (n of them) and whether its conversions may skip the
 // conversion unit: |acc - zero * colsum| <= max(zero, 255 - zero) * sum |w| over a channel's
 // weights; below 2^22 the kernel converts exactly with kMagic.
@@ -601,9 +640,55 @@ int setup_layer(crec_handle* h, size_t li) {
     l.b_bytes = static_cast<uint32_t>(l.nt) * 128;
     l.stage_bytes = l.a_bytes + l.b_bytes;
     l.stages = std::min<int>(8, (200 * 1024) / l.stage_bytes);
-    l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 2 * kMaxAcc) * 8 + 16 + 12 * y.cp + 64;
+    l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 2 * kMaxAcc + 2) * 8 + 16 + 12 * y.cp + 64;
     if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, y.cp))) return rc;
     if (h->int8) l.sat = round_first(h, l, x, y, scale, bias);
+    // band mode where the layer's weights stay resident beside a ring of at least kh + 1 input
+    // rows: every input row then crosses from L2 once a band instead of once a kernel row
+    const int nt = round16(l.cout), chunks = x.cp * h->eb / 16, pairs = (chunks + 1) / 2;
+    const uint32_t w_bytes = static_cast<uint32_t>(l.kh * l.kw * pairs * nt * 32);
+    if (l.residual < 0 && l.kh <= 3 && l.kw <= 3 && (l.sw == 1 || l.sw == 2) && l.pl <= 2 && nt <= 256 &&
+        w_bytes <= 160 * 1024 && !kNoBand) {
+      const int fl = -((l.pl + l.sw - 1) / l.sw);  // floor(-pl / sw)
+      int max_off = 0;
+      for (int kx = 0; kx < l.kw; ++kx) {
+        const int d = kx - l.pl - l.sw * fl;
+        l.kx_parity[kx] = d % l.sw;
+        l.kx_off[kx] = d / l.sw;
+        max_off = std::max(max_off, l.kx_off[kx]);
+      }
+      const int plane_px = (128 + max_off + 7) / 8 * 8;
+      const uint32_t slot_bytes = static_cast<uint32_t>(2 * pairs * l.sw * plane_px * 16);
+      const uint32_t tail = (2 * 16 + 2 * kMaxAcc + 2) * 8 + 16 + 12 * y.cp + 64;
+      const long long room = 232448 - 1024 - 1024 - static_cast<long long>(w_bytes) - tail;
+      const int slots = static_cast<int>(std::min<long long>(16, room / slot_bytes));
+      if (slots >= l.kh + 1) {
+        l.band = true;
+        l.pairs = pairs;
+        l.band_chunks = chunks;
+        l.plane_px = plane_px;
+        l.band_rows = (y.h - 1) * l.sh + l.kh;
+        l.gx0 = fl + 8;  // the tensor map's base is 8 pixel groups to the left (gap columns)
+        l.slot_bytes = slot_bytes;
+        l.load_bytes = static_cast<uint32_t>(chunks * l.sw * plane_px * 16);
+        l.w_bytes = w_bytes;
+        l.stages = slots;
+        // row stacking as the other mode has it: q output rows a tile, each its own MMAs into its own
+        // accumulator columns (N = q x cq), where q divides the output's height and q * cq <= 256
+        // (a tile holds all the (q - 1) * sh + kh input rows it reads at once: the ring keeps one more)
+        int q = 1;
+        for (int k = 1; k <= y.h && k * nt <= 256; ++k)
+          if (y.h % k == 0 && (k - 1) * l.sh + l.kh + 1 <= slots) q = k;
+        l.q_rows = q;
+        l.krows = 1;
+        l.cq = nt;
+        l.nt = q * nt;
+        l.n_tiles = 1;
+        l.smem = 1024 + w_bytes + slots * slot_bytes + (2 * slots + 2 * kMaxAcc + 2) * 8 + 16 + 12 * y.cp + 64;
+        const std::vector<uint8_t> img = band_weight_image(h, l, nt);
+        return upload(h, &l.wimg, img);
+      }
+    }
   }
   const std::vector<uint8_t> img = weight_image(h, l, x.cp, l.nt, l.n_tiles, l.nkb);
   if ((rc = upload(h, &l.wimg, img))) return rc;
@@ -634,6 +719,21 @@ int encode_map(crec_handle* h, CUtensorMap* m, const void* base, uint64_t d0, ui
                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(h, CREC_E_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return CREC_OK;
+}
+
+// A band-mode layer's input: (channel byte, pixel parity, pixel group, row), the base `base`; boxes
+// of 16 channel bytes x plane_px groups of one parity and row.
+int encode_map4(crec_handle* h, CUtensorMap* m, const void* base, uint64_t cbytes, uint64_t sw, uint64_t groups,
+                uint64_t rows, uint64_t pitch, uint32_t plane_px) {
+  const cuuint64_t dims[4] = {cbytes, sw, groups, rows};
+  const cuuint64_t strides[3] = {cbytes, sw * cbytes, pitch};
+  const cuuint32_t box[4] = {16, 1, plane_px, 1};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUresult r = h->encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, es,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(h, CREC_E_CUDA, "cuTensorMapEncodeTiled (4-d) failed (" + std::to_string(r) + ")");
   return CREC_OK;
 }
 
@@ -719,7 +819,34 @@ int launch_conv(crec_handle* h, size_t li, long long cols) {
   ConvParams p{};
   const long long in_pitch = xp.pitch;
   const uint64_t px = static_cast<uint64_t>(x.cp) * h->eb;
-  for (int i = 0; i < l.krows; ++i) {  // input row i of a tile's group of q_rows output rows
+  if (l.band) {
+    const long long in_cols = cols >> x.shift;
+    const uint8_t* base = xp.base - 8LL * l.sw * static_cast<long long>(px);
+    int rc = encode_map4(h, &p.tmap[0], base, px, static_cast<uint64_t>(l.sw),
+                         static_cast<uint64_t>(in_cols / l.sw + 8 + l.plane_px), static_cast<uint64_t>(x.h + 2 * xp.ph),
+                         static_cast<uint64_t>(in_pitch), static_cast<uint32_t>(l.plane_px));
+    if (rc) return rc;
+    p.num_bands = static_cast<int>((ow + 127) / 128);
+    p.band_rows = l.band_rows;
+    p.kh = l.kh;
+    p.kw = l.kw;
+    p.sh = l.sh;
+    p.sw = l.sw;
+    p.pairs = l.pairs;
+    p.chunks = l.band_chunks;
+    p.plane_px = l.plane_px;
+    p.gx0 = l.gx0;
+    for (int k = 0; k < 3; ++k) {
+      p.kx_parity[k] = l.kx_parity[k];
+      p.kx_off[k] = l.kx_off[k];
+    }
+    p.slot_bytes = l.slot_bytes;
+    p.load_bytes = l.load_bytes;
+    p.w_bytes = l.w_bytes;
+    p.row0 = xp.ph - l.pt;
+    if (p.row0 < 0) return set_error(h, CREC_E_MODEL, "band mode: a padding wider than the input's border rows");
+  }
+  for (int i = 0; i < l.krows && !l.band; ++i) {  // input row i of a tile's group of q_rows output rows
     const uint8_t* base = xp.base + static_cast<long long>(i - l.pt + xp.ph) * in_pitch - static_cast<long long>(l.pl) * px;
     int rc = encode_map(h, &p.tmap[i], base, static_cast<uint64_t>(l.nkb) * 128, static_cast<uint64_t>(ow),
                         static_cast<uint64_t>(oh / l.q_rows), static_cast<uint64_t>(l.sw) * px,
@@ -782,12 +909,14 @@ int launch_conv(crec_handle* h, size_t li, long long cols) {
     p.wait_ns = 1000000ull;
     p.idle_producer = 1;
   }
-  const int grid = std::min(p.num_tiles, h->sms);
+  const int grid = std::min(l.band ? p.num_bands : p.num_tiles, h->sms);
   ProfScope prof(h, kProfConv, static_cast<int>(li));
   // the layer's compile-time form
   auto run = [&](auto int8, auto fast, auto res, auto sat, auto stack) -> int {
-    auto* k = conv_gemm_kernel<decltype(int8)::value, decltype(fast)::value, decltype(res)::value, decltype(sat)::value,
-                               decltype(stack)::value>;
+    constexpr bool kI8 = decltype(int8)::value, kF = decltype(fast)::value, kR = decltype(res)::value,
+                   kS = decltype(sat)::value, kQ = decltype(stack)::value;
+    // band mode has no residual
+    auto* k = l.band ? conv_gemm_kernel<kI8, kF, false, kS, kQ, true> : conv_gemm_kernel<kI8, kF, kR, kS, kQ, false>;
     CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
     k<<<grid, kConvThreads, l.smem, s>>>(p);
     return CREC_OK;

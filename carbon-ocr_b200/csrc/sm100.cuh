@@ -120,6 +120,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0,
       : "memory");
 }
 
+// TMA: a tiled box of a 4-d tensor map into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int c0, int c1, int c2, int c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Bulk copy of `bytes` (a multiple of 16, both ends 16-byte aligned) global -> shared.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -163,6 +172,18 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
   d |= static_cast<uint64_t>(1024u >> 4) << 32;    // stride byte offset: 8 rows x 128 bytes
   d |= static_cast<uint64_t>(1u) << 46;            // version (sm_100)
   d |= static_cast<uint64_t>(2u) << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// K-major operand without swizzle: 8-row core matrices of 16 bytes (128 contiguous bytes each);
+// `lbo` the byte step between core matrices along K, `sbo` along M (or N) -- checked on the GPU
+// against a host product, both ways round (only this reading gives it).
+__device__ __forceinline__ uint64_t umma_desc_none(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;  // version (sm_100); layout type 0: no swizzle
   return d;
 }
 
