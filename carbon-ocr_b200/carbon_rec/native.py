@@ -68,7 +68,7 @@ class Box(C.Structure):
 
 class Stats(C.Structure):
     _fields_ = [("runs", C.c_int64), ("launches", C.c_int64), ("h2d_bytes", C.c_int64), ("d2h_bytes", C.c_int64),
-                ("h2d_total", C.c_int64), ("d2h_total", C.c_int64)]
+                ("h2d_total", C.c_int64), ("d2h_total", C.c_int64), ("wide_lines", C.c_int64)]
 
 
 class ProfileEntry(C.Structure):
@@ -380,7 +380,7 @@ class RecDevice:
         st = Stats()
         self._check(lib().crec_last_stats(self._h, C.byref(st)))
         return {"runs": st.runs, "launches": st.launches, "h2d_bytes": st.h2d_bytes, "d2h_bytes": st.d2h_bytes,
-                "h2d_total": st.h2d_total, "d2h_total": st.d2h_total}
+                "h2d_total": st.h2d_total, "d2h_total": st.d2h_total, "wide_lines": st.wide_lines}
 
     def profile(self, enable: int = -1) -> dict:
         """Per-kernel totals {name: (launches, ms, ops)} since profiling was (re)started; enable 1 (re)starts."""

@@ -191,6 +191,16 @@ struct crec_handle {
   int max_pages = 0;
   // run buffers
   LineDesc* d_lines = nullptr;
+  int* d_claim = nullptr;  // the crop kernel's line claims: [2], 0 between launches
+  // lines beyond the crop kernel's reach: a run's list (slot order) on the device, their raw crops
+  // (grown on demand), and the run's widest filter and tallest source span among them
+  int* d_wide_idx = nullptr;
+  uint8_t* d_wide = nullptr;
+  size_t cap_wide = 0;
+  int* hs_wide = nullptr;  // a call's lists, each run's from its first line's index (pinned)
+  size_t cap_hs_wide = 0;
+  int run_wide = 0, run_vtaps = 0, run_htaps = 0, run_rows = 0;
+  long long st_wide = 0;  // the last call's wide lines
   uint8_t* d_mask = nullptr;
   int* d_frame0 = nullptr;
   int* d_length = nullptr;
@@ -739,6 +749,8 @@ int encode_map4(crec_handle* h, CUtensorMap* m, const void* base, uint64_t cbyte
 
 // The crop kernel's shared memory for a run whose widest bucket is max_bw.
 size_t crop_smem_bytes(const crec_handle* h, int max_bw) { return crop_smem(h->height, max_bw).total + 16; }
+// crop_wide_kernel's shared memory, whatever the lines (one CTA an SM)
+constexpr size_t kWideSmem = 200 << 10;
 
 // Kernel kinds of the profile: 0 crop+stem, 1 dense convolutions (tcgen05), 2 depthwise, 3 head+CTC, 4 collapse.
 enum ProfKind { kProfCrop = 0, kProfConv = 1, kProfDw = 2, kProfHead = 3, kProfCollapse = 4 };
@@ -983,19 +995,52 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.out_pitch = s0.pitch;
     p.out_shift = s0.shift;
     p.err = h->d_err;
+    p.claim = h->d_claim;
+    p.wide = h->d_wide;
+    p.wide_pitch = h->cfg.max_width;
     int max_bw = 8;
     for (int i = 0; i < n; ++i) max_bw = std::max(max_bw, h->run_bw[i]);
     p.max_bw = max_bw;
     const size_t smem = crop_smem_bytes(h, max_bw);
     ProfScope prof(h, kProfCrop, 0);
-    // the attribute is the function's, for every handle in the process: set it for this one's size
-    if (h->int8) {
-      CK(cudaFuncSetAttribute(crop_stem_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-      crop_stem_kernel<true><<<n, kCropThreads, smem, s>>>(p);
-    } else {
-      CK(cudaFuncSetAttribute(crop_stem_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-      crop_stem_kernel<false><<<n, kCropThreads, smem, s>>>(p);
+    if (h->run_wide > 0 && !h->run_crops) {
+      // the lines beyond the crop kernel's reach first, into their raw crops
+      WideParams w{};
+      w.pages = h->d_pages;
+      w.lines = h->d_lines;
+      w.index = h->d_wide_idx;
+      w.height = h->height;
+      w.vtaps = h->run_vtaps;
+      w.htaps = h->run_htaps;
+      w.out = h->d_wide;
+      w.pitch = h->cfg.max_width;
+      w.err = h->d_err;
+      // 64 columns of coefficients a strip where they fit; the intermediate takes the rest of
+      // kWideSmem, and must hold one column of the tallest span
+      w.hk_cols = std::max(1, std::min(64, static_cast<int>(kWideSmem / 4 / static_cast<size_t>(4 * (w.htaps + 2)))));
+      const size_t fixed = wide_smem(w.height, w.vtaps, w.htaps, w.hk_cols, 0);
+      if (fixed >= kWideSmem || kWideSmem - fixed < static_cast<size_t>(h->run_rows))
+        return set_error(h, CREC_E_RANGE, "a line's source span (" + std::to_string(h->run_rows) + " rows, " +
+                                              std::to_string(std::max(w.vtaps, w.htaps)) +
+                                              " taps) beyond the resampler's shared memory");
+      w.tmp_bytes = static_cast<int>(kWideSmem - fixed) & ~15;
+      CK(cudaFuncSetAttribute(crop_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kWideSmem)));
+      crop_wide_kernel<<<h->run_wide, kCropThreads, kWideSmem, s>>>(w);
+      CK(cudaGetLastError());
+      ++h->st_launches;  // timed with the crop's
     }
+    // persistent: as many CTAs as fit at once (each takes lines until none are left)
+    auto launch = [&](auto* k) -> int {
+      // the attribute is the function's, for every handle in the process: set it for this one's size
+      CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+      int per_sm = 0;
+      CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kCropThreads, smem));
+      const int grid = std::min(n, std::max(1, per_sm) * h->sms);
+      k<<<grid, kCropThreads, smem, s>>>(p);
+      return CREC_OK;
+    };
+    const int lrc = h->int8 ? launch(crop_stem_kernel<true>) : launch(crop_stem_kernel<false>);
+    if (lrc) return lrc;
     CK(cudaGetLastError());
   }
   for (size_t li = 1; li < h->l.size(); ++li) {
@@ -1179,8 +1224,10 @@ struct Source {  // where a call's lines come from
 int layout_run(crec_handle* h, const Source& src, const int* bw, int a, int b, size_t mask_off, long long* cols_out) {
   const crec_crop_rule& rule = h->cfg.crop;
   long long seg = h->gap;
+  h->run_wide = h->run_vtaps = h->run_htaps = h->run_rows = 0;
   for (int i = a; i < b; ++i) {
     LineDesc& d = h->hs_lines[i];
+    d.wide = -1;
     double reg[4] = {0, 0, 1, 1};
     int width = 0;
     if (src.crops) {
@@ -1197,10 +1244,21 @@ int layout_run(crec_handle* h, const Source& src, const int* bw, int a, int b, s
       if (width > bw[i])
         return set_error(h, CREC_E_RANGE, "crop_lines: line " + std::to_string(i) + " is " + std::to_string(width) +
                                               " px wide, the batch " + std::to_string(bw[i]));
-      const double scale_x = (reg[2] - reg[0]) / width, scale_y = (reg[3] - reg[1]) / rule.height;
-      // the kernel's reach: at most kMaxTaps taps a sample (support up to 15), kMaxSrcRows source rows
-      if (!(scale_x <= 15.0) || !(scale_y <= 15.0) || (reg[3] - reg[1]) + 2 * std::max(1.0, scale_y) + 2 > kMaxSrcRows)
-        return set_error(h, CREC_E_RANGE, "line " + std::to_string(i) + ": a downscale beyond this build's filter reach");
+      // the crop kernel's reach: at most kMaxTaps taps a sample (PIL's ksize, 2 ceil(support) + 1)
+      // and kMaxSrcRows source rows (the bound the kernel computes); past it, crop_wide_kernel
+      const double sx = std::max(1.0, (reg[2] - reg[0]) / width), sy = std::max(1.0, (reg[3] - reg[1]) / rule.height);
+      if (!(sx < 1e6) || !(sy < 1e6))
+        return set_error(h, CREC_E_RANGE, "line " + std::to_string(i) + ": a degenerate crop region");
+      const int ht = static_cast<int>(std::ceil(sx)) * 2 + 1, vt = static_cast<int>(std::ceil(sy)) * 2 + 1;
+      const int rows = static_cast<int>(std::ceil((reg[3] - reg[1]) + 2.0 * sy)) + 4;
+      d.wide = -1;
+      if (ht > kMaxTaps || vt > kMaxTaps || rows > kMaxSrcRows) {
+        d.wide = h->run_wide;
+        h->hs_wide[a + h->run_wide++] = i - a;
+        h->run_htaps = std::max(h->run_htaps, ht);
+        h->run_vtaps = std::max(h->run_vtaps, vt);
+        h->run_rows = std::max(h->run_rows, rows);
+      }
       d.page = pg;
     }
     d.x0 = reg[0];
@@ -1258,6 +1316,7 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
   if ((rc = grow_pinned(h, &h->hs_lines, &h->cap_lines, n)) || (rc = grow_pinned(h, &h->hs_frame0, &h->cap_frame0, n)) ||
       (rc = grow_pinned(h, &h->hs_length, &h->cap_length, n)) ||
       (rc = grow_pinned(h, &h->hs_mask, &h->cap_mask, mask_total)) ||
+      (rc = grow_pinned(h, &h->hs_wide, &h->cap_hs_wide, n)) ||
       (rc = grow_device(h, &h->dp_counts, &cap_dp_lines, n)) || (rc = grow_device(h, &h->dp_offsets, &cap_dp_a, n)) ||
       (rc = grow_device(h, &h->dp_ids, &cap_dp_chars, frame_total)) ||
       (rc = grow_device(h, &h->dp_frames, &cap_dp_c, frame_total)) ||
@@ -1267,6 +1326,7 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
   h->cap_dp_chars = std::min({cap_dp_chars, cap_dp_c, cap_dp_d});
   cudaStream_t s = h->stream;
   h->st_runs = static_cast<long long>(runs.size());
+  h->st_wide = 0;
   h->st_launches = 0;
   h->st_h2d = 0;
   h->st_d2h = 4 + 8;  // the error word, the total
@@ -1276,6 +1336,13 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
     long long cols = 0;
     if ((rc = layout_run(h, src, bw, r.a, r.b, r.mask_off, &cols))) return rc;
     const int m = r.b - r.a;
+    if (h->run_wide > 0) {
+      const size_t need = static_cast<size_t>(h->run_wide) * h->height * h->cfg.max_width;
+      if ((rc = grow_device(h, &h->d_wide, &h->cap_wide, need))) return rc;
+      CK(cudaMemcpyAsync(h->d_wide_idx, h->hs_wide + r.a, sizeof(int) * h->run_wide, cudaMemcpyHostToDevice, s));
+      h->st_h2d += static_cast<long long>(sizeof(int)) * h->run_wide;
+      h->st_wide += h->run_wide;
+    }
     CK(cudaMemcpyAsync(h->d_lines, h->hs_lines + r.a, sizeof(LineDesc) * m, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(h->d_mask, h->hs_mask + r.mask_off, static_cast<size_t>(cols / 8), cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(h->d_frame0, h->hs_frame0 + r.a, sizeof(int) * m, cudaMemcpyHostToDevice, s));
@@ -1312,6 +1379,8 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
     CK(cudaErrorLaunchFailure);
   }
   if (h->profile) collect_profile(h);
+  if (*h->h_err == kErrBadShape)
+    return set_error(h, CREC_E_RANGE, "a line's crop beyond the resamplers' reach");
   if (*h->h_err)
     return set_error(h, CREC_E_TIMEOUT, "a kernel's bounded wait ran out (device error " + std::to_string(*h->h_err) + ")");
   const long long total = *h->h_total;
@@ -1380,6 +1449,10 @@ void free_all(crec_handle* h) {
   cudaFree(h->d_err);
   cudaFree(h->d_crops);
   cudaFree(h->d_crops_in);
+  cudaFree(h->d_claim);
+  cudaFree(h->d_wide_idx);
+  cudaFree(h->d_wide);
+  cudaFreeHost(h->hs_wide);
   cudaFree(h->d_logits);
   cudaFreeHost(h->hs_lines);
   cudaFreeHost(h->hs_frame0);
@@ -1461,8 +1534,10 @@ int open_impl(crec_handle* h, const crec_config* c) {
       (rc = dev_alloc(h, &h->d_length, ml)) || (rc = dev_alloc(h, &h->d_frame_id, frames)) ||
       (rc = dev_alloc(h, &h->d_frame_prob, frames)) || (rc = dev_alloc(h, &h->d_count, ml)) ||
       (rc = dev_alloc(h, &h->d_ids, frames)) || (rc = dev_alloc(h, &h->d_frames, frames)) ||
-      (rc = dev_alloc(h, &h->d_probs, frames)) || (rc = dev_alloc(h, &h->d_err, 1)))
+      (rc = dev_alloc(h, &h->d_probs, frames)) || (rc = dev_alloc(h, &h->d_err, 1)) ||
+      (rc = dev_alloc(h, &h->d_claim, 2)) || (rc = dev_alloc(h, &h->d_wide_idx, ml)))
     return rc;
+  CK(cudaMemset(h->d_claim, 0, 2 * sizeof(int)));
   if ((rc = host_alloc(h, &h->h_err, 1)) || (rc = host_alloc(h, &h->h_total, 1)) ||
       (rc = dev_alloc(h, &h->d_total, 1)))
     return rc;
@@ -2017,6 +2092,7 @@ int crec_last_stats(const crec_handle* h, crec_stats* out) {
     out->h2d_total = h->tot_h2d + h->up_h2d;
   }
   out->d2h_total = h->tot_d2h;
+  out->wide_lines = h->st_wide;
   return CREC_OK;
 }
 

@@ -45,7 +45,7 @@ struct LineDesc {
   double x0, y0, x1, y1;  // the crop region (crop_region)
   int page, width, bw, seg;  // crop width, bucket width, first column of its segment (input resolution)
   int next_seg;              // first column of the next line's segment (or the group's total)
-  int pad_;
+  int wide;                  // -1, or the line's slot in the wide crops (resampled by crop_wide_kernel)
 };
 
 struct CropParams {
@@ -75,6 +75,25 @@ struct CropParams {
   long long out_pitch;
   int out_shift;  // log2 of input columns per stem column
   int* err;
+  int* claim;  // [2] lines claimed past the first wave, CTAs done: both 0 between launches
+  const uint8_t* wide;  // the wide lines' resampled crops, [slot][height][wide_pitch]
+  int wide_pitch;
+};
+
+// The lines beyond the fast resampler's reach (more than kMaxTaps taps a sample, or more than
+// kMaxSrcRows source rows): resampled by crop_wide_kernel into raw crops in global memory, which
+// crop_stem_kernel then finishes like its own.
+struct WideParams {
+  const PageDesc* pages;
+  const LineDesc* lines;
+  const int* index;  // the run's wide lines, in slot order
+  int height;
+  int vtaps, htaps;  // vertical / horizontal taps a sample at most (PIL's ksize over the lines)
+  int hk_cols;       // columns of horizontal coefficients a strip
+  int tmp_bytes;     // the intermediate: source rows x strip columns
+  uint8_t* out;      // [slot][height][pitch]
+  int pitch;
+  int* err;
 };
 
 __device__ __forceinline__ double tri(double x) {
@@ -87,16 +106,17 @@ __device__ __forceinline__ int floor_i(double v) {
 }
 
 // The coefficients of output sample xx of a filter over [in0, in1) to `out` samples:
-// returns the first source index, the count in *n (at most kMaxTaps: the host checks the
-// scale), the fixed-point weights in k[0 .. n) (shared memory).
-__device__ __forceinline__ int coeffs(double in0, double in1, int out, int xx, int32_t* k, int* n) {
+// returns the first source index, the count in *n, the fixed-point weights in k[0 .. n) (shared
+// memory).  The count is at most PIL's ksize, 2 ceil(support) + 1 (the windows' bound), and the
+// callers check that ksize is within max_taps before they call.
+__device__ __forceinline__ int coeffs(double in0, double in1, int out, int xx, int32_t* k, int* n, int max_taps = kMaxTaps) {
   const double scale = __ddiv_rn(__dsub_rn(in1, in0), static_cast<double>(out));
   const double fs = scale < 1.0 ? 1.0 : scale;
   const double support = __dmul_rn(1.0, fs), ss = __ddiv_rn(1.0, fs);
   const double center = __dadd_rn(in0, __dmul_rn(__dadd_rn(static_cast<double>(xx), 0.5), scale));
   const int xmin = floor_i(__dadd_rn(__dsub_rn(center, support), 0.5));
   int cnt = floor_i(__dadd_rn(__dadd_rn(center, support), 0.5)) - xmin;
-  if (cnt > kMaxTaps) cnt = kMaxTaps;
+  if (cnt > max_taps) cnt = max_taps;
   double ww = 0.0;
   for (int x = 0; x < cnt; ++x)
     ww = __dadd_rn(ww, tri(__dmul_rn(__dadd_rn(__dsub_rn(static_cast<double>(x + xmin), center), 0.5), ss)));
@@ -347,13 +367,38 @@ __device__ __forceinline__ void vpass(const uint8_t* col, const int32_t* vfirst,
   }
 }
 
+// The source region a line's filter windows can reach into L2, a bulk prefetch a row (the copy
+// engine streams it in from DRAM while the CTA works on the line before; no thread waits on it),
+// each range rounded to 16 bytes inside the page's buffer.
+__device__ __forceinline__ void prefetch_line(const CropParams& p, int line, int tid, int nthr) {
+  const LineDesc L = p.lines[line];
+  if (p.crops_in || L.wide >= 0) return;
+  const PageDesc P = p.pages[L.page];
+  const int H = p.height, cw = L.width;
+  const double vsup = (L.y1 - L.y0) / H < 1.0 ? 1.0 : (L.y1 - L.y0) / H;
+  const double hsup = (L.x1 - L.x0) / cw < 1.0 ? 1.0 : (L.x1 - L.x0) / cw;
+  const int ylo = max(0, static_cast<int>(floor(L.y0 - vsup)) - 2), yhi = min(P.height, static_cast<int>(ceil(L.y1 + vsup)) + 2);
+  const int xlo = max(0, static_cast<int>(floor(L.x0 - hsup)) - 2), xhi = min(P.width, static_cast<int>(ceil(L.x1 + hsup)) + 2);
+  if (xhi <= xlo) return;
+  const uintptr_t first = reinterpret_cast<uintptr_t>(P.data);
+  const uintptr_t last = first + static_cast<uintptr_t>(static_cast<long long>(P.height - 1) * P.stride + P.width);
+  for (int y = ylo + tid; y < yhi; y += nthr) {
+    const uintptr_t row = first + static_cast<uintptr_t>(static_cast<long long>(y) * P.stride);
+    uintptr_t a = (row + xlo) & ~uintptr_t(15), b = (row + xhi + 15) & ~uintptr_t(15);
+    if (a < first) a += 16;
+    if (b > last) b -= 16;
+    if (b > a) l2_prefetch_bulk(reinterpret_cast<const void*>(a), static_cast<uint32_t>(b - a));
+  }
+}
+
+// Persistent: a CTA takes lines one after another (its first is blockIdx.x, the next ones claimed
+// from p.claim[0] as it starts each line, so that the next line's region is prefetched while this
+// one is worked on); the stem's constants and the tables are set up once a CTA.
 template <bool kInt8>
 __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid_constant__ CropParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
-  const int line = blockIdx.x;
-  const LineDesc L = p.lines[line];
-  const PageDesc P = p.pages[L.page];
-  const int H = p.height, bw = L.bw, cw = p.crops_in ? L.bw : L.width;
+  __shared__ int s_next;
+  const int H = p.height;
   const CropSmem S = crop_smem(H, p.max_bw);
   const int qpitch = S.qpitch;
   uint8_t* qb = sm + S.qb;
@@ -375,6 +420,8 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int taps_stem = p.kh * p.kw;
   auto px = [&](int y, int x) -> uint8_t& { return qb[(y + 2) * qpitch + x + 4]; };
+  int line = blockIdx.x;
+  if (line < p.n) prefetch_line(p, line, tid, nthr);
 
   // the stem's constants; INT8: a channel's taps as one word per kernel row (zeros past kw), and
   // the offset that turns the sum into kMagicBits + (sum - in_zero * colsum): |sum| <= 9 * 255 * 128
@@ -404,34 +451,31 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
     if (kInt8) stab[i] = p.in_table[i];
     // the FP16 engine's input: the ink 1 - p / 255 rounded to float16
     ftab[i] = __half2float(__float2half_rn(__fsub_rn(1.0f, __fdiv_rn(static_cast<float>(i), 255.0f))));
-    hist[i] = 0;
   }
+
+  while (line < p.n) {
+  if (tid == 0) s_next = static_cast<int>(gridDim.x) + atomicAdd(p.claim, 1);
+  for (int i = tid; i < 256; i += nthr) hist[i] = 0;
   if (tid < 8) red[tid] = 0;
-  __syncthreads();  // the tables and counters before any use (a ready crop goes straight to the final pass)
+  // the tables and counters before any use (a ready crop goes straight to the final pass), the
+  // claim; the line before is done with shared memory
+  __syncthreads();
+  const int next = s_next;
+  if (next < p.n) prefetch_line(p, next, tid, nthr);
+  const LineDesc L = p.lines[line];
+  const PageDesc P = p.pages[L.page];
+  const int bw = L.bw, cw = p.crops_in ? L.bw : L.width;
 
   bool flip = false;
   uint8_t ground = 0;
-  if (!p.crops_in) {
-    // the source region into L2 first (the rows and columns the filters' windows can reach), a
-    // bulk prefetch a row (the copy engine streams it in from DRAM while the coefficients are
-    // computed; no thread waits on it), each range rounded to 16 bytes inside the page's buffer
-    {
-      const double vsup = (L.y1 - L.y0) / H < 1.0 ? 1.0 : (L.y1 - L.y0) / H;
-      const double hsup = (L.x1 - L.x0) / cw < 1.0 ? 1.0 : (L.x1 - L.x0) / cw;
-      const int ylo = max(0, static_cast<int>(floor(L.y0 - vsup)) - 2), yhi = min(P.height, static_cast<int>(ceil(L.y1 + vsup)) + 2);
-      const int xlo = max(0, static_cast<int>(floor(L.x0 - hsup)) - 2), xhi = min(P.width, static_cast<int>(ceil(L.x1 + hsup)) + 2);
-      if (xhi > xlo) {
-        const uintptr_t first = reinterpret_cast<uintptr_t>(P.data);
-        const uintptr_t last = first + static_cast<uintptr_t>(static_cast<long long>(P.height - 1) * P.stride + P.width);
-        for (int y = ylo + tid; y < yhi; y += nthr) {
-          const uintptr_t row = first + static_cast<uintptr_t>(static_cast<long long>(y) * P.stride);
-          uintptr_t a = (row + xlo) & ~uintptr_t(15), b = (row + xhi + 15) & ~uintptr_t(15);
-          if (a < first) a += 16;
-          if (b > last) b -= 16;
-          if (b > a) l2_prefetch_bulk(reinterpret_cast<const void*>(a), static_cast<uint32_t>(b - a));
-        }
-      }
+  if (!p.crops_in && L.wide >= 0) {
+    // resampled by crop_wide_kernel: its raw crop into place
+    const uint8_t* src = p.wide + static_cast<long long>(L.wide) * H * p.wide_pitch;
+    for (int i = tid; i < H * cw; i += nthr) {
+      const int y = i / cw, x = i - y * cw;
+      px(y, x) = src[y * p.wide_pitch + x];
     }
+  } else if (!p.crops_in) {
     // this line's tap stride (PIL's ksize), from a bound on the source rows the vertical windows
     // span (each window lies within [y0 - support - 1, y1 + support + 1]), and the taps a window
     // has at most: [floor(c - s + 0.5), floor(c + s + 0.5)) holds at most ceil(2 s) + 1 samples
@@ -443,6 +487,12 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
     const int rows_ub = static_cast<int>(ceil(vspan + 2.0 * vsup)) + 4;
     const int nwh = (min(kMaxTaps, static_cast<int>(ceil(2.0 * hsup)) + 1) + 3) >> 2;
     const int nwv = (min(kMaxTaps, static_cast<int>(ceil(2.0 * vsup)) + 1) + 3) >> 2;
+    // beyond this kernel's reach (the host sends such lines to crop_wide_kernel)
+    if (static_cast<int>(ceil(vsup)) * 2 + 1 > kMaxTaps || static_cast<int>(ceil(hsup)) * 2 + 1 > kMaxTaps ||
+        rows_ub > kMaxSrcRows) {
+      if (tid == 0) atomicCAS(p.err, 0, kErrBadShape);
+      break;
+    }
     // the intermediate, column-major: a column of the strip holds its source rows contiguous in
     // rp bytes (the 8-row chunks, and the vertical windows' word reads, stay inside), rp / 4 odd
     // so that a warp's columns fall in distinct banks
@@ -458,7 +508,7 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
       for (int xx = tid; xx < count; xx += nthr) {
         int32_t* c = hk + xx * (T + 2);
         int n;
-        c[0] = coeffs(L.x0, L.x1, cw, x0 + xx, c + 2, &n);
+        c[0] = coeffs(L.x0, L.x1, cw, x0 + xx, c + 2, &n, T);
         c[1] = n;
       }
     };
@@ -493,7 +543,7 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
     const int rows = vfirst[H - 1] + vcount[H - 1] - top;
     if (rows > kMaxSrcRows || rows > rows_ub || strip * rp > kStripBytes) {
       if (tid == 0) atomicCAS(p.err, 0, kErrBadShape);
-      return;
+      break;
     }
     const int nchunks = (rows + 7) >> 3;
     const bool same_sel = (P.stride & 3) == 0;
@@ -582,6 +632,8 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
         }
       }
     }
+  }
+  if (!p.crops_in) {
     __syncthreads();
     // finish: the ground's histogram (first row, last row, last column)
     for (int x = tid; x < cw; x += nthr) {
@@ -848,6 +900,103 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
     const int c = rest % gapn, oy = rest / gapn;
     const long long col = c < lead ? c : gap0 + (c - lead);
     *reinterpret_cast<uint4*>(p.out + (oy + p.out_ph) * p.out_pitch + col * p.cp_out * eb + v * 16) = z4;
+  }
+  line = next;
+  }
+  // the claim counters back to 0 for the next launch, by the last CTA out (every claim is made by
+  // then: a CTA counts itself out after its last claim)
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(p.claim + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+      p.claim[0] = 0;
+      p.claim[1] = 0;
+    }
+  }
+}
+
+// Shared memory of crop_wide_kernel: vertical coefficients [height][vtaps], their first rows and
+// counts, a strip's horizontal coefficients [hk_cols][htaps + 2] (first, count, taps), the
+// intermediate [rows][strip columns].
+__host__ __device__ inline size_t wide_smem(int height, int vtaps, int htaps, int hk_cols, int tmp_bytes) {
+  return static_cast<size_t>(height) * (vtaps + 2) * 4 + static_cast<size_t>(hk_cols) * (htaps + 2) * 4 +
+         static_cast<size_t>(tmp_bytes);
+}
+
+// The resampling of a line beyond crop_stem_kernel's reach (downscales past 15x, or more source
+// rows than kMaxSrcRows), one CTA a line, the scalar passes of carbon/src/lines.cpp:117-147
+// (resample_scalar): the same coefficients (coeffs), the horizontal pass over every source row
+// the vertical windows span into an 8-bit intermediate, a strip of columns at a time, then the
+// vertical pass.  Writes the raw crop (not yet finished) to out[slot]; crop_stem_kernel finishes it.
+__global__ void __launch_bounds__(kCropThreads) crop_wide_kernel(const __grid_constant__ WideParams p) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int slot = blockIdx.x;
+  const LineDesc L = p.lines[p.index[slot]];
+  const PageDesc P = p.pages[L.page];
+  const int H = p.height, cw = L.width;
+  int32_t* vk = reinterpret_cast<int32_t*>(sm);
+  int32_t* vfirst = vk + H * p.vtaps;
+  int32_t* vcount = vfirst + H;
+  int32_t* hk = vcount + H;
+  const int hstride = p.htaps + 2;
+  uint8_t* tmp = reinterpret_cast<uint8_t*>(hk + p.hk_cols * hstride);
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  // the line's ksize each way against the buffers' (uniform over the CTA)
+  const double hscale = (L.x1 - L.x0) / cw, hsup = hscale < 1.0 ? 1.0 : hscale;
+  const double vscale = (L.y1 - L.y0) / H, vsup = vscale < 1.0 ? 1.0 : vscale;
+  if (static_cast<int>(ceil(hsup)) * 2 + 1 > p.htaps || static_cast<int>(ceil(vsup)) * 2 + 1 > p.vtaps) {
+    if (tid == 0) atomicCAS(p.err, 0, kErrBadShape);
+    return;
+  }
+  for (int yy = tid; yy < H; yy += nthr) {
+    int n;
+    vfirst[yy] = coeffs(L.y0, L.y1, H, yy, vk + yy * p.vtaps, &n, p.vtaps);
+    vcount[yy] = n;
+  }
+  __syncthreads();
+  const int top = vfirst[0], rows = vfirst[H - 1] + vcount[H - 1] - top;
+  if (rows <= 0 || rows > p.tmp_bytes) {
+    if (tid == 0) atomicCAS(p.err, 0, kErrBadShape);
+    return;
+  }
+  const int strip = min(p.hk_cols, p.tmp_bytes / rows);
+  uint8_t* out = p.out + static_cast<long long>(slot) * H * p.pitch;
+  for (int x0 = 0; x0 < cw; x0 += strip) {
+    const int sc = min(strip, cw - x0);
+    for (int xx = tid; xx < sc; xx += nthr) {
+      int32_t* c = hk + xx * hstride;
+      int n;
+      c[0] = coeffs(L.x0, L.x1, cw, x0 + xx, c + 2, &n, p.htaps);
+      c[1] = n;
+    }
+    __syncthreads();
+    // horizontal: item (r, xx), the columns of a row side by side; pixels off the page read as paper
+    for (int i = tid; i < rows * sc; i += nthr) {
+      const int r = i / sc, xx = i - r * sc;
+      const int32_t* c = hk + xx * hstride;
+      const int xmin = c[0], n = c[1], y = top + r;
+      int32_t ss = 1 << 21;
+      if (y >= 0 && y < P.height) {
+        const uint8_t* src = P.data + static_cast<long long>(y) * P.stride;
+        for (int t = 0; t < n; ++t) {
+          const int x = xmin + t;
+          ss += ((x >= 0 && x < P.width) ? static_cast<int32_t>(__ldg(src + x)) : 255) * c[2 + t];
+        }
+      } else {
+        for (int t = 0; t < n; ++t) ss += 255 * c[2 + t];
+      }
+      tmp[i] = clip8d(ss);
+    }
+    __syncthreads();
+    // vertical: item (yy, xx)
+    for (int i = tid; i < H * sc; i += nthr) {
+      const int yy = i / sc, xx = i - yy * sc;
+      const int f = vfirst[yy] - top, n = vcount[yy];
+      const int32_t* k = vk + yy * p.vtaps;
+      int32_t ss = 1 << 21;
+      for (int t = 0; t < n; ++t) ss += static_cast<int32_t>(tmp[(f + t) * sc + xx]) * k[t];
+      out[yy * p.pitch + x0 + xx] = clip8d(ss);
+    }
+    __syncthreads();  // the strip's intermediate and coefficients before the next strip's
   }
 }
 

@@ -181,6 +181,7 @@ CREC_API int crec_crop_region(const crec_box* box, const crec_crop_rule* rule, d
 typedef struct crec_stats {
   int64_t runs, launches, h2d_bytes, d2h_bytes;
   int64_t h2d_total, d2h_total;
+  int64_t wide_lines; /* the last call's lines resampled by the wide-reach path (past 15x or 1024 source rows) */
 } crec_stats;
 CREC_API int crec_last_stats(const crec_handle* h, crec_stats* out);
 

@@ -269,6 +269,72 @@ def test_tall_lines_and_odd_strides_crop_bit_exact(rec_latin, orc):
             assert np.array_equal(crops[i], want[j]), (p, int(i), boxes[i])
 
 
+def wide_reach_pages(seed=13):
+    """A page with lines 350 to 600 px tall (downscales ~15x to ~26x: 33 to 55 taps a sample, past
+    the crop kernel's 31), 1000 to 1500 px tall (more than 1024 source rows), 250 to 340 px tall
+    (~11x to ~15x, just inside), some over the page's edges, among ordinary 20 to 60 px lines, all
+    in one run."""
+    rng = np.random.default_rng(seed)
+    w, h = 2481, 3508
+    page = np.clip(rng.normal(226, 14, (h, w)), 0, 255).astype(np.uint8)
+    for _ in range(3000):
+        x, y = int(rng.integers(0, w - 60)), int(rng.integers(0, h - 60))
+        page[y:y + int(rng.integers(4, 60)), x:x + int(rng.integers(2, 30))] = int(rng.integers(0, 90))
+    boxes = []
+    for lo, hi, count in ((350, 600, 40), (1000, 1500, 6), (250, 340, 12), (20, 60, 30)):
+        k = 0
+        while k < count:
+            bh = rng.uniform(lo, hi)
+            x0, y0 = rng.uniform(-100, w - 100), rng.uniform(-150, h - bh + 150)
+            bw = rng.uniform(40, 2600)
+            if (bw + 0.6 * bh) * 32 / (1.4 * bh) > 1000:
+                continue
+            boxes.append([x0, y0, x0 + bw, y0 + bh])
+            k += 1
+    boxes = np.asarray(boxes)[rng.permutation(len(boxes))]
+    return page, boxes
+
+
+def beyond_fast_reach(box) -> bool:
+    """The host's rule: PIL's ksize 2 ceil(max(1, scale)) + 1 either way above 31 taps, or more than
+    1024 source rows in the vertical windows' bound ceil(span + 2 support) + 4."""
+    reg, width = native.crop_region(box)
+    sx, sy = max(1.0, (reg[2] - reg[0]) / width), max(1.0, (reg[3] - reg[1]) / 32)
+    taps = 2 * int(np.ceil(max(sx, sy))) + 1
+    return taps > 32 or int(np.ceil((reg[3] - reg[1]) + 2 * sy)) + 4 > 1024
+
+
+def test_wide_reach_lines_crop_bit_exact(rec_latin, orc):
+    """Lines past the crop kernel's reach go through the scalar wide-reach kernel: their crops equal
+    the oracle's (and the reference's compiled crop_lines where it is here) byte for byte, the
+    others' too, and the decodings equal those of the run without crop copies."""
+    page, boxes = wide_reach_pages()
+    want_wide = sum(beyond_fast_reach(b) for b in boxes)
+    assert 10 <= want_wide < len(boxes)
+    page_of = np.zeros(len(boxes), np.int32)
+    dev = native.RecDevice(rec_latin[0].to_blob(), native.INT8, max_lines=256, max_width=1024, max_pages=1,
+                           max_page_bytes=page.size)
+    try:
+        dev.set_pages([page])
+        dev.arm_crops(1024)
+        dev.arm_logits()
+        got, lengths = dev.recognize(page_of, boxes, 1024)
+        assert dev.last_stats()["wide_lines"] == want_wide
+        crops = dev.crops(len(boxes), 1024)
+        dev_logits = dev.logits([1024] * len(boxes), 800)
+    finally:
+        dev.close()
+    want, _ = orc.crop_lines(page, boxes, 1024, O.CropRule.default())
+    for i in range(len(boxes)):
+        assert np.array_equal(crops[i], want[i]), (i, boxes[i], beyond_fast_reach(boxes[i]))
+    if O.Reference.available():
+        ref_crops, _ = O.Reference().crop_lines(page, boxes, 1024)
+        assert np.array_equal(np.asarray(crops)[:, :, :1024], ref_crops)
+    got2, lengths2, logits2 = decodings_without_crop_copies(rec_latin[0].to_blob(), [page], page_of, boxes,
+                                                            max_page_bytes=page.size)
+    assert_same_decodings(got, lengths, got2, lengths2, dev_logits, logits2)
+
+
 def test_scheduler_runs_are_independent_of_grouping(rec_latin):
     """Lines of several pages at their ladder buckets, cut into many runs (a small column budget) or
     one: the same decodings, each line's also the same as when it is read alone."""
