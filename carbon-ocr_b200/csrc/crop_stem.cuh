@@ -559,8 +559,7 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
       const int groups = max(1, nthr / sc);
       const int rg = tid / sc, xx = tid - rg * sc;
       const int32_t* c = hk + (x0 - xc0 + xx) * (T + 2);
-      // (also: the previous strip's vertical pass is done with tmp)
-      const bool hbad = __syncthreads_or(rg < groups && hbad_of(c)) != 0;
+      __syncthreads();  // the previous strip's vertical pass is done with tmp
       if (rg < groups) {
         // horizontal pass: every source row the vertical windows read, 8-row chunks split over
         // the row groups
@@ -568,7 +567,9 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
         int32_t paper = 0;  // a row off the page: 255 * the weights' sum
         for (int t = 0; t < n; ++t) paper += 255 * c[2 + t];
         uint8_t* col = tmp + xx * rp;
-        if (!hbad) {
+        // a column's own choice (its row groups agree: same coefficients), so that a window at
+        // the page's edge sends only its own column to the tap-by-tap loop below
+        if (!hbad_of(c)) {
 #define CREC_HPASS(NW)                                                                  \
   case NW:                                                                              \
     if (same_sel) hpass<NW, true>(P, c, paper, top, rg, nchunks, groups, col);          \
@@ -583,7 +584,7 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
           }
 #undef CREC_HPASS
         } else {
-          // a window off the page's edge (pixels there read as paper) or wider than the bound
+          // a window off the page's edge (pixels there read as paper)
           for (int r = rg; r < rows; r += groups) {
             const int y = top + r;
             int32_t ss = 1 << 21;
@@ -694,7 +695,10 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
       // a time; words across the border, the pad or the crop's right edge byte by byte
       // item i: row i / wpr, word i % wpr (the quotient a multiply-high by 2^32 / wpr rounded up,
       // exact while i * wpr < 2^32)
-      const int wpr = qpitch >> 2;
+      // only the words the stem reads: its windows' 8-byte reads start at most at qb column bw + 4
+      // (at most 4 columns of left padding) and end before bw + 12, so bw / 4 + 3 words a row (5,
+      // to spare); the rest of the run's widest row is never read for this line
+      const int wpr = min(qpitch >> 2, (bw >> 2) + 5);
       const uint32_t inv = static_cast<uint32_t>(0xffffffffu / static_cast<uint32_t>(wpr)) + 1u;
       const uint32_t fx = flip ? 0xffffffffu : 0u;
       for (int i = tid; i < (H + 4) * wpr; i += nthr) {
