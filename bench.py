@@ -310,10 +310,31 @@ def run_sweep(args) -> int:
                     tops = ops / (ms * 1e-3) / 1e12
                     rows.append({"precision": name, "c": c, "h": h, "w": w, "ms": round(ms, 4), "tops": round(tops, 1),
                                  "frac": round(tops / peaks[prec], 4)})
+    # the head GEMM [N T, K] x [K, classes] fused with the frames' argmax and CTC probabilities
+    # (crec_head_sweep): config 4's [256 x 256, 256] x [256, 800] and the reference's GPU-head cases' K
+    # and class counts at the same N T
+    heads = []
+    frames = n * 256
+    for prec, name in ((native.INT8, "int8"), (native.FP16, "fp16")):
+        for k, classes in ((256, 800), (128, 33), (192, 1500 if prec == native.FP16 else 1000), (320, 400)):
+            hr = np.random.default_rng(k + classes)
+            w = hr.normal(0.0, 0.06, (classes, k)).astype(np.float16).astype(np.float32)
+            b = hr.normal(0.0, 0.5, classes).astype(np.float32)
+            f = hr.normal(0.0, 1.0, (frames, k)).astype(np.float16)
+            fp, i8, (xs, xz) = model.make_head(k, classes, w, b, f[:4096].astype(np.float32).T[None, :, None, :])
+            if prec == native.INT8:
+                x = np.clip(np.rint(f.astype(np.float32) / np.float32(xs)) + xz, 0, 255).astype(np.uint8)
+            else:
+                x = f
+            blob = netdef.compile_model(i8 if prec == native.INT8 else fp).to_blob()
+            _, _, _, ms = native.head_sweep(blob, prec, x, classes, repeat=max(1, args.steps))
+            tops = 2.0 * frames * k * classes / (ms * 1e-3) / 1e12
+            heads.append({"precision": name, "frames": frames, "k": k, "classes": classes, "ms": round(ms, 4),
+                          "tops": round(tops, 1), "frac": round(tops / peaks[prec], 4)})
     out = {"metric": "config 4 kernel sweep: 3x3 s1 implicit-GEMM conv TOPS (N=256 lines)", "unit": "TOP/s",
            "peaks_measured": {"int8_n256_tops": peaks[native.INT8], "fp16_n256_tflops": peaks[native.FP16]},
            "timing": f"CUDA events, mean of {max(1, args.steps)} launches after a warm-up, inputs resident",
-           "shapes": rows}
+           "shapes": rows, "heads": heads}
     print(json.dumps(out))
     return 0
 

@@ -336,3 +336,35 @@ def make_conv(c_in: int, c_out: int, height: int, seed: int = 0, stride: int = 1
     yname = "conv.relu" if relu else "conv.out"
     quant = {"x": params(float(sample.min()), float(sample.max())), yname: params(float(out.min()), float(out.max()))}
     return fp, build(quant), quant["x"]
+
+
+def make_head(k: int, classes: int, w: np.ndarray, b: np.ndarray, sample: np.ndarray):
+    """BASELINE.json config 4's head: one 1x1 convolution, k -> classes, with the given weights
+    [classes, k] and biases [classes], on inputs [N, k, 1, W]: (fp32 ONNX, int8 Q/DQ ONNX, (input
+    scale, input zero point)).  The INT8 file quantizes the input per tensor and the output by MinMax
+    over a float run, both from `sample` [N, k, 1, W]; its output is the codes' Q/DQ, as rec-latin's
+    head ends."""
+    wt = {"head.w": np.asarray(w, np.float32).reshape(classes, k, 1, 1), "head.b": np.asarray(b, np.float32)}
+
+    def build(quant):
+        bl = _Builder(quant, wt)
+        x = bl.qdq("x")
+        y = bl.conv("head", x, 1, 1, 1, 1, (0, 0, 0, 0), False)
+        out = y
+        if quant is not None:
+            bl.node("Identity", [bl.qdq(y)], ["y"])
+            out = bl.qdq("y", params_of=y)
+        bl.g.inputs = [pb.ValueInfo("x", pb.FLOAT, ["N", k, 1, "W"])]
+        bl.g.outputs = [pb.ValueInfo(out, pb.FLOAT, ["N", classes, 1, "W"])]
+        return pb.Model(bl.g, 17, {})
+
+    fp = build(None)
+    out = forward_float(netdef.compile_model(fp), np.asarray(sample, np.float32))
+
+    def params(lo, hi):
+        lo, hi = min(lo, 0.0), max(hi, 0.0)
+        s = np.float32((hi - lo) / 255.0)
+        return float(s), int(np.clip(np.rint(-lo / float(s)), 0, 255))
+
+    quant = {"x": params(float(sample.min()), float(sample.max())), "head.out": params(float(out.min()), float(out.max()))}
+    return fp, build(quant), quant["x"]

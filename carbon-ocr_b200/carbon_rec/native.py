@@ -27,7 +27,8 @@ _NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA
 EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec_set_pages", "crec_prefetch_pages",
            "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_ctc_greedy", "crec_ctc_greedy_noalloc", "crec_width_bucket", "crec_crop_region",
            "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats",
-           "crec_profile", "crec_profile_layers", "crec_mma_peak", "crec_debug_inject", "crec_conv_sweep"]
+           "crec_profile", "crec_profile_layers", "crec_mma_peak", "crec_debug_inject", "crec_conv_sweep",
+           "crec_head_sweep"]
 
 
 class CrecError(RuntimeError):
@@ -117,6 +118,7 @@ def lib() -> C.CDLL:
         L.crec_mma_peak.argtypes = [i, i, i, i, C.POINTER(C.c_double)]
         L.crec_debug_inject.argtypes = [p, i]
         L.crec_conv_sweep.argtypes = [i, i, p, C.c_size_t, i, i, i, p, p, i, C.POINTER(C.c_double)]
+        L.crec_head_sweep.argtypes = [i, i, p, C.c_size_t, i, p, p, p, p, i, C.POINTER(C.c_double)]
         _lib = L
     return _lib
 
@@ -170,6 +172,26 @@ def conv_sweep(blob: bytes, precision: int, x: np.ndarray, c_out: int, repeat: i
     if rc != OK:
         raise CrecError(rc, "crec_conv_sweep")
     return y, ms.value
+
+
+def head_sweep(blob: bytes, precision: int, x: np.ndarray, classes: int, repeat: int = 3, device: int = 0,
+               logits: bool = False):
+    """crec_head_sweep: x [frames, K] (uint8 codes for INT8, float16 for FP16) through the blob's one
+    1x1 convolution as the fused head: (ids [frames], probs [frames], logits [frames, classes] or
+    None, ms a launch)."""
+    x = np.ascontiguousarray(x)
+    frames = x.shape[0]
+    ids = np.zeros(frames, np.int32)
+    probs = np.zeros(frames, np.float32)
+    lg = np.zeros((frames, classes), np.float32) if logits else None
+    ms = C.c_double(0.0)
+    b = C.create_string_buffer(bytes(blob), len(blob))
+    rc = lib().crec_head_sweep(device, precision, C.cast(b, C.c_void_p), len(blob), frames, x.ctypes.data,
+                               ids.ctypes.data, probs.ctypes.data, lg.ctypes.data if logits else None, repeat,
+                               C.byref(ms))
+    if rc != OK:
+        raise CrecError(rc, "crec_head_sweep")
+    return ids, probs, lg, ms.value
 
 
 def width_bucket(crop_width: int) -> int:

@@ -610,19 +610,23 @@ int setup_layer(crec_handle* h, size_t li) {
   l.nkb = (window + 127) / 128;
   l.last_steps = (window - (l.nkb - 1) * 128 + 31) / 32;
   if (li + 1 == h->l.size()) {  // the head
-    if (l.nkb * 16384 > 65536) return set_error(h, CREC_E_MODEL, "a head reading more than 512 bytes a frame");
+    if (l.nkb > 8) return set_error(h, CREC_E_MODEL, "a head reading more than 1024 bytes a frame");
     l.krows = 1;
-    l.nchunk = std::min(kHeadChunk, round16(l.cout));
-    l.chunks = (l.cout + l.nchunk - 1) / l.nchunk;
+    // a tile's frames stay resident (A: all K blocks) beside two class chunks of weights (B):
+    // the widest chunk (N, up to 128 classes) with which that fits
+    const uint32_t codes = h->int8 ? 128u * head_code_stride(l.cout) : 0u;
+    l.a_bytes = static_cast<uint32_t>(l.nkb) * 16384;
+    for (l.nchunk = std::min(kHeadChunk, round16(l.cout));; l.nchunk -= 16) {
+      l.chunks = (l.cout + l.nchunk - 1) / l.nchunk;
+      l.b_bytes = static_cast<uint32_t>(l.nkb) * l.nchunk * 128;
+      l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + head_tail_bytes(l.chunks * l.nchunk);
+      if (l.smem + 1024 <= 232448) break;
+      if (l.nchunk == 16) return set_error(h, CREC_E_MODEL, "the head does not fit in shared memory");
+    }
     l.nt = l.nchunk;
     l.cq = l.nt;
     l.n_tiles = l.chunks;
-    l.a_bytes = static_cast<uint32_t>(l.nkb) * 16384;
-    l.b_bytes = static_cast<uint32_t>(l.nkb) * l.nchunk * 128;
-    const uint32_t codes = h->int8 ? 128u * head_code_stride(l.cout) : 0u;
     const int ncls = l.chunks * l.nchunk;
-    l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + head_tail_bytes(ncls);
-    if (l.smem + 1024 > 232448) return set_error(h, CREC_E_MODEL, "the head does not fit in shared memory");
     if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, ncls))) return rc;
   } else {
     // row stacking: the number of output rows a tile computes that gets the most outputs from
@@ -953,6 +957,74 @@ int launch_conv(crec_handle* h, size_t li, long long cols) {
   return CREC_OK;
 }
 
+// The head (the last layer, a 1x1 convolution on one row) over `cols` input columns, fused with the
+// frames' argmax and (INT8: in a kernel of its own after it) their CTC probabilities.
+int launch_head(crec_handle* h, size_t li, long long cols) {
+  cudaStream_t s = h->stream;
+  const Layer& l = h->l[li];
+  const Value& x = h->v[l.in];
+  const Value& y = h->v[l.out];
+  const Value& xp = h->v[x.phys];
+  const long long ow = cols >> y.shift;
+  HeadParams p{};
+  // a frame's K bytes exactly: the last K block's box past them reads zeros (TMA's fill), not the
+  // next frame's bytes
+  int rc = encode_map(h, &p.tmap, xp.base + static_cast<long long>(xp.ph) * xp.pitch,
+                      static_cast<uint64_t>(x.cp) * h->eb, static_cast<uint64_t>(ow), 1,
+                      static_cast<uint64_t>(x.cp) * h->eb, static_cast<uint64_t>(xp.pitch));
+  if (rc) return rc;
+  p.wimg = l.wimg;
+  p.nkb = l.nkb;
+  p.last_steps = l.last_steps;
+  p.classes = l.cout;
+  p.nchunk = l.nchunk;
+  p.chunks = l.chunks;
+  p.ow = static_cast<int>(ow);
+  p.num_tiles = static_cast<int>((ow + 127) / 128);
+  p.a_bytes = l.a_bytes;
+  p.b_bytes = l.b_bytes;
+  p.off = l.hoff;
+  p.scale = l.scale;
+  p.bias = l.dbias;
+  p.out_zero = y.zero;
+  p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
+  p.table = h->head_table;
+  p.nb_codes = h->d_nb_codes;
+  p.nb_row_bytes = h->nb_row_bytes;
+  p.nb_frame = h->d_nb_frame;
+  p.nb_best = h->d_nb_best;
+  p.nb_count = h->d_nb_count;
+  p.mask8 = h->d_mask;
+  p.out_shift = y.shift;
+  p.frame_id = h->d_frame_id;
+  p.frame_prob = h->d_frame_prob;
+  p.logits = h->d_logits;
+  p.err = h->d_err;
+  const int grid = std::min(p.num_tiles, h->sms);
+  p.nb_region = (p.num_tiles + grid - 1) / grid * 128;
+  ProfScope prof(h, kProfHead, static_cast<int>(li));
+  if (h->int8 && l.fast) {
+    CK(cudaFuncSetAttribute(head_ctc_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+    head_ctc_kernel<true, true><<<grid, kHeadThreads, l.smem, s>>>(p);
+  } else if (h->int8) {
+    CK(cudaFuncSetAttribute(head_ctc_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+    head_ctc_kernel<true, false><<<grid, kHeadThreads, l.smem, s>>>(p);
+  } else {
+    CK(cudaFuncSetAttribute(head_ctc_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+    head_ctc_kernel<false, false><<<grid, kHeadThreads, l.smem, s>>>(p);
+  }
+  CK(cudaGetLastError());
+  if (h->int8) {  // the listed frames' class-order sums
+    ProfScope sums(h, kProfHead, static_cast<int>(li));
+    const int smem = kSumRows * 256 * static_cast<int>(sizeof(float));
+    CK(cudaFuncSetAttribute(ctc_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    ctc_sums_kernel<<<grid, kSumThreads, smem, s>>>(h->d_nb_codes, h->nb_row_bytes, h->d_nb_frame, h->d_nb_best,
+                                                    h->d_nb_count, p.nb_region, h->ctc_terms, l.cout, h->d_frame_prob);
+    CK(cudaGetLastError());
+  }
+  return CREC_OK;
+}
+
 // Launches every layer for the lines laid out in h_lines (already on the device), `cols` input columns.
 int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
   cudaStream_t s = h->stream;
@@ -1052,60 +1124,8 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     const int oh = y.h;
     const long long ow = cols >> y.shift;
     if (li + 1 == h->l.size()) {
-      HeadParams p{};
-      int rc = encode_map(h, &p.tmap, xp.base + static_cast<long long>(xp.ph) * xp.pitch,
-                          static_cast<uint64_t>(l.nkb) * 128, static_cast<uint64_t>(ow), 1,
-                          static_cast<uint64_t>(x.cp) * h->eb, static_cast<uint64_t>(xp.pitch));
+      const int rc = launch_head(h, li, cols);
       if (rc) return rc;
-      p.wimg = l.wimg;
-      p.nkb = l.nkb;
-      p.last_steps = l.last_steps;
-      p.classes = l.cout;
-      p.nchunk = l.nchunk;
-      p.chunks = l.chunks;
-      p.ow = static_cast<int>(ow);
-      p.num_tiles = static_cast<int>((ow + 127) / 128);
-      p.a_bytes = l.a_bytes;
-      p.b_bytes = l.b_bytes;
-      p.off = l.hoff;
-      p.scale = l.scale;
-      p.bias = l.dbias;
-      p.out_zero = y.zero;
-      p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
-      p.table = h->head_table;
-      p.nb_codes = h->d_nb_codes;
-      p.nb_row_bytes = h->nb_row_bytes;
-      p.nb_frame = h->d_nb_frame;
-      p.nb_best = h->d_nb_best;
-      p.nb_count = h->d_nb_count;
-      p.mask8 = h->d_mask;
-      p.out_shift = y.shift;
-      p.frame_id = h->d_frame_id;
-      p.frame_prob = h->d_frame_prob;
-      p.logits = h->d_logits;
-      p.err = h->d_err;
-      const int grid = std::min(p.num_tiles, h->sms);
-      p.nb_region = (p.num_tiles + grid - 1) / grid * 128;
-      ProfScope prof(h, kProfHead, static_cast<int>(li));
-      if (h->int8 && l.fast) {
-        CK(cudaFuncSetAttribute(head_ctc_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-        head_ctc_kernel<true, true><<<grid, kHeadThreads, l.smem, s>>>(p);
-      } else if (h->int8) {
-        CK(cudaFuncSetAttribute(head_ctc_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-        head_ctc_kernel<true, false><<<grid, kHeadThreads, l.smem, s>>>(p);
-      } else {
-        CK(cudaFuncSetAttribute(head_ctc_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-        head_ctc_kernel<false, false><<<grid, kHeadThreads, l.smem, s>>>(p);
-      }
-      CK(cudaGetLastError());
-      if (h->int8) {  // the listed frames' class-order sums
-        ProfScope sums(h, kProfHead, static_cast<int>(li));
-        const int smem = kSumRows * 256 * static_cast<int>(sizeof(float));
-        CK(cudaFuncSetAttribute(ctc_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        ctc_sums_kernel<<<grid, kSumThreads, smem, s>>>(h->d_nb_codes, h->nb_row_bytes, h->d_nb_frame, h->d_nb_best,
-                                                        h->d_nb_count, p.nb_region, h->ctc_terms, l.cout, h->d_frame_prob);
-        CK(cudaGetLastError());
-      }
       continue;
     }
     if (l.kind == kKindDw) {
@@ -2205,8 +2225,9 @@ namespace {
 // Opens `h` as a layer-only device (no crop, no head): the blob's one dense convolution between
 // its input value (h_in rows) and output value, each input line bw columns wide, n of them laid
 // out as a run is; the layer set up exactly as in a recognizer (setup_layer, the same tensors).
-int open_layer(crec_handle* h, int device, int precision, const void* model, size_t model_bytes, int n, int h_in,
-               int bw, long long* cols_out) {
+// A bare handle for one layer of a blob on `device` (the sweeps): the device, its tensor-map
+// encoder, a stream, the blob read.
+int open_device(crec_handle* h, int device, int precision, const void* model, size_t model_bytes) {
   h->int8 = precision == CREC_INT8;
   h->eb = h->int8 ? 1 : 2;
   h->device = device;
@@ -2221,7 +2242,12 @@ int open_layer(crec_handle* h, int device, int precision, const void* model, siz
   if (!fn || q != cudaDriverEntryPointSuccess) return set_error(h, CREC_E_CUDA, "cuTensorMapEncodeTiled is not available");
   h->encode = reinterpret_cast<EncodeTiled>(fn);
   CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
-  int rc = read_model(h, static_cast<const uint8_t*>(model), model_bytes);
+  return read_model(h, static_cast<const uint8_t*>(model), model_bytes);
+}
+
+int open_layer(crec_handle* h, int device, int precision, const void* model, size_t model_bytes, int n, int h_in,
+               int bw, long long* cols_out) {
+  int rc = open_device(h, device, precision, model, model_bytes);
   if (rc) return rc;
   if (h->l.size() != 1 || h->l[0].kind != kKindConv || h->l[0].residual >= 0)
     return set_error(h, CREC_E_MODEL, "a blob of one dense convolution");
@@ -2259,7 +2285,118 @@ int open_layer(crec_handle* h, int device, int precision, const void* model, siz
   return CREC_OK;
 }
 
+// A handle for a blob of one 1x1 convolution run as the recognizer's head over `frames` frames of
+// one row: the frames at input columns [gap, gap + frames), every column the head computes
+// masked in (the mask's 8-column groups).
+int open_head(crec_handle* h, int device, int precision, const void* model, size_t model_bytes, int frames,
+              long long* cols_out) {
+  int rc = open_device(h, device, precision, model, model_bytes);
+  if (rc) return rc;
+  if (h->l.size() != 1 || h->l[0].kind != kKindConv || h->l[0].residual >= 0 || h->l[0].kh != 1 || h->l[0].kw != 1 ||
+      h->l[0].sh != 1 || h->l[0].sw != 1 || h->l[0].pl || h->l[0].pr || h->l[0].pt || h->l[0].pb)
+    return set_error(h, CREC_E_MODEL, "a blob of one 1x1 convolution");
+  const Layer head = h->l[0];
+  Value& x = h->v[head.in];
+  Value& y = h->v[head.out];
+  if ((x.c * h->eb) % 16) return set_error(h, CREC_E_MODEL, "a head input of whole 16-byte channel groups");
+  if (h->int8 && !y.u8) return set_error(h, CREC_E_MODEL, "the INT8 head's output must be quantized (Q/DQ)");
+  x.h = 1;
+  x.shift = 0;
+  x.phys = head.in;
+  x.real = true;
+  x.cp = x.c;
+  y.h = 1;
+  y.shift = 0;
+  y.phys = head.out;
+  y.real = false;
+  h->max_shift = 0;
+  h->head_shift = 0;
+  h->gap = 8;
+  Layer stub{};
+  stub.kind = kKindResize;
+  h->l = {stub, head};  // setup_layer's view: the last layer (the head), not the first (the stem)
+  const long long cols = round_up(static_cast<long long>(h->gap) + frames, 128LL);
+  h->max_cols = cols;
+  if ((rc = setup_layer(h, 1)) || (rc = alloc_values(h))) return rc;
+  const size_t ncols = static_cast<size_t>(cols);
+  if ((rc = dev_alloc(h, &h->d_mask, ncols / 8)) || (rc = dev_alloc(h, &h->d_err, 1)) ||
+      (rc = dev_alloc(h, &h->d_frame_id, ncols)) || (rc = dev_alloc(h, &h->d_frame_prob, ncols)) ||
+      (rc = dev_alloc(h, &h->d_logits, ncols * static_cast<size_t>(y.c))))
+    return rc;
+  if (h->int8) {
+    std::vector<float> tab(256);
+    for (int q = 0; q < 256; ++q) tab[q] = static_cast<float>(q - y.zero) * y.scale;
+    if ((rc = upload(h, &h->head_table, tab))) return rc;
+    CK(cudaMalloc(&h->ctc_terms, 256 * 256 * sizeof(float)));
+    ctc_terms_kernel<<<256, 256, 0, h->stream>>>(h->head_table, h->ctc_terms);
+    CK(cudaGetLastError());
+    h->nb_row_bytes = round16(y.c);
+    const size_t tiles = (ncols + 127) / 128, entries = (tiles + h->sms - 1) / h->sms * h->sms * 128;
+    if ((rc = dev_alloc(h, &h->d_nb_codes, entries * static_cast<size_t>(h->nb_row_bytes))) ||
+        (rc = dev_alloc(h, &h->d_nb_frame, entries)) || (rc = dev_alloc(h, &h->d_nb_best, entries)) ||
+        (rc = dev_alloc(h, &h->d_nb_count, 2 * static_cast<size_t>(h->sms))))
+      return rc;
+  }
+  std::vector<uint8_t> mask(ncols / 8, 0);
+  std::memset(mask.data() + h->gap / 8, 1, static_cast<size_t>((frames + 7) / 8));
+  CK(cudaMemcpy(h->d_mask, mask.data(), mask.size(), cudaMemcpyHostToDevice));
+  CK(cudaMemset(h->d_err, 0, sizeof(int)));
+  CK(cudaStreamSynchronize(h->stream));
+  *cols_out = cols;
+  return CREC_OK;
+}
+
 }  // namespace
+
+int crec_head_sweep(int device, int precision, const void* model, size_t model_bytes, int frames, const void* x,
+                    int32_t* ids, float* probs, float* logits, int repeat, double* ms) {
+  if (!model || !x || !ids || !probs || !ms || frames <= 0 || frames > (1 << 24) || repeat < 1 ||
+      (precision != CREC_INT8 && precision != CREC_FP16))
+    return CREC_E_INVALID;
+  std::unique_ptr<crec_handle, void (*)(crec_handle*)> hold(new crec_handle(), [](crec_handle* p) {
+    free_all(p);
+    delete p;
+  });
+  crec_handle* h = hold.get();
+  long long cols = 0;
+  int rc = open_head(h, device, precision, model, model_bytes, frames, &cols);
+  if (rc) return rc;
+  const Layer& l = h->l[1];
+  const Value& xv = h->v[l.in];
+  const int classes = h->v[l.out].c;
+  const size_t row = static_cast<size_t>(xv.cp) * h->eb;  // a frame's bytes
+  CK(cudaMemcpy(xv.base + static_cast<long long>(xv.ph) * xv.pitch + static_cast<long long>(h->gap) * row, x,
+                row * frames, cudaMemcpyHostToDevice));
+  float* keep = h->d_logits;
+  h->d_logits = nullptr;  // the timed launches write no logits
+  if ((rc = launch_head(h, 1, cols))) return rc;  // warm-up
+  CK(cudaStreamSynchronize(h->stream));
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventCreate(&e1));
+  CK(cudaEventRecord(e0, h->stream));
+  for (int r = 0; r < repeat && rc == CREC_OK; ++r) rc = launch_head(h, 1, cols);
+  CK(cudaEventRecord(e1, h->stream));
+  CK(cudaEventSynchronize(e1));
+  float t = 0.0f;
+  cudaEventElapsedTime(&t, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  h->d_logits = keep;
+  if (rc) return rc;
+  if (logits && (rc = launch_head(h, 1, cols))) return rc;  // once more, keeping the logits
+  CK(cudaStreamSynchronize(h->stream));
+  int err = 0;
+  CK(cudaMemcpy(&err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) return CREC_E_TIMEOUT;
+  *ms = static_cast<double>(t) / repeat;
+  CK(cudaMemcpy(ids, h->d_frame_id + h->gap, sizeof(int32_t) * frames, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(probs, h->d_frame_prob + h->gap, sizeof(float) * frames, cudaMemcpyDeviceToHost));
+  if (logits)
+    CK(cudaMemcpy(logits, h->d_logits + static_cast<size_t>(h->gap) * classes, sizeof(float) * frames * classes,
+                  cudaMemcpyDeviceToHost));
+  return CREC_OK;
+}
 
 int crec_conv_sweep(int device, int precision, const void* model, size_t model_bytes, int n, int h_in, int w,
                     const void* x, void* y, int repeat, double* ms) {

@@ -233,6 +233,20 @@ CREC_API int crec_debug_inject(crec_handle* h, int what);
 CREC_API int crec_conv_sweep(int device, int precision, const void* model, size_t model_bytes, int n, int h, int w,
                              const void* x, void* y, int repeat, double* ms);
 
+/* The head sweep (BASELINE.json config 4's head GEMM; the reference's GPU head is
+ * carbon::cuda::ctc_head_argmax, carbon/include/carbon/cuda.h, tested in
+ * tests/cpp/cuda_ctc_head_test.cpp): a blob's one 1x1 convolution, K channels to `classes`, run
+ * as this build's fused head (tcgen05 GEMM, each frame's argmax and, for a frame whose best class
+ * is not 0 -- the CTC blank --, its probability 1 / sum_c exp(logit_c - logit_best)) over `frames`
+ * frames x [frames][K] (uint8 codes for CREC_INT8, float16 for CREC_FP16).  ids[frames] get the
+ * first class of the highest logit, probs[frames] the probability (0 for blank frames); logits
+ * (optional, [frames][classes]) each frame's logits as the head computed them (INT8: the
+ * dequantized output codes).  K * element bytes must be a multiple of 16 and at most 1024.  *ms:
+ * the mean device time of the head's launches (with the INT8 probability sums) over `repeat`
+ * after one warm-up.  A measurement and parity hook. */
+CREC_API int crec_head_sweep(int device, int precision, const void* model, size_t model_bytes, int frames,
+                             const void* x, int32_t* ids, float* probs, float* logits, int repeat, double* ms);
+
 /* The CUDA stream (a cudaStream_t) the handle's work runs on, for device-side timing. */
 CREC_API void* crec_stream(crec_handle* h);
 
