@@ -26,7 +26,7 @@ _NAMES = {E_INVALID: "invalid argument", E_NOMEM: "out of memory", E_CUDA: "CUDA
 # every entry point include/carbon_rec.h declares
 EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec_set_pages", "crec_prefetch_pages",
            "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_ctc_greedy", "crec_ctc_greedy_noalloc", "crec_width_bucket", "crec_crop_region",
-           "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats",
+           "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats", "crec_candidates",
            "crec_profile", "crec_profile_layers", "crec_mma_peak", "crec_debug_inject", "crec_conv_sweep",
            "crec_head_sweep"]
 
@@ -113,6 +113,7 @@ def lib() -> C.CDLL:
         L.crec_debug_value.argtypes = [p, i, p, i64]
         L.crec_debug_logits.argtypes = [p, p, i64]
         L.crec_last_stats.argtypes = [p, C.POINTER(Stats)]
+        L.crec_candidates.argtypes = [p, p, i, i, p, p, p, p, p, i64]
         L.crec_profile.argtypes = [p, i, C.POINTER(ProfileEntry), i]
         L.crec_profile_layers.argtypes = [p, C.POINTER(ProfileEntry), i]
         L.crec_mma_peak.argtypes = [i, i, i, i, C.POINTER(C.c_double)]
@@ -435,6 +436,30 @@ class RecDevice:
             res.append(out[at:at + classes * k].reshape(classes, k))
             at += classes * k
         return res
+
+    def candidates(self, rows, topk: int, capacity: int | None = None) -> list:
+        """crec_candidates: the beam's candidates of lines `rows` of the last recognize call, a
+        (ids [t, k], logp [t, k], blank [t]) per row (carbon::FrameCandidates; k = topk clamped to
+        [0, min(16, classes - 1)])."""
+        rows = np.ascontiguousarray(rows, np.int32)
+        n = len(rows)
+        cap = capacity if capacity is not None else 4096 * max(n, 1)
+        frames = np.zeros(max(n, 1), np.int32)
+        kk = C.c_int32(0)
+        kmax = max(0, min(int(topk), 16))
+        ids = np.zeros(max(cap * kmax, 1), np.int32)
+        logp = np.zeros(max(cap * kmax, 1), np.float32)
+        blank = np.zeros(max(cap, 1), np.float32)
+        self._check(lib().crec_candidates(self._h, rows.ctypes.data, n, int(topk), C.byref(kk), frames.ctypes.data,
+                                          ids.ctypes.data, logp.ctypes.data, blank.ctypes.data, cap))
+        topk = kk.value
+        out, at = [], 0
+        for j in range(n):
+            t = int(frames[j])
+            out.append((ids[at * topk:(at + t) * topk].reshape(t, topk), logp[at * topk:(at + t) * topk].reshape(t, topk),
+                        blank[at:at + t]))
+            at += t
+        return out
 
     def value(self, index: int, nbytes: int, dtype=np.uint8) -> np.ndarray:
         out = np.zeros(nbytes, np.uint8)

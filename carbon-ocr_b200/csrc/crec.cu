@@ -71,7 +71,7 @@ struct Layer {
   int32_t* colsum = nullptr;
   float* scale = nullptr;
   float* dbias = nullptr;
-  int8_t* dw8 = nullptr;  // depthwise [taps][cp], stem [cout][taps]
+  int8_t* dw8 = nullptr;  // depthwise [taps][cp], stem [cout][taps], head [cout][input cp]
   float* dwf = nullptr;
   int32_t* hoff = nullptr;  // the INT8 epilogue's per-channel offsets (HeadParams::off, ConvParams::off, DwParams::off)
   uint32_t* dwt = nullptr;  // the INT8 row depthwise's tap-transposed weights (DwParams::wt)
@@ -252,6 +252,14 @@ struct crec_handle {
   bool inject_timeout = false, inject_sticky = false;
   // the last run
   int last_n = 0;
+  int last_a = 0;                          // the last run's first line in its call
+  std::vector<int> last_frame0, last_len;  // its lines' first frame columns and lengths (the beam's candidates)
+  // crec_candidates' buffers (grown on demand)
+  int32_t* d_cand_cols = nullptr;
+  int32_t* d_cand_ids = nullptr;
+  float* d_cand_vals = nullptr;
+  float* d_cand_fr = nullptr;  // [3][frames]: best, sum, the blank's logit
+  size_t cap_cand_frames = 0, cap_cand_cells = 0;
   long long last_cols = 0;
   std::vector<int> last_seg, last_bw;
 };
@@ -627,6 +635,18 @@ int setup_layer(crec_handle* h, size_t li) {
     l.cq = l.nt;
     l.n_tiles = l.chunks;
     const int ncls = l.chunks * l.nchunk;
+    // the weights [classes][x.cp], zeros past the real channels (the beam's candidates)
+    if (h->int8) {
+      std::vector<int8_t> w(static_cast<size_t>(l.cout) * x.cp, 0);
+      for (int c = 0; c < l.cout; ++c)
+        for (int j = 0; j < l.cin; ++j) w[static_cast<size_t>(c) * x.cp + j] = l.w8[static_cast<size_t>(c) * l.cin + j];
+      if ((rc = upload(h, &l.dw8, w))) return rc;
+    } else {
+      std::vector<float> w(static_cast<size_t>(l.cout) * x.cp, 0.0f);
+      for (int c = 0; c < l.cout; ++c)
+        for (int j = 0; j < l.cin; ++j) w[static_cast<size_t>(c) * x.cp + j] = half_round(l.wf[static_cast<size_t>(c) * l.cin + j]);
+      if ((rc = upload(h, &l.dwf, w))) return rc;
+    }
     if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, ncls))) return rc;
   } else {
     // row stacking: the number of output rows a tile computes that gets the most outputs from
@@ -1306,6 +1326,7 @@ int layout_run(crec_handle* h, const Source& src, const int* bw, int a, int b, s
 // max_columns columns, every run's copies and launches queued, one sync, the results packed.
 int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_lines* out) {
   out->total = 0;
+  h->last_n = 0;  // until this call's last run is queued: no candidates from an earlier call
   if (n == 0) return CREC_OK;
   struct Run {
     int a, b;
@@ -1418,6 +1439,9 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
   out->total = total;
   const Run& last = runs.back();
   h->last_n = last.b - last.a;
+  h->last_a = last.a;
+  h->last_frame0.assign(h->hs_frame0 + last.a, h->hs_frame0 + last.b);
+  h->last_len.assign(h->hs_length + last.a, h->hs_length + last.b);
   h->last_cols = last.cols;
   h->last_seg.resize(h->last_n);
   h->last_bw.resize(h->last_n);
@@ -1470,6 +1494,10 @@ void free_all(crec_handle* h) {
   cudaFree(h->d_crops);
   cudaFree(h->d_crops_in);
   cudaFree(h->d_claim);
+  cudaFree(h->d_cand_cols);
+  cudaFree(h->d_cand_ids);
+  cudaFree(h->d_cand_vals);
+  cudaFree(h->d_cand_fr);
   cudaFree(h->d_wide_idx);
   cudaFree(h->d_wide);
   cudaFreeHost(h->hs_wide);
@@ -2098,6 +2126,86 @@ int crec_debug_inject(crec_handle* h, int what) {
   if (what == CREC_INJECT_TIMEOUT) h->inject_timeout = true;
   else if (what == CREC_INJECT_STICKY) h->inject_sticky = true;
   else return set_error(h, CREC_E_INVALID, "debug_inject: what");
+  return CREC_OK;
+}
+
+int crec_candidates(crec_handle* h, const int32_t* rows, int n, int topk, int32_t* k_out, int32_t* frames, int32_t* ids,
+                    float* logp, float* blank, int64_t capacity) {
+  if (!h) return CREC_E_INVALID;
+  if (h->broken) return set_error(h, CREC_E_STICKY, "the GPU is broken for this process");
+  if (n < 0 || !k_out || (n > 0 && (!rows || !frames || !blank)) || (n > 0 && topk > 0 && (!ids || !logp)))
+    return set_error(h, CREC_E_INVALID, "candidates: arguments");
+  const Layer& head = h->l.back();
+  const Value& x = h->v[head.in];
+  const Value& xp = h->v[x.phys];
+  const int classes = h->v[head.out].c;
+  // as the reference's GPU device clamps it (carbon/src/cuda/pipeline_cuda.cpp:501)
+  topk = std::clamp(topk, 0, std::min(classes - 1, 16));
+  *k_out = topk;
+  std::vector<int32_t> cols;
+  for (int j = 0; j < n; ++j) {
+    const int r = rows[j] - h->last_a;
+    if (r < 0 || r >= h->last_n)
+      return set_error(h, CREC_E_RANGE, "candidates: line " + std::to_string(rows[j]) +
+                                            " is not in the last run of the last recognize call");
+    frames[j] = h->last_len[r];
+    for (int t = 0; t < h->last_len[r]; ++t) cols.push_back(h->last_frame0[r] + t);
+  }
+  const size_t total = cols.size();
+  if (static_cast<int64_t>(total) > capacity) return set_error(h, CREC_E_RANGE, "candidates: capacity too small");
+  if (total == 0) return CREC_OK;
+  CK(cudaSetDevice(h->device));
+  cudaStream_t s = h->stream;
+  const size_t cells = total * std::max(topk, 1);
+  size_t cap_f = h->cap_cand_frames, cap_f2 = 3 * cap_f, cap_c = h->cap_cand_cells, cap_c2 = cap_c;
+  int rc;
+  if ((rc = grow_device(h, &h->d_cand_cols, &cap_f, total)) || (rc = grow_device(h, &h->d_cand_fr, &cap_f2, 3 * total)) ||
+      (rc = grow_device(h, &h->d_cand_ids, &cap_c, cells)) || (rc = grow_device(h, &h->d_cand_vals, &cap_c2, cells)))
+    return rc;
+  h->cap_cand_frames = std::min(cap_f, cap_f2 / 3);
+  h->cap_cand_cells = std::min(cap_c, cap_c2);
+  CK(cudaMemcpyAsync(h->d_cand_cols, cols.data(), sizeof(int32_t) * total, cudaMemcpyHostToDevice, s));
+  CandParams p{};
+  p.x = xp.base + static_cast<long long>(xp.ph) * xp.pitch;
+  p.cp = x.cp;
+  p.k = x.cp;
+  p.classes = classes;
+  p.topk = topk;
+  p.w8 = head.dw8;
+  p.wf = head.dwf;
+  p.colsum = head.colsum;
+  p.scale = head.scale;
+  p.bias = head.dbias;
+  p.in_zero = x.zero;
+  p.out_zero = h->v[head.out].zero;
+  p.out_inv_scale = h->int8 ? 1.0f / h->v[head.out].scale : 1.0f;
+  p.table = h->head_table;
+  p.cols = h->d_cand_cols;
+  p.frames = static_cast<int>(total);
+  p.ids = h->d_cand_ids;
+  p.vals = h->d_cand_vals;
+  p.best = h->d_cand_fr;
+  p.sum = h->d_cand_fr + total;
+  p.blank = h->d_cand_fr + 2 * total;
+  const int smem = classes * 4 + static_cast<int>(round16(x.cp * h->eb));
+  auto* k = h->int8 ? candidates_kernel<true> : candidates_kernel<false>;
+  CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  k<<<static_cast<unsigned>(total), kCandThreads, smem, s>>>(p);
+  CK(cudaGetLastError());
+  std::vector<float> fr(3 * total), vals(cells);
+  if (topk > 0) {
+    CK(cudaMemcpyAsync(ids, h->d_cand_ids, sizeof(int32_t) * total * topk, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(vals.data(), h->d_cand_vals, sizeof(float) * total * topk, cudaMemcpyDeviceToHost, s));
+  }
+  CK(cudaMemcpyAsync(fr.data(), h->d_cand_fr, sizeof(float) * 3 * total, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  // carbon/src/cpu/kernels.cpp:658-664: each frame's offset best + ln(sum), in float with the C
+  // library's logf, as the CPU reference takes it
+  for (size_t f = 0; f < total; ++f) {
+    const float off = fr[f] + std::log(fr[total + f]);
+    for (int q = 0; q < topk; ++q) logp[f * topk + q] = vals[f * topk + q] - off;
+    blank[f] = fr[2 * total + f] - off;
+  }
   return CREC_OK;
 }
 

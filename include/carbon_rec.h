@@ -174,6 +174,22 @@ CREC_API int crec_width_bucket(int crop_width);
  * the crop's width. */
 CREC_API int crec_crop_region(const crec_box* box, const crec_crop_rule* rule, double* region, int* width);
 
+/* The beam's candidates (carbon::PipelineModels::candidates, carbon/include/carbon/pipeline.h:133-141;
+ * carbon::frame_candidates, carbon/include/carbon/beam.h:40-51) of lines rows[0..n) of the last
+ * recognize call (indices into its lines; each must lie in the call's last run -- a call of more
+ * lines or columns than a run holds keeps only its last run's head input; ask before the next
+ * call).  topk is clamped to [0, min(16, classes - 1)], as the reference's GPU device clamps it,
+ * and *k gets the value used.  frames[j] gets line j's frame count t_j (its length, as the call
+ * returned it), and the lines' frames are packed in row order, line j's from the sum of the earlier
+ * t's: for each frame its k likeliest classes but the blank, best first (ties to the lower id),
+ * ids[f * k + q] and their log-probabilities logp[f * k + q], and the blank's, blank[f]; each the
+ * logit less the frame's best and ln of the class-order sum of exp(logit - best), as the CPU
+ * reference's ctc_topk computes them (the INT8 logits are the run's own codes, made again on the
+ * GPU from the head's input; FP16 logits within about 1e-3 of the fused head's).  capacity: the
+ * frames the arrays hold (ids and logp capacity * k entries). */
+CREC_API int crec_candidates(crec_handle* h, const int32_t* rows, int n, int topk, int32_t* k, int32_t* frames,
+                             int32_t* ids, float* logp, float* blank, int64_t capacity);
+
 /* What the last call did: device runs, kernel launches, bytes copied host -> device and back
  * (for crec_set_pages, the upload of the pages it took, whether it made that upload itself or a
  * crec_prefetch_pages made it); and the bytes copied each way since the handle was opened (every

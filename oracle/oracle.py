@@ -37,6 +37,9 @@ def build(force: bool = False) -> None:
                                "-fvisibility=hidden", str(src), "-o", str(ORC_SO), "-lm"])
     if (REFERENCE_ROOT / "carbon" / "src" / "lines.cpp").exists():
         subprocess.check_call(["make", "-s", "-f", "ref.mk", f"REF={REFERENCE_ROOT}", "-j8"], cwd=HERE)
+        if (HERE.parent / "carbon-ocr_b200" / "carbon_rec" / "libcarbon_rec.so").exists():
+            # INTEGRATION.md's adapter behind the reference's PipelineModels (tests/adapter_run.cpp)
+            subprocess.check_call(["make", "-s", "-f", "ref.mk", f"REF={REFERENCE_ROOT}", "adapter"], cwd=HERE)
 
 
 class CropRule(C.Structure):
@@ -57,6 +60,19 @@ def _ptr(a: np.ndarray):
 
 class _Common:
     lib: C.CDLL
+
+    def ctc_topk(self, logits: np.ndarray, t_n: int, k: int):
+        """One line's logits [classes, frames] -> the beam's candidates of its first t_n frames:
+        (ids [t_n, k], logp [t_n, k], blank [t_n]) (carbon::frame_candidates)."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        classes, frames = logits.shape
+        ids = np.zeros((t_n, k), np.int32)
+        logp = np.zeros((t_n, k), np.float32)
+        blank = np.zeros(t_n, np.float32)
+        r = self._ctc_topk(_ptr(logits), classes, frames, t_n, k, _ptr(ids), _ptr(logp), _ptr(blank))
+        if r not in (None, 0):
+            raise ValueError(f"ctc_topk failed ({r})")
+        return ids, logp, blank
 
     def crop_lines(self, page: np.ndarray, boxes: np.ndarray, out_width: int, rule: CropRule | None = None):
         """boxes [n, 4] (x0, y0, x1, y1) on page [h, w] uint8 -> (crops [n, 32, out_width], widths [n])."""
@@ -99,9 +115,12 @@ class Oracle(_Common):
         L.orc_exp_neg.restype = C.c_float
         L.orc_ctc_greedy.argtypes = [_p, _i, _i, _i, _p, _i, _p, _p, _p, _p, _p, _p]
         L.orc_ctc_greedy.restype = None
+        L.orc_ctc_topk.argtypes = [_p, _i, _i, _i, _i, _p, _p, _p]
+        L.orc_ctc_topk.restype = None
         L.orc_ctc_collapse.argtypes = [_p, _p, _i, _i, _p, _i, _p, _p, _p, _p]
         L.orc_ctc_collapse.restype = None
         self._crop_lines = L.orc_crop_lines
+        self._ctc_topk = L.orc_ctc_topk
 
     def crop_region(self, box, rule: CropRule | None = None):
         rule = rule or CropRule.default()
@@ -236,7 +255,10 @@ class Reference(_Common):
         L.ref_bench_pages.argtypes = [C.c_char_p, C.c_char_p, _i, _i, _i, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _i,
                                       C.POINTER(C.c_int64)]
         L.ref_bench_pages.restype = _d
+        L.ref_ctc_topk.argtypes = [_p, _i, _i, _i, _i, _p, _p, _p]
+        L.ref_ctc_topk.restype = _i
         self._crop_lines = L.ref_crop_lines
+        self._ctc_topk = L.ref_ctc_topk
 
     def error(self) -> str:
         return self.lib.ref_last_error().decode()

@@ -669,3 +669,41 @@ ORC_API void orc_ctc_greedy(const float* logits, int n, int classes, int frames,
   free(arg);
   free(prob);
 }
+
+/* carbon/src/cpu/kernels.cpp:617-665 (ctc_topk, the scalar reference; carbon::frame_candidates,
+ * carbon/src/beam.cpp:301-310): of one line's logits [classes][frames], its first t_n frames:
+ * each frame's best logit, the class-order sum of exp_neg(l_c - best), its k likeliest classes
+ * but the blank by insertion in class order (a later class must beat a kept one, so ties keep
+ * the lower id), ids[t * k + j]; logp[t * k + j] and blank[t] each the logit less best + logf(sum)
+ * (the C library's logf, as std::log(float) is). */
+ORC_API void orc_ctc_topk(const float* logits, int classes, int frames, int t_n, int k, int32_t* ids, float* logp,
+                          float* blank) {
+  for (int t = 0; t < t_n; ++t) {
+    float best = -INFINITY, sum = 0.0f;
+    for (int c = 0; c < classes; ++c) {
+      const float v = logits[(size_t)c * frames + t];
+      best = v > best ? v : best;
+    }
+    for (int c = 0; c < classes; ++c) sum = sum + orc_exp_neg(logits[(size_t)c * frames + t] - best);
+    float* lt = logp + (size_t)t * k;
+    int32_t* it = ids + (size_t)t * k;
+    for (int j = 0; j < k; ++j) {
+      lt[j] = -INFINITY;
+      it[j] = 0;
+    }
+    for (int c = 1; c < classes && k > 0; ++c) {
+      const float v = logits[(size_t)c * frames + t];
+      if (!(v > lt[k - 1])) continue;
+      int j = k - 1;
+      for (; j > 0 && lt[j - 1] < v; --j) {
+        lt[j] = lt[j - 1];
+        it[j] = it[j - 1];
+      }
+      lt[j] = v;
+      it[j] = c;
+    }
+    const float off = best + logf(sum);
+    for (int j = 0; j < k; ++j) lt[j] = lt[j] - off;
+    blank[t] = logits[t] - off;
+  }
+}

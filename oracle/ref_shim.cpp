@@ -135,6 +135,16 @@ int ref_light_on_dark(const uint8_t* crop, int w, int h, int64_t stride, int mar
 
 float ref_exp_neg(float x) { return carbon::cpu::detail::exp_neg(x); }
 
+// cpu::ctc_topk (what carbon::frame_candidates calls) on one line's logits [classes][frames].
+int ref_ctc_topk(const float* logits, int classes, int frames, int t_n, int k, int32_t* ids, float* logp, float* blank) {
+  try {
+    carbon::cpu::ctc_topk(logits, classes, frames, t_n, k, ids, logp, blank);
+    return 0;
+  } catch (const std::exception& e) {
+    return fail(e);
+  }
+}
+
 // ctc_greedy: per line its count, and up to `cap` ids, frames and probs at line i * cap.
 int ref_ctc_greedy(const float* logits, int n, int classes, int frames, const int32_t* lengths, int cap,
                    int32_t* counts, int32_t* ids, int32_t* frame_of, float* probs) {

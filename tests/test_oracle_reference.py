@@ -69,6 +69,23 @@ def test_ctc_greedy_matches_reference(orc, ref):
                     assert np.array_equal(c.view(np.int32), z.view(np.int32))
 
 
+def test_ctc_topk_matches_reference(orc, ref):
+    """The beam's candidates (cpu::ctc_topk, carbon::frame_candidates): tie-heavy integer grids and
+    float logits, k from 0 to classes - 1, lines cut short of their frames."""
+    rng = np.random.default_rng(29)
+    for classes, frames in ((2, 5), (7, 40), (33, 17), (800, 72)):
+        for grid in (True, False):
+            l = (rng.integers(-12, 13, (classes, frames)) * 0.25 if grid else rng.normal(0, 3, (classes, frames)))
+            l = l.astype(np.float32)
+            for k in sorted({0, 1, min(5, classes - 1), min(16, classes - 1), classes - 1}):
+                t_n = frames - frames // 4
+                a = orc.ctc_topk(l, t_n, k)
+                b = ref.ctc_topk(l, t_n, k)
+                assert np.array_equal(a[0], b[0]), (classes, k)
+                assert np.array_equal(a[1].view(np.int32), b[1].view(np.int32)), (classes, k)
+                assert np.array_equal(a[2].view(np.int32), b[2].view(np.int32)), (classes, k)
+
+
 @pytest.mark.parametrize("tag", ["int8", "fp32"])
 def test_rec_latin_matches_reference(orc, ref, rec_latin, tmp_path, tag):
     n8, n32, i8, fp = rec_latin
