@@ -513,16 +513,20 @@ std::vector<uint8_t> band_weight_image(const crec_handle* h, const Layer& l, int
 }
 
 // The INT8 epilogue's per-channel offsets (n of them) and whether its conversions may skip the
-// conversion unit: |acc - zero * colsum| <= max(zero, 255 - zero) * sum |w| over a channel's
-// weights; below 2^22 the kernel converts exactly with kMagic.
+// conversion unit: a channel's sum(k) (a_k - zero) w_k over inputs a_k in [0, 255] lies in
+// [-(zero P + (255 - zero) N), (255 - zero) P + zero N], P and N the sums of its positive weights
+// and of its negative weights' magnitudes (both ends reached); below 2^22 in magnitude for every
+// channel, the kernel converts exactly with kMagic.
 int upload_offsets(crec_handle* h, Layer& l, int zero, const std::vector<int32_t>& colsum, int n) {
-  const long long reach = std::max(zero, 255 - zero);
   const size_t per = l.w8.size() / static_cast<size_t>(l.cout);
   long long worst = 0;
   for (int j = 0; j < l.cout; ++j) {
-    long long a = 0;
-    for (size_t k = 0; k < per; ++k) a += std::abs(static_cast<int>(l.w8[j * per + k]));
-    worst = std::max(worst, a * reach);
+    long long pos = 0, neg = 0;
+    for (size_t k = 0; k < per; ++k) {
+      const int w = l.w8[j * per + k];
+      (w > 0 ? pos : neg) += std::abs(w);
+    }
+    worst = std::max({worst, (255 - zero) * pos + zero * neg, zero * pos + (255 - zero) * neg});
   }
   l.fast = worst < (1LL << 22);
   std::vector<int32_t> off(n, 0);
