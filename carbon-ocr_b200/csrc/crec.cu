@@ -1040,7 +1040,7 @@ int launch_head(crec_handle* h, size_t li, long long cols) {
   CK(cudaGetLastError());
   if (h->int8) {  // the listed frames' class-order sums
     ProfScope sums(h, kProfHead, static_cast<int>(li));
-    const int smem = kSumRows * 256 * static_cast<int>(sizeof(float));
+    const int smem = kSumRows * kSumPitch * static_cast<int>(sizeof(float));
     CK(cudaFuncSetAttribute(ctc_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     ctc_sums_kernel<<<grid, kSumThreads, smem, s>>>(h->d_nb_codes, h->nb_row_bytes, h->d_nb_frame, h->d_nb_best,
                                                     h->d_nb_count, p.nb_region, h->ctc_terms, l.cout, h->d_frame_prob);

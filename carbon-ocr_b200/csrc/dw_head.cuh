@@ -752,8 +752,11 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
 // terms[best][q_c]) (carbon/src/cpu/kernels.cpp:799-828), a thread a frame.  The terms rows of
 // the best codes a run lists (codes from the least listed one up, at most kSumRows rows) are
 // staged in shared memory, so the chain of dependent adds reads its terms there; a frame whose
-// best code is below them reads its row from global memory.
+// best code is below them reads its row from global memory.  The staged rows are kSumPitch floats
+// apart, one more than a row: the warp's frames look up the same class at once, and their codes
+// for it cluster, so with a pitch of 256 the lookups of different rows would fall in one bank.
 constexpr int kSumRows = 192;
+constexpr int kSumPitch = 257;
 constexpr int kSumThreads = 512;
 
 template <bool kShared>
@@ -787,18 +790,25 @@ __global__ void __launch_bounds__(kSumThreads) ctc_sums_kernel(const uint8_t* nb
                                                                const int32_t* nb_frame, const int32_t* nb_best,
                                                                const int* nb_count, int nb_region, const float* terms,
                                                                int classes, float* frame_prob) {
-  extern __shared__ __align__(16) float srows[];  // [rows][256]: terms rows lo .. 255
+  extern __shared__ __align__(16) float srows[];  // [rows][kSumPitch]: terms rows lo .. 255
   const int count = nb_count[2 * blockIdx.x];
   if (count == 0) return;
   const int lo = max(255 - nb_count[2 * blockIdx.x + 1], 256 - kSumRows);
   const long long first = static_cast<long long>(blockIdx.x) * nb_region;
   const float4* src = reinterpret_cast<const float4*>(terms + static_cast<size_t>(lo) * 256);
-  for (int i = threadIdx.x; i < (256 - lo) * 64; i += blockDim.x) reinterpret_cast<float4*>(srows)[i] = __ldg(src + i);
+  for (int i = threadIdx.x; i < (256 - lo) * 64; i += blockDim.x) {
+    const float4 v = __ldg(src + i);
+    float* d = srows + (i >> 6) * kSumPitch + (i & 63) * 4;
+    d[0] = v.x;
+    d[1] = v.y;
+    d[2] = v.z;
+    d[3] = v.w;
+  }
   __syncthreads();
   for (long long k = first + threadIdx.x; k < first + count; k += blockDim.x) {
     const int b = nb_best[k];
     const uint8_t* row = nb_codes + k * row_bytes;
-    const float sum = b >= lo ? class_sum<true>(row, classes, srows + (b - lo) * 256)
+    const float sum = b >= lo ? class_sum<true>(row, classes, srows + (b - lo) * kSumPitch)
                               : class_sum<false>(row, classes, terms + static_cast<size_t>(b) * 256);
     frame_prob[nb_frame[k]] = __fdiv_rn(1.0f, sum);
   }
