@@ -28,7 +28,7 @@ EXPORTS = ["crec_open", "crec_close", "crec_last_error", "crec_is_broken", "crec
            "crec_set_pages_device", "crec_recognize", "crec_recognize_lines", "crec_recognize_crops", "crec_ctc_greedy", "crec_ctc_greedy_noalloc", "crec_width_bucket", "crec_crop_region",
            "crec_stream", "crec_debug_crops", "crec_debug_value", "crec_debug_logits", "crec_last_stats", "crec_candidates",
            "crec_profile", "crec_profile_layers", "crec_mma_peak", "crec_debug_inject", "crec_conv_sweep",
-           "crec_head_sweep"]
+           "crec_head_sweep", "crec_ctc_head_blob"]
 
 
 class CrecError(RuntimeError):
@@ -120,6 +120,7 @@ def lib() -> C.CDLL:
         L.crec_debug_inject.argtypes = [p, i]
         L.crec_conv_sweep.argtypes = [i, i, p, C.c_size_t, i, i, i, p, p, i, C.POINTER(C.c_double)]
         L.crec_head_sweep.argtypes = [i, i, p, C.c_size_t, i, p, p, p, p, i, C.POINTER(C.c_double)]
+        L.crec_ctc_head_blob.argtypes = [p, C.c_size_t, p, C.c_size_t, C.POINTER(C.c_size_t), C.c_char_p, C.c_size_t]
         _lib = L
     return _lib
 
@@ -193,6 +194,22 @@ def head_sweep(blob: bytes, precision: int, x: np.ndarray, classes: int, repeat:
     if rc != OK:
         raise CrecError(rc, "crec_head_sweep")
     return ids, probs, lg, ms.value
+
+
+def ctc_head_blob(file_bytes: bytes) -> bytes:
+    """crec_ctc_head_blob: a CTCHEAD1 file's bytes (<model>.head.bin) -> the FP16 blob of its head;
+    raises CrecError(E_MODEL) with the reason for a file that is not a head."""
+    f = C.create_string_buffer(bytes(file_bytes), len(file_bytes))
+    n = C.c_size_t(0)
+    err = C.create_string_buffer(256)
+    rc = lib().crec_ctc_head_blob(C.cast(f, C.c_void_p), len(file_bytes), None, 0, C.byref(n), err, 256)
+    if rc == E_RANGE:
+        out = C.create_string_buffer(n.value)
+        rc = lib().crec_ctc_head_blob(C.cast(f, C.c_void_p), len(file_bytes), C.cast(out, C.c_void_p), n.value,
+                                      C.byref(n), err, 256)
+        if rc == OK:
+            return out.raw[:n.value]
+    raise CrecError(rc, err.value.decode() or "crec_ctc_head_blob")
 
 
 def width_bucket(crop_width: int) -> int:

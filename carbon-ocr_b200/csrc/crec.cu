@@ -631,7 +631,7 @@ int setup_layer(crec_handle* h, size_t li) {
     for (l.nchunk = std::min(kHeadChunk, round16(l.cout));; l.nchunk -= 16) {
       l.chunks = (l.cout + l.nchunk - 1) / l.nchunk;
       l.b_bytes = static_cast<uint32_t>(l.nkb) * l.nchunk * 128;
-      l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + head_tail_bytes(l.chunks * l.nchunk);
+      l.smem = 1024 + l.a_bytes + 2 * l.b_bytes + codes + head_tail_bytes(l.chunks * l.nchunk, h->int8);
       if (l.smem + 1024 <= 232448) break;
       if (l.nchunk == 16) return set_error(h, CREC_E_MODEL, "the head does not fit in shared memory");
     }
@@ -652,6 +652,7 @@ int setup_layer(crec_handle* h, size_t li) {
       if ((rc = upload(h, &l.dwf, w))) return rc;
     }
     if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, ncls))) return rc;
+    if (h->int8) l.sat = round_first(h, l, x, y, scale, bias);
   } else {
     // row stacking: the number of output rows a tile computes that gets the most outputs from
     // an MMA (N up to 256; the rows divide the output's height; no residual), where that is at
@@ -1024,19 +1025,21 @@ int launch_head(crec_handle* h, size_t li, long long cols) {
   p.frame_prob = h->d_frame_prob;
   p.logits = h->d_logits;
   p.err = h->d_err;
+  p.sat = l.sat ? 1 : 0;
   const int grid = std::min(p.num_tiles, h->sms);
   p.nb_region = (p.num_tiles + grid - 1) / grid * 128;
   ProfScope prof(h, kProfHead, static_cast<int>(li));
-  if (h->int8 && l.fast) {
-    CK(cudaFuncSetAttribute(head_ctc_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-    head_ctc_kernel<true, true><<<grid, kHeadThreads, l.smem, s>>>(p);
-  } else if (h->int8) {
-    CK(cudaFuncSetAttribute(head_ctc_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-    head_ctc_kernel<true, false><<<grid, kHeadThreads, l.smem, s>>>(p);
-  } else {
-    CK(cudaFuncSetAttribute(head_ctc_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
-    head_ctc_kernel<false, false><<<grid, kHeadThreads, l.smem, s>>>(p);
-  }
+  auto launch = [&](auto* k) -> int {
+    CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem));
+    k<<<grid, kHeadThreads, l.smem, s>>>(p);
+    return CREC_OK;
+  };
+  const int lrc = !h->int8            ? launch(head_ctc_kernel<false, false, false>)
+                  : l.fast && l.sat   ? launch(head_ctc_kernel<true, true, true>)
+                  : l.fast            ? launch(head_ctc_kernel<true, true, false>)
+                  : l.sat             ? launch(head_ctc_kernel<true, false, true>)
+                                      : launch(head_ctc_kernel<true, false, false>);
+  if (lrc) return lrc;
   CK(cudaGetLastError());
   if (h->int8) {  // the listed frames' class-order sums
     ProfScope sums(h, kProfHead, static_cast<int>(li));
@@ -2459,6 +2462,60 @@ int open_head(crec_handle* h, int device, int precision, const void* model, size
 }
 
 }  // namespace
+
+int crec_ctc_head_blob(const void* file, size_t bytes, void* blob, size_t capacity, size_t* blob_bytes, char* error,
+                       size_t error_size) {
+  auto fail = [&](const std::string& m) {
+    if (error && error_size) std::snprintf(error, error_size, "%s", m.c_str());
+    return CREC_E_MODEL;
+  };
+  if (!file || !blob_bytes) return CREC_E_INVALID;
+  // carbon/src/lines.cpp:372-398 (load_ctc_head): "CTCHEAD1", int32 classes, int32 k, the weight
+  // [classes][k] in float16, the bias [classes] in float32, little-endian, nothing after
+  const uint8_t* b = static_cast<const uint8_t*>(file);
+  constexpr size_t kHeader = 16;
+  if (bytes < kHeader || std::memcmp(b, "CTCHEAD1", 8) != 0)
+    return fail("not a CTC head (the export writes <model>.head.bin)");
+  int32_t dims[2];
+  std::memcpy(dims, b + 8, sizeof dims);
+  const int classes = dims[0], k = dims[1];
+  const size_t cells = static_cast<size_t>(std::max(classes, 0)) * static_cast<size_t>(std::max(k, 0));
+  const size_t want = kHeader + cells * 2 + static_cast<size_t>(std::max(classes, 0)) * 4;
+  if (classes <= 0 || k <= 0 || bytes != want)
+    return fail("a head of " + std::to_string(classes) + " classes by " + std::to_string(k) + " takes " +
+                std::to_string(want) + " bytes, the file has " + std::to_string(bytes));
+  // a CRECMDL1 float blob of the one 1x1 convolution, k channels to `classes` (as netdef writes it)
+  const size_t need = 8 + 8 * 4 + 2 * 24 + 20 * 4 + cells * 4 + static_cast<size_t>(classes) * 4;
+  *blob_bytes = need;
+  if (!blob || capacity < need) return CREC_E_RANGE;
+  uint8_t* o = static_cast<uint8_t*>(blob);
+  auto put = [&](const void* v, size_t n) {
+    std::memcpy(o, v, n);
+    o += n;
+  };
+  auto u32 = [&](uint32_t v) { put(&v, 4); };
+  put("CRECMDL1", 8);
+  for (uint32_t v : {1u, 1u, 2u, 1u, 0u, 1u, 1u, 0u}) u32(v);  // version, float, values, layers, in, out, height
+  for (int c : {k, classes}) {  // c, u8, scale, zero, border rows, border columns
+    u32(static_cast<uint32_t>(c));
+    u32(0);
+    const float one = 1.0f;
+    put(&one, 4);
+    u32(0);
+    u32(0);
+    u32(0);
+  }
+  const int32_t fields[20] = {kKindConv, 0, 1, -1, 1, 1, 1, 1, 0, 0, 0, 0, k, classes, 0, 1, 1, 1, 0, 0};
+  put(fields, sizeof fields);
+  for (size_t i = 0; i < cells; ++i) {
+    __half_raw r;
+    std::memcpy(&r.x, b + kHeader + 2 * i, 2);
+    const float w = __half2float(__half(r));
+    put(&w, 4);
+  }
+  put(b + kHeader + cells * 2, static_cast<size_t>(classes) * 4);
+  return CREC_OK;
+}
 
 int crec_head_sweep(int device, int precision, const void* model, size_t model_bytes, int frames, const void* x,
                     int32_t* ids, float* probs, float* logits, int repeat, double* ms) {

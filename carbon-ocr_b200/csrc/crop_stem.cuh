@@ -342,28 +342,31 @@ __device__ __forceinline__ void hpass(const PageDesc& P, const int32_t* c, int32
   }
 }
 
-// Vertical pass of one output column: output rows first, first + step, ... < H, row yy's window
-// at col[vfirst[yy] - top ..), its weight planes at vkp[yy * 24 ..] (k0 | k1 | k2, 8 words
-// each); every window at most 4 * NW taps, and the word reads inside the column's slot.
+// Vertical pass of a strip, a thread an output row and every tpr-th column of the strip from c0
+// (tpr threads a row): the row's weight planes stay in registers across its columns.  Column xx's
+// intermediate is at tmp + xx * rp; row yy's window at vfirst[yy] - top; the output pixel (yy, xx)
+// at out0[yy * qpitch + xx]; every window at most 4 * NW taps, its word reads inside the column's slot.
 template <int NW>
-__device__ __forceinline__ void vpass(const uint8_t* col, const int32_t* vfirst, const uint32_t* vkp, int top, int H,
-                                      int first, int step, uint8_t* out, int qpitch) {
-  for (int yy = first; yy < H; yy += step) {
-    const int f = vfirst[yy] - top;
-    const uint32_t* wp = reinterpret_cast<const uint32_t*>(col + (f & ~3));
-    const uint32_t sel = 0x3210u + static_cast<uint32_t>(f & 3) * 0x1111u;
-    uint32_t w[NW + 1], k0[NW], k1[NW], k2[NW];
+__device__ __forceinline__ void vpass_rows(const uint8_t* tmp, int rp, const int32_t* vfirst, const uint32_t* vkp,
+                                           int top, int yy, int c0, int tpr, int sc, uint8_t* out0, int qpitch) {
+  uint32_t k0[NW], k1[NW], k2[NW];
+  const uint32_t* k = vkp + yy * 24;
+#pragma unroll
+  for (int j = 0; j < NW; ++j) {
+    k0[j] = k[j];
+    k1[j] = k[8 + j];
+    k2[j] = k[16 + j];
+  }
+  const int f = vfirst[yy] - top;
+  const uint32_t sel = 0x3210u + static_cast<uint32_t>(f & 3) * 0x1111u;
+  uint8_t* out = out0 + yy * qpitch;
+  for (int xx = c0; xx < sc; xx += tpr) {
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(tmp + xx * rp + (f & ~3));
+    uint32_t w[NW + 1];
 #pragma unroll
     for (int j = 0; j <= NW; ++j) w[j] = wp[j];
-    const uint32_t* k = vkp + yy * 24;
-#pragma unroll
-    for (int j = 0; j < NW; ++j) {
-      k0[j] = k[j];
-      k1[j] = k[8 + j];
-      k2[j] = k[16 + j];
-    }
     const int32_t v = window_sum<NW>(w, sel, k0, k1, k2) >> 22;
-    out[yy * qpitch] = static_cast<uint8_t>(v < 0 ? 0 : v > 255 ? 255 : v);
+    out[xx] = static_cast<uint8_t>(v < 0 ? 0 : v > 255 ? 255 : v);
   }
 }
 
@@ -602,14 +605,14 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
         }
       }
       __syncthreads();
-      if (rg < groups) {
-        // vertical pass: the strip's output pixels
-        const uint8_t* col = tmp + xx * rp;
-        uint8_t* out = &px(0, x0 + xx);
-        if (!vbad) {
+      if (!vbad) {
+        // vertical pass: the strip's output pixels, a thread a row and every tpr-th column
+        const int tpr = nthr / H, yy = tid / tpr, c0 = tid - yy * tpr;
+        if (yy < H) {
+          uint8_t* out0 = &px(0, x0);
 #define CREC_VPASS(NW) \
   case NW:             \
-    vpass<NW>(col, vfirst, vkp, top, H, rg, groups, out, qpitch); \
+    vpass_rows<NW>(tmp, rp, vfirst, vkp, top, yy, c0, tpr, sc, out0, qpitch); \
     break;
           switch (nwv) {
             CREC_VPASS(1)
@@ -622,14 +625,16 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
             CREC_VPASS(8)
           }
 #undef CREC_VPASS
-        } else {
-          for (int yy = rg; yy < H; yy += groups) {
-            const int f = vfirst[yy] - top, n = vcount[yy];
-            const int32_t* k = vk + yy * kMaxTaps;
-            int32_t ss = 1 << 21;
-            for (int t = 0; t < n; ++t) ss += col[f + t] * k[t];
-            out[yy * qpitch] = clip8d(ss);
-          }
+        }
+      } else if (rg < groups) {
+        const uint8_t* col = tmp + xx * rp;
+        uint8_t* out = &px(0, x0 + xx);
+        for (int yy = rg; yy < H; yy += groups) {
+          const int f = vfirst[yy] - top, n = vcount[yy];
+          const int32_t* k = vk + yy * kMaxTaps;
+          int32_t ss = 1 << 21;
+          for (int t = 0; t < n; ++t) ss += col[f + t] * k[t];
+          out[yy * qpitch] = clip8d(ss);
         }
       }
     }
@@ -655,14 +660,25 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
     __syncthreads();
     if (p.flip_margin > 0) {
       const int g = red[0], lo = g - p.flip_margin, hi = g + p.flip_margin;
+      // four pixels a word (crop widths are multiples of 8, the crop starts at column 4 of qb):
+      // byte-wise compares, their 0xff bytes counted by popc (8 bits a pixel); an item is a
+      // (row, word), the quotient a multiply-high as in the final pass below
       int below = 0, above = 0, dark = 0;
-      for (int x = tid; x < cw; x += nthr)
-        for (int y = 0; y < H; ++y) {
-          const int v = px(y, x);
-          below += v <= lo;
-          above += v >= hi;
-          dark += v <= 127;
-        }
+      const int nw = cw >> 2;
+      const uint32_t inv = static_cast<uint32_t>(0xffffffffu / static_cast<uint32_t>(nw)) + 1u;
+      const uint32_t lo4 = static_cast<uint32_t>(lo < 0 ? 0 : lo) * 0x01010101u;
+      const uint32_t hi4 = static_cast<uint32_t>(hi > 255 ? 255 : hi) * 0x01010101u;
+      const bool any_lo = lo >= 0, any_hi = hi <= 255;
+      for (int i = tid; i < H * nw; i += nthr) {
+        const int y = static_cast<int>(__umulhi(static_cast<uint32_t>(i), inv)), w4 = i - y * nw;
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(&px(y, 4 * w4));
+        if (any_lo) below += __popc(__vcmpleu4(w, lo4));
+        if (any_hi) above += __popc(__vcmpgeu4(w, hi4));
+        dark += __popc(__vcmpleu4(w, 0x7f7f7f7fu));
+      }
+      below >>= 3;
+      above >>= 3;
+      dark >>= 3;
       for (int o = 16; o > 0; o >>= 1) {
         below += __shfl_xor_sync(0xffffffffu, below, o);
         above += __shfl_xor_sync(0xffffffffu, above, o);

@@ -324,6 +324,8 @@ struct HeadParams {
   const float* bias;
   int out_zero;
   float out_inv_scale;
+  int sat;             // INT8: |v * inv_scale| < 2^21 for every frame (the host's bound), so a code may be
+                       // rounded first and clamped by the saturating byte pack
   const float* table;  // INT8 [256]: the u8 logits' values
   uint8_t* nb_codes;   // INT8: the run's non-blank frames' class codes, row k at k * nb_row_bytes
   int nb_row_bytes;    // classes rounded up to 16
@@ -349,9 +351,12 @@ __host__ __device__ constexpr int head_code_stride(int classes) {
   return ((classes + 15) / 16 | 1) * 16;
 }
 
-// Bytes of the head's shared memory after A, B and the codes: barriers, per-class constants,
-// the per-frame merge slots and the list of non-blank frames.
-__host__ __device__ constexpr int head_tail_bytes(int ncls) { return 128 + 12 * ncls + (3 * 512 + 3 * 128 + 4) * 4; }
+// Bytes of the head's shared memory after A, B and the codes: barriers, per-class constants (INT8
+// offset, scale and bias; FP16 the bias alone), the per-frame merge slots and the list of
+// non-blank frames.
+__host__ __device__ constexpr int head_tail_bytes(int ncls, bool int8) {
+  return 128 + (int8 ? 12 : 4) * ncls + (3 * 512 + 3 * 128 + 4) * 4;
+}
 
 // carbon/src/cpu/kernels.h:216-250 (exp_neg), each multiply and add rounded on its own.
 __device__ __forceinline__ float exp_neg_d(float x) {
@@ -384,7 +389,7 @@ __device__ __forceinline__ uint32_t first_byte_eq(uint32_t w, uint32_t m4) {
   return (v - 0x01010101u) & ~v & 0x80808080u;
 }
 
-template <bool kInt8, bool kFast>
+template <bool kInt8, bool kFast, bool kSat>
 __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_constant__ HeadParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -400,10 +405,10 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
   uint64_t* t_full = bars + 6;    // [4] TMEM buffers: 0, 1 the even chunks', 2, 3 the odd chunks'
   uint64_t* t_empty = bars + 10;  // [4]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
-  const int ncls = p.chunks * p.nchunk;
-  int32_t* s_off = reinterpret_cast<int32_t*>(bars + 16);  // [ncls] per-class constants
-  float* s_scale = reinterpret_cast<float*>(s_off + ncls);
-  float* s_bias = s_scale + ncls;
+  const int ncls = p.chunks * p.nchunk, nconst = kInt8 ? ncls : 0;
+  int32_t* s_off = reinterpret_cast<int32_t*>(bars + 16);  // INT8 [ncls] per-class constants
+  float* s_scale = reinterpret_cast<float*>(s_off + nconst);
+  float* s_bias = s_scale + nconst;                         // [ncls]
   int32_t* s_hmax = reinterpret_cast<int32_t*>(s_bias + ncls);  // [4][128] each (half, part)'s highest code (FP16: logit)
   int32_t* s_hbest = s_hmax + 512;                              // FP16 [4][128] each (half, part)'s best class
   float* s_hsum = reinterpret_cast<float*>(s_hbest + 512);     // FP16 [4][128] each (half, part)'s sum
@@ -415,8 +420,10 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   for (int j = threadIdx.x; j < ncls; j += blockDim.x) {
-    s_off[j] = kInt8 ? p.off[j] : 0;
-    s_scale[j] = kInt8 ? p.scale[j] : 0.0f;
+    if constexpr (kInt8) {
+      s_off[j] = p.off[j];
+      s_scale[j] = p.scale[j];
+    }
     s_bias[j] = p.bias[j];
   }
   if (threadIdx.x < 4) s_count[threadIdx.x] = 0;
@@ -544,44 +551,46 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
 #pragma unroll
               for (int u = 0; u < 4; u += 2) {
                 // carbon/src/net/net.cpp:703-720: (acc - zero * colsum) * scale + bias, requantized;
-                // two classes at a time on the packed FP32 pipe (the same roundings)
+                // two classes at a time on the packed FP32 pipe (the same roundings); with kSat the
+                // clamp is the saturating pack below (rounding and clamping to integer bounds commute
+                // where |q| < 2^21)
                 const int32_t a0 = static_cast<int32_t>(r[4 * k + u]), a1 = static_cast<int32_t>(r[4 * k + u + 1]);
                 const float2 f = kFast ? magic_to_float2(a0 + oo[u], a1 + oo[u + 1]) : exact_i2f2(a0 - oo[u], a1 - oo[u + 1]);
                 float2 q = fmul_pair_rn(fadd2_rn(fmul_pair_rn(f, make_float2(ss[u], ss[u + 1])), make_float2(bv[u], bv[u + 1])),
                                     make_float2(p.out_inv_scale, p.out_inv_scale));
-                q.x = fminf(fmaxf(q.x, lo), hi);
-                q.y = fminf(fmaxf(q.y, lo), hi);
+                if constexpr (!kSat) {
+                  q.x = fminf(fmaxf(q.x, lo), hi);
+                  q.y = fminf(fmaxf(q.y, lo), hi);
+                }
                 int32_t t0, t1;
                 magic_rint_bits2(q, t0, t1);
-                code[4 * k + u] = t0 + zc;  // in [0, 255]
+                code[4 * k + u] = t0 + zc;
                 code[4 * k + u + 1] = t1 + zc;
               }
             }
             uint4 packed;
             uint32_t* pw = reinterpret_cast<uint32_t*>(&packed);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              pw[k] = __byte_perm(__byte_perm(code[4 * k], code[4 * k + 1], 0x0040),
-                                  __byte_perm(code[4 * k + 2], code[4 * k + 3], 0x0040), 0x5410);
+            for (int k = 0; k < 4; ++k) pw[k] = pack_sat_u8x4(code + 4 * k);  // in [0, 255] already without kSat
             *reinterpret_cast<uint4*>(my + j0) = packed;
-            if (j0 + 16 > p.classes) {
+            if (j0 + 16 > p.classes) {  // classes past the last: out of the maximum (code 0)
 #pragma unroll
-              for (int i = 0; i < 16; ++i)
-                if (j0 + i >= p.classes) code[i] = 0;
+              for (int k = 0; k < 4; ++k) {
+                const int keep = p.classes - j0 - 4 * k;  // bytes of word k that are real classes
+                pw[k] &= keep >= 4 ? 0xffffffffu : keep <= 0 ? 0u : (1u << (8 * keep)) - 1u;
+              }
             }
-            int32_t m8[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) m8[i] = max(code[i], code[i + 8]);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) m8[i] = max(m8[i], m8[i + 4]);
-            const int32_t m16 = max(max(m8[0], m8[1]), max(m8[2], m8[3]));
+            // the highest code: byte-wise maxima of the four words, then of the last word's bytes
+            uint32_t m4 = __vmaxu4(__vmaxu4(pw[0], pw[1]), __vmaxu4(pw[2], pw[3]));
+            m4 = __vmaxu4(m4, m4 >> 16);
+            const int32_t m16 = static_cast<int32_t>(__vmaxu4(m4, m4 >> 8) & 0xffu);
             if (m16 > mx) {  // a new highest code: the first of this group's classes holding it (the
                              // classes come in increasing order, so the earlier holder is kept on a tie;
-                             // bytes past `classes` follow the real ones and never come first)
+                             // bytes past `classes` are 0 here and never come first)
               mx = m16;
-              const uint32_t m4 = static_cast<uint32_t>(m16) * 0x01010101u;
-              const uint32_t f0 = first_byte_eq(pw[0], m4), f1 = first_byte_eq(pw[1], m4);
-              const uint32_t f2 = first_byte_eq(pw[2], m4), f3 = first_byte_eq(pw[3], m4);
+              const uint32_t m4b = static_cast<uint32_t>(m16) * 0x01010101u;
+              const uint32_t f0 = first_byte_eq(pw[0], m4b), f1 = first_byte_eq(pw[1], m4b);
+              const uint32_t f2 = first_byte_eq(pw[2], m4b), f3 = first_byte_eq(pw[3], m4b);
               fi = j0 + (f0   ? (__ffs(f0) - 1) >> 3
                          : f1 ? 4 + ((__ffs(f1) - 1) >> 3)
                          : f2 ? 8 + ((__ffs(f2) - 1) >> 3)

@@ -260,6 +260,14 @@ CREC_API int crec_conv_sweep(int device, int precision, const void* model, size_
  * dequantized output codes).  K * element bytes must be a multiple of 16 and at most 1024.  *ms:
  * the mean device time of the head's launches (with the INT8 probability sums) over `repeat`
  * after one warm-up.  A measurement and parity hook. */
+/* carbon::load_ctc_head (carbon/include/carbon/lines.h:120-135, carbon/src/lines.cpp:372-398): a
+ * recognizer's last 1x1 convolution as the export writes it, <model>.head.bin ("CTCHEAD1", int32
+ * classes, int32 k, the weight [classes][k] in float16, the bias [classes] in float32), checked as
+ * the reference checks it (CREC_E_MODEL, the reason in `error`), made into this library's FP16
+ * model blob of that one layer (for crec_head_sweep with CREC_FP16).  *blob_bytes gets the blob's
+ * size; CREC_E_RANGE when blob is null or capacity is smaller. */
+CREC_API int crec_ctc_head_blob(const void* file, size_t bytes, void* blob, size_t capacity, size_t* blob_bytes,
+                                char* error, size_t error_size);
 CREC_API int crec_head_sweep(int device, int precision, const void* model, size_t model_bytes, int frames,
                              const void* x, int32_t* ids, float* probs, float* logits, int repeat, double* ms);
 

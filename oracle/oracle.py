@@ -257,11 +257,24 @@ class Reference(_Common):
         L.ref_bench_pages.restype = _d
         L.ref_ctc_topk.argtypes = [_p, _i, _i, _i, _i, _p, _p, _p]
         L.ref_ctc_topk.restype = _i
+        L.ref_load_ctc_head.argtypes = [C.c_char_p, _p, _p, _p, _p, _i64]
+        L.ref_load_ctc_head.restype = _i
         self._crop_lines = L.ref_crop_lines
         self._ctc_topk = L.ref_ctc_topk
 
     def error(self) -> str:
         return self.lib.ref_last_error().decode()
+
+    def load_ctc_head(self, path, cap: int = 1 << 26):
+        """carbon::load_ctc_head: (classes, k, weight float16 [classes, k], bias [classes]); raises
+        ValueError with the reference's message for a file it refuses."""
+        classes, k = C.c_int(), C.c_int()
+        w = np.zeros(cap, np.uint16)
+        b = np.zeros(cap, np.float32)
+        if self.lib.ref_load_ctc_head(str(path).encode(), C.byref(classes), C.byref(k), _ptr(w), _ptr(b), cap) != 0:
+            raise ValueError(self.error())
+        n = classes.value * k.value
+        return classes.value, k.value, w[:n].view(np.float16).reshape(classes.value, k.value), b[:classes.value]
 
     def crop_region(self, box, rule: CropRule | None = None):
         rule = rule or CropRule.default()

@@ -135,6 +135,22 @@ int ref_light_on_dark(const uint8_t* crop, int w, int h, int64_t stride, int mar
 
 float ref_exp_neg(float x) { return carbon::cpu::detail::exp_neg(x); }
 
+// carbon::load_ctc_head on a file: its classes and k, and up to `cap` weights (float16 bits) and
+// `classes` biases (or -1, the reason in ref_last_error()).
+int ref_load_ctc_head(const char* path, int* classes, int* k, uint16_t* weight, float* bias, int64_t cap) {
+  try {
+    const carbon::CtcHead hd = carbon::load_ctc_head(path);
+    *classes = hd.classes;
+    *k = hd.k;
+    const size_t n = std::min<size_t>(hd.weight.size(), static_cast<size_t>(std::max<int64_t>(cap, 0)));
+    std::memcpy(weight, hd.weight.data(), n * 2);
+    if (static_cast<int64_t>(hd.weight.size()) <= cap) std::memcpy(bias, hd.bias.data(), hd.bias.size() * 4);
+    return 0;
+  } catch (const std::exception& e) {
+    return fail(e);
+  }
+}
+
 // cpu::ctc_topk (what carbon::frame_candidates calls) on one line's logits [classes][frames].
 int ref_ctc_topk(const float* logits, int classes, int frames, int t_n, int k, int32_t* ids, float* logp, float* blank) {
   try {

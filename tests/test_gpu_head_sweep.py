@@ -17,6 +17,7 @@ tcgen05 GEMM with each frame's argmax and CTC probability in its epilogue).
   An INT8 head of more classes than its shared memory holds codes for (1500) is refused."""
 from __future__ import annotations
 
+import struct
 import tempfile
 from pathlib import Path
 
@@ -47,18 +48,34 @@ def test_head_fp16_matches_the_unfused_head(n, k, classes, frames):
     f, w, b = case_data(k, classes, n * frames, seed=k + classes)
     fp, _, _ = model.make_head(k, classes, w.astype(np.float32), b, f.astype(np.float32).T[None, :, None, :])
     ids, probs, _, ms = native.head_sweep(netdef.compile_model(fp).to_blob(), native.FP16, f, classes, repeat=2)
+    grade_fp16(f, w, b, ids, probs, n * frames)
+    assert ms > 0
+
+
+def test_rec_cjk_head_from_its_head_file():
+    """The factorized rec-cjk head's last layer (docs/MODELS.md:215-219 of the reference: a 1x1 from
+    192 channels to 12,000 classes) given as the export writes it, a CTCHEAD1 file
+    (crec_ctc_head_blob), through the fused FP16 head: 4 lines of 64 frames, graded as above."""
+    f, w, b = case_data(192, 12000, 4 * 64, seed=12)
+    head = b"CTCHEAD1" + struct.pack("<ii", 12000, 192) + w.tobytes() + b.tobytes()
+    ids, probs, _, ms = native.head_sweep(native.ctc_head_blob(head), native.FP16, f, 12000, repeat=2)
+    grade_fp16(f, w, b, ids, probs, 4 * 64)
+    assert ms > 0
+
+
+def grade_fp16(f, w, b, ids, probs, frames):
+    classes = w.shape[0]
     logit = f.astype(np.float64) @ w.astype(np.float64).T + b.astype(np.float64)  # [frames, classes]
     best = logit.argmax(1)
     top = logit[np.arange(len(best)), best]
     assert ((ids >= 0) & (ids < classes)).all()
     tie = ids != best
     assert (top[tie] - logit[np.arange(len(best)), ids][tie] < FP32_ACC_TOL).all()
-    assert tie.sum() <= n * frames // 100 + 1
+    assert tie.sum() <= frames // 100 + 1
     s = np.exp(logit - top[:, None]).sum(1)
     keep = ~tie & (best != 0)
     assert np.all(np.abs(probs[keep] - 1.0 / s[keep]) <= FP32_ACC_TOL / s[keep])
     assert (probs[~tie & (best == 0)] == 0).all()
-    assert ms > 0
 
 
 @pytest.fixture(scope="module")
