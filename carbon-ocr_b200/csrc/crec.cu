@@ -192,6 +192,10 @@ struct crec_handle {
   // run buffers
   LineDesc* d_lines = nullptr;
   int* d_claim = nullptr;  // the crop kernel's line claims: [2], 0 between launches
+  int* d_order = nullptr;  // [max_lines] a run's lines in claim order
+  int* hs_order = nullptr;  // a call's claim orders, each run's from its first line's index (pinned)
+  size_t cap_hs_order = 0;
+  std::vector<int> order_count;  // the counting sort's buckets
   // lines beyond the crop kernel's reach: a run's list (slot order) on the device, their raw crops
   // (grown on demand), and the run's widest filter and tallest source span among them
   int* d_wide_idx = nullptr;
@@ -1095,6 +1099,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
     p.out_shift = s0.shift;
     p.err = h->d_err;
     p.claim = h->d_claim;
+    p.order = h->d_order;
     p.wide = h->d_wide;
     p.wide_pitch = h->cfg.max_width;
     int max_bw = 8;
@@ -1329,6 +1334,23 @@ int layout_run(crec_handle* h, const Source& src, const int* bw, int a, int b, s
   return CREC_OK;
 }
 
+// The crop kernel's claim order for lines [a, b) of the call (laid out): the costliest first, by
+// a counting sort on a line's source width plus twice its bucket width (the horizontal pass reads
+// the one, the vertical pass, finish and stem work over the other), in buckets of 64.
+void order_run(crec_handle* h, int a, int b) {
+  constexpr int kBuckets = 1024;
+  std::vector<int>& cnt = h->order_count;
+  cnt.assign(kBuckets + 1, 0);
+  auto key = [&](int i) {
+    const LineDesc& d = h->hs_lines[i];
+    const double k = ((d.x1 - d.x0) + 2.0 * d.bw) / 64.0;
+    return kBuckets - 1 - static_cast<int>(std::min<double>(kBuckets - 1, std::max(0.0, k)));  // costliest -> 0
+  };
+  for (int i = a; i < b; ++i) ++cnt[key(i) + 1];
+  for (int k = 0; k < kBuckets; ++k) cnt[k + 1] += cnt[k];
+  for (int i = a; i < b; ++i) h->hs_order[a + cnt[key(i)]++] = i - a;
+}
+
 // Lines [0, n) of a call, bucket widths bw[i]: cut into runs of at most max_lines lines and
 // max_columns columns, every run's copies and launches queued, one sync, the results packed.
 int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_lines* out) {
@@ -1365,6 +1387,7 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
       (rc = grow_pinned(h, &h->hs_length, &h->cap_length, n)) ||
       (rc = grow_pinned(h, &h->hs_mask, &h->cap_mask, mask_total)) ||
       (rc = grow_pinned(h, &h->hs_wide, &h->cap_hs_wide, n)) ||
+      (rc = grow_pinned(h, &h->hs_order, &h->cap_hs_order, n)) ||
       (rc = grow_device(h, &h->dp_counts, &cap_dp_lines, n)) || (rc = grow_device(h, &h->dp_offsets, &cap_dp_a, n)) ||
       (rc = grow_device(h, &h->dp_ids, &cap_dp_chars, frame_total)) ||
       (rc = grow_device(h, &h->dp_frames, &cap_dp_c, frame_total)) ||
@@ -1384,6 +1407,9 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
     long long cols = 0;
     if ((rc = layout_run(h, src, bw, r.a, r.b, r.mask_off, &cols))) return rc;
     const int m = r.b - r.a;
+    order_run(h, r.a, r.b);
+    CK(cudaMemcpyAsync(h->d_order, h->hs_order + r.a, sizeof(int) * m, cudaMemcpyHostToDevice, s));
+    h->st_h2d += static_cast<long long>(sizeof(int)) * m;
     if (h->run_wide > 0) {
       const size_t need = static_cast<size_t>(h->run_wide) * h->height * h->cfg.max_width;
       if ((rc = grow_device(h, &h->d_wide, &h->cap_wide, need))) return rc;
@@ -1501,6 +1527,8 @@ void free_all(crec_handle* h) {
   cudaFree(h->d_crops);
   cudaFree(h->d_crops_in);
   cudaFree(h->d_claim);
+  cudaFree(h->d_order);
+  cudaFreeHost(h->hs_order);
   cudaFree(h->d_cand_cols);
   cudaFree(h->d_cand_ids);
   cudaFree(h->d_cand_vals);
@@ -1590,7 +1618,8 @@ int open_impl(crec_handle* h, const crec_config* c) {
       (rc = dev_alloc(h, &h->d_frame_prob, frames)) || (rc = dev_alloc(h, &h->d_count, ml)) ||
       (rc = dev_alloc(h, &h->d_ids, frames)) || (rc = dev_alloc(h, &h->d_frames, frames)) ||
       (rc = dev_alloc(h, &h->d_probs, frames)) || (rc = dev_alloc(h, &h->d_err, 1)) ||
-      (rc = dev_alloc(h, &h->d_claim, 2)) || (rc = dev_alloc(h, &h->d_wide_idx, ml)))
+      (rc = dev_alloc(h, &h->d_claim, 2)) || (rc = dev_alloc(h, &h->d_wide_idx, ml)) ||
+      (rc = dev_alloc(h, &h->d_order, ml)))
     return rc;
   CK(cudaMemset(h->d_claim, 0, 2 * sizeof(int)));
   if ((rc = host_alloc(h, &h->h_err, 1)) || (rc = host_alloc(h, &h->h_total, 1)) ||

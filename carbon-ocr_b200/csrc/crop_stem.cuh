@@ -76,6 +76,7 @@ struct CropParams {
   int out_shift;  // log2 of input columns per stem column
   int* err;
   int* claim;  // [2] lines claimed past the first wave, CTAs done: both 0 between launches
+  const int* order;  // [n] the lines in the order they are claimed (the costliest first)
   const uint8_t* wide;  // the wide lines' resampled crops, [slot][height][wide_pitch]
   int wide_pitch;
 };
@@ -394,9 +395,10 @@ __device__ __forceinline__ void prefetch_line(const CropParams& p, int line, int
   }
 }
 
-// Persistent: a CTA takes lines one after another (its first is blockIdx.x, the next ones claimed
-// from p.claim[0] as it starts each line, so that the next line's region is prefetched while this
-// one is worked on); the stem's constants and the tables are set up once a CTA.
+// Persistent: a CTA takes lines one after another in p.order (its first is the blockIdx.x-th, the
+// next ones claimed from p.claim[0] as it starts each line, so that the next line's region is
+// prefetched while this one is worked on; the costliest lines first, so the last wave is short);
+// the stem's constants and the tables are set up once a CTA.
 template <bool kInt8>
 __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid_constant__ CropParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
@@ -423,8 +425,8 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int taps_stem = p.kh * p.kw;
   auto px = [&](int y, int x) -> uint8_t& { return qb[(y + 2) * qpitch + x + 4]; };
-  int line = blockIdx.x;
-  if (line < p.n) prefetch_line(p, line, tid, nthr);
+  int claimed = blockIdx.x;
+  if (claimed < p.n) prefetch_line(p, p.order[claimed], tid, nthr);
 
   // the stem's constants; INT8: a channel's taps as one word per kernel row (zeros past kw), and
   // the offset that turns the sum into kMagicBits + (sum - in_zero * colsum): |sum| <= 9 * 255 * 128
@@ -456,7 +458,8 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
     ftab[i] = __half2float(__float2half_rn(__fsub_rn(1.0f, __fdiv_rn(static_cast<float>(i), 255.0f))));
   }
 
-  while (line < p.n) {
+  while (claimed < p.n) {
+  const int line = p.order[claimed];
   if (tid == 0) s_next = static_cast<int>(gridDim.x) + atomicAdd(p.claim, 1);
   for (int i = tid; i < 256; i += nthr) hist[i] = 0;
   if (tid < 8) red[tid] = 0;
@@ -464,7 +467,7 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
   // claim; the line before is done with shared memory
   __syncthreads();
   const int next = s_next;
-  if (next < p.n) prefetch_line(p, next, tid, nthr);
+  if (next < p.n) prefetch_line(p, p.order[next], tid, nthr);
   const LineDesc L = p.lines[line];
   const PageDesc P = p.pages[L.page];
   const int bw = L.bw, cw = p.crops_in ? L.bw : L.width;
@@ -921,7 +924,7 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
     const long long col = c < lead ? c : gap0 + (c - lead);
     *reinterpret_cast<uint4*>(p.out + (oy + p.out_ph) * p.out_pitch + col * p.cp_out * eb + v * 16) = z4;
   }
-  line = next;
+  claimed = next;
   }
   // the claim counters back to 0 for the next launch, by the last CTA out (every claim is made by
   // then: a CTA counts itself out after its last claim)
