@@ -367,6 +367,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     const float lo = p.relu ? 0.0f : static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
     const int32_t zc = p.out_zero - kMagicBits, rzc = kMagicBits - p.res_zero;
     const uint32_t zb = static_cast<uint32_t>(p.out_zero) * 0x01010101u;
+    // INT8 without row stacking and a pixel's channels a multiple of 32 bytes: a thread's two groups
+    // of a TMEM read (an even group first) are 32 aligned contiguous bytes, stored at once
+    const bool pair32 = !kStack && (p.cp_out * p.ebytes) % 32 == 0;
     // this CTA's tile s: its first output row, its first output column, its channel tile (false
     // past the last one).  Tiles go round the CTAs (tile blockIdx.x + s * gridDim.x), or in band
     // mode band by band, each band's output rows in order
@@ -414,13 +417,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       if (kRes && valid)
         res = p.res + (oy + p.res_ph) * p.res_pitch + static_cast<long long>(ox >> p.res_shift) * p.res_cp * p.ebytes;
       const int c0 = n * p.nt;
-      // 16 of the tile's columns from r[0..16), starting at tile column tc: output row oy + q, channel cb
-      auto store16 = [&](const uint32_t* r, int tc) {
-        const int q = kStack ? ((tc >> 4) * p.cq_inv) >> 16 : 0;
-        const int cb = c0 + tc - q * p.cq;
-        if (!inside || cb >= p.cp_out || oy + q >= p.oh) return;
-        uint8_t* dst = dst0 + q * p.out_pitch;
-        if constexpr (kInt8) {
+      // INT8: the codes of 16 of the tile's columns from r[0..16), output channels cb on
+      auto code16 = [&](const uint32_t* r, int cb) -> uint4 {
           uint4 o;
           if (!valid) {
             o = make_uint4(zb, zb, zb, zb);
@@ -509,7 +507,16 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
             }
             o = make_uint4(pack_sat_u8x4(code), pack_sat_u8x4(code + 4), pack_sat_u8x4(code + 8), pack_sat_u8x4(code + 12));
           }
-          *reinterpret_cast<uint4*>(dst + cb) = o;
+          return o;
+      };
+      // 16 of the tile's columns from r[0..16), starting at tile column tc: output row oy + q, channel cb
+      auto store16 = [&](const uint32_t* r, int tc) {
+        const int q = kStack ? ((tc >> 4) * p.cq_inv) >> 16 : 0;
+        const int cb = c0 + tc - q * p.cq;
+        if (!inside || cb >= p.cp_out || oy + q >= p.oh) return;
+        uint8_t* dst = dst0 + q * p.out_pitch;
+        if constexpr (kInt8) {
+          *reinterpret_cast<uint4*>(dst + cb) = code16(r, cb);
         } else {
           alignas(16) __half o[16];
           if (!valid) {
@@ -530,8 +537,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
               o[i] = __float2half_rn(j < p.c_out ? v : 0.0f);
             }
           }
-          *reinterpret_cast<uint4*>(dst + cb * 2) = *reinterpret_cast<const uint4*>(o);
-          *reinterpret_cast<uint4*>(dst + cb * 2 + 16) = *reinterpret_cast<const uint4*>(o + 8);
+          // one 32-byte store: a pixel's channel pitch and cb * 2 are multiples of 32 bytes
+          st_global_v8(dst + cb * 2, *reinterpret_cast<const uint4*>(o), *reinterpret_cast<const uint4*>(o + 8));
         }
       };
       // TMEM read 32 columns at a time (the other warps on the SM hide the loads' latency); the
@@ -552,8 +559,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
         tmem_wait_ld();
         tmem_pin(ra);
         if (g + w >= g1) release();
-        store16(ra, g * 16);
-        if (w == 2) store16(ra + 16, g * 16 + 16);
+        if (kInt8 && pair32 && w == 2 && inside && c0 + g * 16 + 32 <= p.cp_out) {
+          // two groups of one pixel, 32 contiguous bytes: one full-sector store
+          const int cb = c0 + g * 16;
+          st_global_v8(dst0 + cb, code16(ra, cb), code16(ra + 16, cb + 16));
+        } else {
+          store16(ra, g * 16);
+          if (w == 2) store16(ra + 16, g * 16 + 16);
+        }
       }
     }
   }

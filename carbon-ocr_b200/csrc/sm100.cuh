@@ -311,6 +311,13 @@ __device__ __forceinline__ void magic_rint_bits2(float2 x, int32_t& r0, int32_t&
   r1 = __float_as_int(t.y);
 }
 
+// 32 bytes to global memory in one store (sm_100's 256-bit st.global; p 32-byte aligned).
+__device__ __forceinline__ void st_global_v8(void* p, uint4 a, uint4 b) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a.x), "r"(a.y), "r"(a.z),
+               "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
+}
+
 // Bytes hi and lo, each saturated to [0, 255], above them the low 16 bits of `upper`:
 // upper << 16 | sat(hi) << 8 | sat(lo) (PTX cvt.pack.sat.u8.s32.b32).
 __device__ __forceinline__ uint32_t pack_sat_u8x2(int32_t hi, int32_t lo, uint32_t upper) {
