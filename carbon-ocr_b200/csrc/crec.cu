@@ -597,6 +597,7 @@ int setup_layer(crec_handle* h, size_t li) {
   }
   if (l.kind == kKindDw) {  // [taps][cp]
     const int cp = y.cp;
+    if (h->int8) l.sat = round_first(h, l, x, y, scale, bias);
     if (h->int8) {
       std::vector<int8_t> w(static_cast<size_t>(taps) * cp, 0);
       for (int c = 0; c < l.cout; ++c)
@@ -1182,6 +1183,7 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
       p.bias = l.dbias;
       p.out_zero = y.zero;
       p.relu = l.relu;
+      p.sat = l.sat ? 1 : 0;
       p.out_inv_scale = h->int8 ? 1.0f / y.scale : 1.0f;
       p.out = y.base;
       p.out_ph = y.ph;
@@ -1196,8 +1198,9 @@ int launch_run(crec_handle* h, int n, long long cols, bool keep_crops) {
         const long long tiles = static_cast<long long>(oh) * ((ow + kDwTile - 1) / kDwTile);
         const int ncols = dw_row_cols(l.kw, x.extra);
         const int smem = ((ncols * y.cp + 15) & ~15) + 24 * y.cp;
-        CK(cudaFuncSetAttribute(dw_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        dw_row_kernel<<<static_cast<int>(tiles), 256, smem, s>>>(p);
+        auto* k = l.sat ? dw_row_kernel<true> : dw_row_kernel<false>;
+        CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        k<<<static_cast<int>(tiles), 256, smem, s>>>(p);
       } else if (!h->int8 && l.kh == 1 && xp.cp == y.cp && (l.kw == 3 || l.kw == 5 || l.kw == 7 || l.kw == 9)) {
         // FP16, one kernel row: a CTA 2 x kDwF16Run output pixels of a row
         const int tiles = static_cast<int>(static_cast<long long>(oh) * ((ow + 2 * kDwF16Run - 1) / (2 * kDwF16Run)));

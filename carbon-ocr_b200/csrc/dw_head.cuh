@@ -31,6 +31,7 @@ struct DwParams {
   const float* scale;
   const float* bias;
   int out_zero, relu;
+  int sat;  // INT8 row kernel: |v * inv_scale| < 2^21 always (round first, clamp while packing)
   float out_inv_scale;
   uint8_t* out;
   int out_ph;
@@ -132,6 +133,7 @@ constexpr int kDwTile = 64;
 
 __host__ __device__ inline int dw_row_cols(int kw, int in_shift) { return ((kDwTile - 1 + kw - 1) >> in_shift) + 2; }
 
+template <bool kSat>
 __global__ void __launch_bounds__(256) dw_row_kernel(const __grid_constant__ DwParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int cp = p.cp, G = cp >> 4;
@@ -218,14 +220,16 @@ __global__ void __launch_bounds__(256) dw_row_kernel(const __grid_constant__ DwP
       for (int u = 0; u < 4; u += 2) {  // two channels at a time on the packed FP32 pipe
         float2 q = out_stage2(acc[4 * k + u], acc[4 * k + u + 1], make_float2(ss[u], ss[u + 1]),
                               make_float2(bb[u], bb[u + 1]), p.out_inv_scale);
-        q.x = fminf(fmaxf(q.x, lo), hi);
-        q.y = fminf(fmaxf(q.y, lo), hi);
+        if constexpr (!kSat) {  // with kSat the clamp is the saturating pack (rounding first is exact there)
+          q.x = fminf(fmaxf(q.x, lo), hi);
+          q.y = fminf(fmaxf(q.y, lo), hi);
+        }
         int32_t t0, t1;
         magic_rint_bits2(q, t0, t1);
         code[u] = c0 + 4 * k + u < p.c ? t0 + zc : p.out_zero;
         code[u + 1] = c0 + 4 * k + u + 1 < p.c ? t1 + zc : p.out_zero;
       }
-      wv[k] = __byte_perm(__byte_perm(code[0], code[1], 0x0040), __byte_perm(code[2], code[3], 0x0040), 0x5410);
+      wv[k] = pack_sat_u8x4(code);
     }
     *reinterpret_cast<uint4*>(dst) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
   }
