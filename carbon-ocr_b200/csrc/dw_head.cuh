@@ -776,22 +776,31 @@ template <bool kShared>
 __device__ __forceinline__ float class_sum(const uint8_t* row, int classes, const float* trow) {
   float sum = 0.0f;
   const uint4* r4 = reinterpret_cast<const uint4*>(row);
-  const int full = classes & ~15;
-  uint4 w = full ? __ldg(r4) : make_uint4(0, 0, 0, 0);
-  for (int j0 = 0; j0 < full; j0 += 16) {
-    const uint4 cur = w;
-    if (j0 + 16 < full) w = __ldg(r4 + (j0 >> 4) + 1);  // the next 16 codes in flight
-    const uint32_t ww[4] = {cur.x, cur.y, cur.z, cur.w};
-    float t[16];
+  const int nfull = classes >> 4;
+  // the next four 16-code chunks in flight (a ring of registers), so the chain of adds does not
+  // wait on each chunk's load; the chunks are added in class order
+  constexpr int kAhead = 4;
+  uint4 ring[kAhead];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t q = (ww[i >> 2] >> (8 * (i & 3))) & 0xffu;
-      t[i] = kShared ? trow[q] : __ldg(trow + q);
+  for (int a = 0; a < kAhead; ++a) ring[a] = a < nfull ? __ldg(r4 + a) : make_uint4(0, 0, 0, 0);
+  for (int c = 0; c < nfull; c += kAhead) {
+#pragma unroll
+    for (int a = 0; a < kAhead; ++a) {
+      if (c + a >= nfull) break;
+      const uint4 cur = ring[a];
+      if (c + a + kAhead < nfull) ring[a] = __ldg(r4 + c + a + kAhead);
+      const uint32_t ww[4] = {cur.x, cur.y, cur.z, cur.w};
+      float t[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t q = (ww[i >> 2] >> (8 * (i & 3))) & 0xffu;
+        t[i] = kShared ? trow[q] : __ldg(trow + q);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, t[i]);
     }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, t[i]);
   }
-  for (int j = full; j < classes; ++j) {
+  for (int j = nfull << 4; j < classes; ++j) {
     const uint32_t q = row[j];
     sum = __fadd_rn(sum, kShared ? trow[q] : __ldg(trow + q));
   }
