@@ -130,9 +130,11 @@ def reduce_sum(v: float, world: int, device: str) -> float:
     return float(t.item())
 
 
-# measured: dram__bytes_read.sum + dram__bytes_write.sum of all conv_gemm launches of one
-# 524,288-column run / 11, x 4 (a 2,097,152-column run)
-CONV_TRAFFIC_PER_LAUNCH = 646.2e6 / 11 * 4
+# measured by ncu: dram__bytes_read.sum + dram__bytes_write.sum of the 11 conv_gemm launches of
+# one 524,288-column run of 128 config-5 pages, 631.4 MB, / 11,
+# x 4 (a 2,097,152-column run); scaled by columns to the bench's runs below (a lower bound: at the
+# capture's size the outputs mostly stay in L2)
+CONV_TRAFFIC_PER_LAUNCH = 631.4e6 / 11 * 4
 
 
 class ClockSampler:
