@@ -32,6 +32,7 @@
 #include "dw_head.cuh"
 #include "peak.cuh"
 #include "sm100.cuh"
+#include "host_pool.h"
 #include "stager.h"
 
 using namespace crec;
@@ -45,6 +46,8 @@ constexpr int kKindConv = 0, kKindDw = 1, kKindResize = 2;
 // step).  It needs its input written chunk-planar by the layer before.
 constexpr bool kNoBand = true;
 constexpr size_t kGuard = 64 << 10;
+constexpr int kPoolLines = 2048;    // a run's layout goes to the host pool from this many lines
+constexpr int kOrderBuckets = 1024;  // the crop kernel's claim order: a counting sort's buckets
 
 struct Value {
   int c = 0, u8 = 0, ph = 0, pw = 0, zero = 0;
@@ -196,6 +199,8 @@ struct crec_handle {
   int* hs_order = nullptr;  // a call's claim orders, each run's from its first line's index (pinned)
   size_t cap_hs_order = 0;
   std::vector<int> order_count;  // the counting sort's buckets
+  std::vector<int> hs_key;       // a call's lines' claim keys
+  std::unique_ptr<crec::HostPool> pool;  // the layout's threads (made for the first large run)
   // lines beyond the crop kernel's reach: a run's list (slot order) on the device, their raw crops
   // (grown on demand), and the run's widest filter and tallest source span among them
   int* d_wide_idx = nullptr;
@@ -223,6 +228,12 @@ struct crec_handle {
   float* dp_probs = nullptr;
   long long* d_total = nullptr;
   long long* h_total = nullptr;  // pinned
+  // a call's running total after each run but the last (pinned), recorded with the run's event, so
+  // the run's decodings are read back while the next run computes (on the readback stream)
+  long long* h_run_total = nullptr;
+  size_t cap_run_total = 0;
+  std::vector<cudaEvent_t> ev_run;
+  cudaStream_t read_stream = nullptr;
   size_t cap_dp_lines = 0, cap_dp_chars = 0;
   int32_t* d_frame_id = nullptr;
   float* d_frame_prob = nullptr;
@@ -1274,88 +1285,134 @@ struct Source {  // where a call's lines come from
   const int32_t* widths = nullptr;
 };
 
-// Lays out lines [a, b) of a call as one run (its LineDescs, mask, frame starts and lengths in
-// the call's staging at the given offsets); returns the run's input columns in *cols.
+// Lays out lines [a, b) of a call as one run (its LineDescs, mask, frame starts and lengths, claim
+// keys in the call's staging at the given offsets); returns the run's input columns in *cols.
+// The segments are one prefix sum; each line's crop region, checks, descriptor and mask bytes are
+// then independent, so they run on the host pool in parts of consecutive lines, and the first
+// failing line's error is the one reported, as one pass in line order would.
 int layout_run(crec_handle* h, const Source& src, const int* bw, int a, int b, size_t mask_off, long long* cols_out) {
   const crec_crop_rule& rule = h->cfg.crop;
   long long seg = h->gap;
-  h->run_wide = h->run_vtaps = h->run_htaps = h->run_rows = 0;
   for (int i = a; i < b; ++i) {
-    LineDesc& d = h->hs_lines[i];
-    d.wide = -1;
-    double reg[4] = {0, 0, 1, 1};
-    int width = 0;
-    if (src.crops) {
-      width = src.widths[i];
-      if (width <= 0 || width > bw[i] || bw[i] > src.pitch)
-        return set_error(h, CREC_E_RANGE, "recognize_crops: line " + std::to_string(i) + " width " +
-                                              std::to_string(width) + ", bucket " + std::to_string(bw[i]));
-      d.page = 0;
-    } else {
-      crec_crop_region(&src.boxes[i], &rule, reg, &width);
-      const int pg = src.page_of[i];
-      if (pg < 0 || pg >= static_cast<int>(h->pages.size()))
-        return set_error(h, CREC_E_INVALID, "line " + std::to_string(i) + ": page " + std::to_string(pg) + " not set");
-      if (width > bw[i])
-        return set_error(h, CREC_E_RANGE, "crop_lines: line " + std::to_string(i) + " is " + std::to_string(width) +
-                                              " px wide, the batch " + std::to_string(bw[i]));
-      // the crop kernel's reach: at most kMaxTaps taps a sample (PIL's ksize, 2 ceil(support) + 1)
-      // and kMaxSrcRows source rows (the bound the kernel computes); past it, crop_wide_kernel
-      const double sx = std::max(1.0, (reg[2] - reg[0]) / width), sy = std::max(1.0, (reg[3] - reg[1]) / rule.height);
-      if (!(sx < 1e6) || !(sy < 1e6))
-        return set_error(h, CREC_E_RANGE, "line " + std::to_string(i) + ": a degenerate crop region");
-      const int ht = static_cast<int>(std::ceil(sx)) * 2 + 1, vt = static_cast<int>(std::ceil(sy)) * 2 + 1;
-      const int rows = static_cast<int>(std::ceil((reg[3] - reg[1]) + 2.0 * sy)) + 4;
-      d.wide = -1;
-      if (ht > kMaxTaps || vt > kMaxTaps || rows > kMaxSrcRows) {
-        d.wide = h->run_wide;
-        h->hs_wide[a + h->run_wide++] = i - a;
-        h->run_htaps = std::max(h->run_htaps, ht);
-        h->run_vtaps = std::max(h->run_vtaps, vt);
-        h->run_rows = std::max(h->run_rows, rows);
-      }
-      d.page = pg;
-    }
-    d.x0 = reg[0];
-    d.y0 = reg[1];
-    d.x1 = reg[2];
-    d.y1 = reg[3];
-    d.width = width;
-    d.bw = bw[i];
-    d.seg = static_cast<int>(seg);
-    h->hs_frame0[i] = static_cast<int>(seg >> h->head_shift);
-    h->hs_length[i] = std::min(bw[i] >> h->head_shift, width / rule.frame_px);
+    h->hs_lines[i].seg = static_cast<int>(seg);
     seg += bw[i] + h->gap;
   }
+  const long long end = seg - h->gap;  // the column after the last line
   const long long cols = round_up(seg, 128LL << h->max_shift);
-  if (cols > h->max_cols) return set_error(h, CREC_E_RANGE, "a run wider than the configured columns");
-  for (int i = a; i < b; ++i) h->hs_lines[i].next_seg = i + 1 < b ? h->hs_lines[i + 1].seg : static_cast<int>(cols);
   uint8_t* mask = h->hs_mask + mask_off;
-  std::memset(mask, 0, static_cast<size_t>(cols / 8));
-  for (int i = a; i < b; ++i) std::memset(mask + h->hs_lines[i].seg / 8, 1, static_cast<size_t>(bw[i] / 8));
+  const int gap8 = h->gap / 8;
+  struct Part {
+    int err = CREC_OK;
+    std::string msg;
+    std::vector<int> wide;  // lines past the crop kernel's reach, in line order
+    int ht = 0, vt = 0, rows = 0;
+  };
+  const int m = b - a;
+  const int parts = h->pool && m >= kPoolLines ? std::min(4 * h->pool->threads(), m / 256) : 1;
+  std::vector<Part> part(static_cast<size_t>(parts));
+  auto lay = [&](int p) {
+    const int lo = a + static_cast<int>(static_cast<long long>(m) * p / parts);
+    const int hi = a + static_cast<int>(static_cast<long long>(m) * (p + 1) / parts);
+    Part& P = part[static_cast<size_t>(p)];
+    for (int i = lo; i < hi; ++i) {
+      LineDesc& d = h->hs_lines[i];
+      d.wide = -1;
+      double reg[4] = {0, 0, 1, 1};
+      int width = 0;
+      if (src.crops) {
+        width = src.widths[i];
+        if (width <= 0 || width > bw[i] || bw[i] > src.pitch) {
+          P.err = CREC_E_RANGE;
+          P.msg = "recognize_crops: line " + std::to_string(i) + " width " + std::to_string(width) + ", bucket " +
+                  std::to_string(bw[i]);
+          return;
+        }
+        d.page = 0;
+      } else {
+        crec_crop_region(&src.boxes[i], &rule, reg, &width);
+        const int pg = src.page_of[i];
+        if (pg < 0 || pg >= static_cast<int>(h->pages.size())) {
+          P.err = CREC_E_INVALID;
+          P.msg = "line " + std::to_string(i) + ": page " + std::to_string(pg) + " not set";
+          return;
+        }
+        if (width > bw[i]) {
+          P.err = CREC_E_RANGE;
+          P.msg = "crop_lines: line " + std::to_string(i) + " is " + std::to_string(width) + " px wide, the batch " +
+                  std::to_string(bw[i]);
+          return;
+        }
+        // the crop kernel's reach: at most kMaxTaps taps a sample (PIL's ksize, 2 ceil(support) + 1)
+        // and kMaxSrcRows source rows (the bound the kernel computes); past it, crop_wide_kernel
+        const double sx = std::max(1.0, (reg[2] - reg[0]) / width), sy = std::max(1.0, (reg[3] - reg[1]) / rule.height);
+        if (!(sx < 1e6) || !(sy < 1e6)) {
+          P.err = CREC_E_RANGE;
+          P.msg = "line " + std::to_string(i) + ": a degenerate crop region";
+          return;
+        }
+        const int ht = static_cast<int>(std::ceil(sx)) * 2 + 1, vt = static_cast<int>(std::ceil(sy)) * 2 + 1;
+        const int rows = static_cast<int>(std::ceil((reg[3] - reg[1]) + 2.0 * sy)) + 4;
+        if (ht > kMaxTaps || vt > kMaxTaps || rows > kMaxSrcRows) {
+          P.wide.push_back(i);
+          P.ht = std::max(P.ht, ht);
+          P.vt = std::max(P.vt, vt);
+          P.rows = std::max(P.rows, rows);
+        }
+        d.page = pg;
+      }
+      d.x0 = reg[0];
+      d.y0 = reg[1];
+      d.x1 = reg[2];
+      d.y1 = reg[3];
+      d.width = width;
+      d.bw = bw[i];
+      d.next_seg = i + 1 < b ? h->hs_lines[i + 1].seg : static_cast<int>(cols);
+      h->hs_frame0[i] = d.seg >> h->head_shift;
+      h->hs_length[i] = std::min(bw[i] >> h->head_shift, width / rule.frame_px);
+      // the claim order's key: a line's source width plus twice its bucket width, in buckets of 64
+      // (the horizontal pass reads the one; the vertical pass, finish and stem work over the other)
+      const double k = ((d.x1 - d.x0) + 2.0 * d.bw) / 64.0;
+      h->hs_key[i] = kOrderBuckets - 1 - static_cast<int>(std::min<double>(kOrderBuckets - 1, std::max(0.0, k)));
+      std::memset(mask + (d.seg / 8 - gap8), 0, static_cast<size_t>(gap8));
+      std::memset(mask + d.seg / 8, 1, static_cast<size_t>(bw[i] / 8));
+    }
+  };
+  if (parts > 1)
+    h->pool->run(parts, lay);
+  else
+    lay(0);
+  for (const Part& P : part)
+    if (P.err) return set_error(h, P.err, P.msg);
+  h->run_wide = h->run_vtaps = h->run_htaps = h->run_rows = 0;
+  for (const Part& P : part) {
+    for (int i : P.wide) {
+      h->hs_lines[i].wide = h->run_wide;
+      h->hs_wide[a + h->run_wide++] = i - a;
+    }
+    h->run_htaps = std::max(h->run_htaps, P.ht);
+    h->run_vtaps = std::max(h->run_vtaps, P.vt);
+    h->run_rows = std::max(h->run_rows, P.rows);
+  }
+  if (cols > h->max_cols) return set_error(h, CREC_E_RANGE, "a run wider than the configured columns");
+  std::memset(mask + end / 8, 0, static_cast<size_t>((cols - end) / 8));
   *cols_out = cols;
   return CREC_OK;
 }
 
 // The crop kernel's claim order for lines [a, b) of the call (laid out): the costliest first, by
-// a counting sort on a line's source width plus twice its bucket width (the horizontal pass reads
-// the one, the vertical pass, finish and stem work over the other), in buckets of 64.
+// a counting sort on the keys layout_run computed.
 void order_run(crec_handle* h, int a, int b) {
-  constexpr int kBuckets = 1024;
   std::vector<int>& cnt = h->order_count;
-  cnt.assign(kBuckets + 1, 0);
-  auto key = [&](int i) {
-    const LineDesc& d = h->hs_lines[i];
-    const double k = ((d.x1 - d.x0) + 2.0 * d.bw) / 64.0;
-    return kBuckets - 1 - static_cast<int>(std::min<double>(kBuckets - 1, std::max(0.0, k)));  // costliest -> 0
-  };
-  for (int i = a; i < b; ++i) ++cnt[key(i) + 1];
-  for (int k = 0; k < kBuckets; ++k) cnt[k + 1] += cnt[k];
-  for (int i = a; i < b; ++i) h->hs_order[a + cnt[key(i)]++] = i - a;
+  cnt.assign(kOrderBuckets + 1, 0);
+  const int* key = h->hs_key.data();
+  for (int i = a; i < b; ++i) ++cnt[key[i] + 1];
+  for (int k = 0; k < kOrderBuckets; ++k) cnt[k + 1] += cnt[k];
+  for (int i = a; i < b; ++i) h->hs_order[a + cnt[key[i]]++] = i - a;
 }
 
 // Lines [0, n) of a call, bucket widths bw[i]: cut into runs of at most max_lines lines and
-// max_columns columns, every run's copies and launches queued, one sync, the results packed.
+// max_columns columns, each run laid out and queued while the one before computes; a finished
+// run's decodings are read back while the next one computes; the last run's after one sync.
 int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_lines* out) {
   out->total = 0;
   h->last_n = 0;  // until this call's last run is queued: no candidates from an earlier call
@@ -1367,17 +1424,19 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
   };
   std::vector<Run> runs;
   size_t mask_total = 0, frame_total = 0;
+  const long long unit = 128LL << h->max_shift;
+  const long long fit = h->max_cols / unit * unit;  // round_up(c, unit) <= max_cols exactly when c <= fit
   for (int a = 0; a < n;) {
     long long cols = h->gap;
     int b = a;
     while (b < n && b - a < h->cfg.max_lines) {
       const long long next = cols + bw[b] + h->gap;
-      if (round_up(next, 128LL << h->max_shift) > h->max_cols) break;
+      if (next > fit) break;
       cols = next;
       ++b;
     }
     if (b == a) return set_error(h, CREC_E_RANGE, "a line wider than the configured columns");
-    const long long rc = round_up(cols, 128LL << h->max_shift);
+    const long long rc = round_up(cols, unit);
     runs.push_back({a, b, rc, mask_total, frame_total});
     mask_total += static_cast<size_t>(rc / 8);
     frame_total += static_cast<size_t>(rc >> h->head_shift);
@@ -1391,6 +1450,7 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
       (rc = grow_pinned(h, &h->hs_mask, &h->cap_mask, mask_total)) ||
       (rc = grow_pinned(h, &h->hs_wide, &h->cap_hs_wide, n)) ||
       (rc = grow_pinned(h, &h->hs_order, &h->cap_hs_order, n)) ||
+      (rc = grow_pinned(h, &h->h_run_total, &h->cap_run_total, runs.size())) ||
       (rc = grow_device(h, &h->dp_counts, &cap_dp_lines, n)) || (rc = grow_device(h, &h->dp_offsets, &cap_dp_a, n)) ||
       (rc = grow_device(h, &h->dp_ids, &cap_dp_chars, frame_total)) ||
       (rc = grow_device(h, &h->dp_frames, &cap_dp_c, frame_total)) ||
@@ -1398,6 +1458,17 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
     return rc;
   h->cap_dp_lines = std::min(cap_dp_lines, cap_dp_a);
   h->cap_dp_chars = std::min({cap_dp_chars, cap_dp_c, cap_dp_d});
+  if (h->hs_key.size() < static_cast<size_t>(n)) h->hs_key.resize(static_cast<size_t>(n));
+  if (!h->pool && n >= kPoolLines) {
+    const int hw = static_cast<int>(std::thread::hardware_concurrency());
+    h->pool = std::make_unique<crec::HostPool>(std::clamp(hw / 2, 1, 8) - 1);
+  }
+  while (h->ev_run.size() + 1 < runs.size()) {
+    cudaEvent_t e = nullptr;
+    CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    h->ev_run.push_back(e);
+  }
+  if (runs.size() > 1 && !h->read_stream) CK(cudaStreamCreateWithFlags(&h->read_stream, cudaStreamNonBlocking));
   cudaStream_t s = h->stream;
   h->st_runs = static_cast<long long>(runs.size());
   h->st_wide = 0;
@@ -1406,50 +1477,78 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
   h->st_d2h = 4 + 8;  // the error word, the total
   CK(cudaMemsetAsync(h->d_err, 0, sizeof(int), s));
   CK(cudaMemsetAsync(h->d_total, 0, sizeof(long long), s));
-  for (const Run& r : runs) {
+  // a finished run's decodings into the caller's buffers: its lines' counts and offsets, and the
+  // characters the runs before it did not have (the call's total after it is `total`)
+  long long read_total = 0;
+  auto read_run = [&](const Run& q, long long total, cudaStream_t rs) -> int {
+    if (total > out->capacity) return set_error(h, CREC_E_RANGE, "crec_lines: capacity too small");
+    const size_t m = static_cast<size_t>(q.b - q.a);
+    CK(cudaMemcpyAsync(out->counts + q.a, h->dp_counts + q.a, sizeof(int32_t) * m, cudaMemcpyDeviceToHost, rs));
+    CK(cudaMemcpyAsync(out->offsets + q.a, h->dp_offsets + q.a, sizeof(int32_t) * m, cudaMemcpyDeviceToHost, rs));
+    if (total > read_total) {  // the characters themselves, and nothing else
+      const size_t k = static_cast<size_t>(total - read_total);
+      CK(cudaMemcpyAsync(out->ids + read_total, h->dp_ids + read_total, sizeof(int32_t) * k, cudaMemcpyDeviceToHost, rs));
+      CK(cudaMemcpyAsync(out->frames + read_total, h->dp_frames + read_total, sizeof(int32_t) * k,
+                         cudaMemcpyDeviceToHost, rs));
+      CK(cudaMemcpyAsync(out->probs + read_total, h->dp_probs + read_total, sizeof(float) * k, cudaMemcpyDeviceToHost,
+                         rs));
+    }
+    CK(cudaStreamSynchronize(rs));
+    read_total = total;
+    return CREC_OK;
+  };
+  for (size_t r = 0; r < runs.size(); ++r) {
+    const Run& q = runs[r];
     long long cols = 0;
-    if ((rc = layout_run(h, src, bw, r.a, r.b, r.mask_off, &cols))) return rc;
-    const int m = r.b - r.a;
-    order_run(h, r.a, r.b);
-    CK(cudaMemcpyAsync(h->d_order, h->hs_order + r.a, sizeof(int) * m, cudaMemcpyHostToDevice, s));
+    if ((rc = layout_run(h, src, bw, q.a, q.b, q.mask_off, &cols))) return rc;
+    const int m = q.b - q.a;
+    order_run(h, q.a, q.b);
+    CK(cudaMemcpyAsync(h->d_order, h->hs_order + q.a, sizeof(int) * m, cudaMemcpyHostToDevice, s));
     h->st_h2d += static_cast<long long>(sizeof(int)) * m;
     if (h->run_wide > 0) {
       const size_t need = static_cast<size_t>(h->run_wide) * h->height * h->cfg.max_width;
       if ((rc = grow_device(h, &h->d_wide, &h->cap_wide, need))) return rc;
-      CK(cudaMemcpyAsync(h->d_wide_idx, h->hs_wide + r.a, sizeof(int) * h->run_wide, cudaMemcpyHostToDevice, s));
+      CK(cudaMemcpyAsync(h->d_wide_idx, h->hs_wide + q.a, sizeof(int) * h->run_wide, cudaMemcpyHostToDevice, s));
       h->st_h2d += static_cast<long long>(sizeof(int)) * h->run_wide;
       h->st_wide += h->run_wide;
     }
-    CK(cudaMemcpyAsync(h->d_lines, h->hs_lines + r.a, sizeof(LineDesc) * m, cudaMemcpyHostToDevice, s));
-    CK(cudaMemcpyAsync(h->d_mask, h->hs_mask + r.mask_off, static_cast<size_t>(cols / 8), cudaMemcpyHostToDevice, s));
-    CK(cudaMemcpyAsync(h->d_frame0, h->hs_frame0 + r.a, sizeof(int) * m, cudaMemcpyHostToDevice, s));
-    CK(cudaMemcpyAsync(h->d_length, h->hs_length + r.a, sizeof(int) * m, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(h->d_lines, h->hs_lines + q.a, sizeof(LineDesc) * m, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(h->d_mask, h->hs_mask + q.mask_off, static_cast<size_t>(cols / 8), cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(h->d_frame0, h->hs_frame0 + q.a, sizeof(int) * m, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(h->d_length, h->hs_length + q.a, sizeof(int) * m, cudaMemcpyHostToDevice, s));
     h->run_crops = nullptr;
     if (src.crops) {
-      CK(cudaMemcpyAsync(h->d_crops_in, src.crops + static_cast<size_t>(r.a) * h->height * src.pitch,
+      CK(cudaMemcpyAsync(h->d_crops_in, src.crops + static_cast<size_t>(q.a) * h->height * src.pitch,
                          static_cast<size_t>(m) * h->height * src.pitch, cudaMemcpyHostToDevice, s));
       h->run_crops = h->d_crops_in;
       h->crops_in_pitch = src.pitch;
     }
     h->st_h2d += static_cast<long long>(sizeof(LineDesc) * m + cols / 8 + 2 * sizeof(int) * m);
     if (src.crops) h->st_h2d += static_cast<long long>(m) * h->height * src.pitch;
-    add_run_ops(h, bw, r.a, r.b);
-    h->run_bw = bw + r.a;
+    add_run_ops(h, bw, q.a, q.b);
+    h->run_bw = bw + q.a;
     if ((rc = launch_run(h, m, cols, h->d_crops != nullptr))) return rc;
     {  // this run's characters packed after the previous runs'
       ProfScope prof(h, kProfCollapse, static_cast<int>(h->l.size()));
-      scan_counts_kernel<<<1, 1024, 0, s>>>(h->d_count, m, h->dp_counts + r.a, h->dp_offsets + r.a, h->d_total);
+      scan_counts_kernel<<<1, 1024, 0, s>>>(h->d_count, m, h->dp_counts + q.a, h->dp_offsets + q.a, h->d_total);
       pack_kernel<<<(m * 32 + 255) / 256, 256, 0, s>>>(h->d_ids, h->d_frames, h->d_probs, h->d_frame0,
-                                                      h->dp_counts + r.a, h->dp_offsets + r.a, m, h->dp_ids,
+                                                      h->dp_counts + q.a, h->dp_offsets + q.a, m, h->dp_ids,
                                                       h->dp_frames, h->dp_probs);
       ++h->st_launches;
     }
     CK(cudaGetLastError());
+    if (r + 1 < runs.size()) {  // the call's total after this run, and the run's end
+      CK(cudaMemcpyAsync(h->h_run_total + r, h->d_total, sizeof(long long), cudaMemcpyDeviceToHost, s));
+      CK(cudaEventRecord(h->ev_run[r], s));
+      h->st_d2h += 8;
+    }
+    if (r > 0) {  // the run before this one, read back while this one computes
+      CK(cudaEventSynchronize(h->ev_run[r - 1]));
+      if ((rc = read_run(runs[r - 1], h->h_run_total[r - 1], h->read_stream))) return rc;
+    }
   }
   CK(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(h->h_total, h->d_total, sizeof(long long), cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(out->counts, h->dp_counts, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(out->offsets, h->dp_offsets, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
   if (h->inject_sticky) {  // test hook: the completion check fails as after a faulted kernel
     h->inject_sticky = false;
@@ -1461,13 +1560,7 @@ int recognize_all(crec_handle* h, const Source& src, const int* bw, int n, crec_
   if (*h->h_err)
     return set_error(h, CREC_E_TIMEOUT, "a kernel's bounded wait ran out (device error " + std::to_string(*h->h_err) + ")");
   const long long total = *h->h_total;
-  if (total > out->capacity) return set_error(h, CREC_E_RANGE, "crec_lines: capacity too small");
-  if (total > 0) {  // the characters themselves, and nothing else
-    CK(cudaMemcpyAsync(out->ids, h->dp_ids, sizeof(int32_t) * total, cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(out->frames, h->dp_frames, sizeof(int32_t) * total, cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(out->probs, h->dp_probs, sizeof(float) * total, cudaMemcpyDeviceToHost, s));
-    CK(cudaStreamSynchronize(s));
-  }
+  if ((rc = read_run(runs.back(), total, s))) return rc;
   h->st_d2h += static_cast<long long>(8 * n + 12 * total);
   h->tot_h2d += h->st_h2d;
   h->tot_d2h += h->st_d2h;
@@ -1545,6 +1638,10 @@ void free_all(crec_handle* h) {
   cudaFreeHost(h->hs_length);
   cudaFreeHost(h->hs_mask);
   cudaFreeHost(h->h_total);
+  cudaFreeHost(h->h_run_total);
+  for (cudaEvent_t e : h->ev_run) cudaEventDestroy(e);
+  if (h->read_stream) cudaStreamDestroy(h->read_stream);
+  h->pool.reset();
   cudaFree(h->dp_counts);
   cudaFree(h->dp_offsets);
   cudaFree(h->dp_ids);
@@ -1993,6 +2090,11 @@ int crec_recognize_lines(crec_handle* h, const int32_t* page_of, const crec_box*
   if (n == 0) return CREC_OK;
   CK(cudaSetDevice(h->device));
   std::vector<int> bws(n);
+  // a bucket width is a multiple of the width step and of the network's horizontal stride (a
+  // power of two): with a power-of-two step both are one mask, without a division a line
+  const int step = h->cfg.crop.width_step;
+  const bool pow2 = step > 0 && (step & (step - 1)) == 0;
+  const int mask = ((1 << h->max_shift) - 1) | (pow2 ? step - 1 : 0);
   for (int i = 0; i < n; ++i) {
     if (bw) {
       bws[i] = bw[i];
@@ -2002,7 +2104,7 @@ int crec_recognize_lines(crec_handle* h, const int32_t* page_of, const crec_box*
       crec_crop_region(&boxes[i], &h->cfg.crop, reg, &w);
       bws[i] = crec_width_bucket(w);
     }
-    if (bws[i] <= 0 || bws[i] > h->cfg.max_width || bws[i] % h->cfg.crop.width_step || bws[i] % (1 << h->max_shift))
+    if (bws[i] <= 0 || bws[i] > h->cfg.max_width || (bws[i] & mask) || (!pow2 && bws[i] % step))
       return set_error(h, CREC_E_INVALID, "recognize_lines: line " + std::to_string(i) + " bucket width " + std::to_string(bws[i]));
   }
   Source src;

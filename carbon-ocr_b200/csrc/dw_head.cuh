@@ -743,7 +743,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_ctc_kernel(const __grid_
         }
         named_bar(1, 512);
         if (e == 0) {  // read by every thread before the barrier; the next list follows the next one
-          s_count[2] += listed;
+          s_count[2] = s_count[2] + listed;
           s_count[0] = 0;
         }
       }

@@ -67,3 +67,34 @@ def test_device_memory_refused_at_open(rec_latin):
     assert e.value.code == native.E_NOMEM
     dev = native.RecDevice(rec_latin[0].to_blob(), native.INT8, max_lines=64, max_width=1024)
     dev.close()
+
+
+def test_a_large_runs_first_bad_line_is_the_error(rec_latin):
+    """A run of thousands of lines is laid out by the host pool in parts; the error reported is the
+    first failing line's, as one pass in line order reports it, and the handle goes on."""
+    pages, boxes = synth.pages(5, 1, 2480, 3508, 64)
+    n = 6000
+    bx = np.tile(np.asarray(boxes[0], np.float64), (n // 64 + 1, 1))[:n]
+    bw = np.array([native.width_bucket(native.crop_region(b)[1]) for b in bx[:64]] * (n // 64 + 1), np.int32)[:n]
+    dev = native.RecDevice(rec_latin[0].to_blob(), native.INT8, max_lines=8192, max_width=1024, max_pages=1,
+                           max_page_bytes=pages[0].size, max_columns=1 << 22)
+    try:
+        dev.set_pages(pages)
+        page_of = np.zeros(n, np.int32)
+        want = dev.recognize_lines(page_of, bx, bw, flat=True)
+        bad = page_of.copy()
+        bad[[2500, 4100, 5999]] = 3  # no page 3
+        with pytest.raises(native.CrecError) as e:
+            dev.recognize_lines(bad, bx, bw, flat=True)
+        assert e.value.code == native.E_INVALID and "line 2500:" in str(e.value)
+        narrow = bw.copy()
+        narrow[[4100, 4200]] = 32  # narrower than the line's crop
+        with pytest.raises(native.CrecError) as e:
+            dev.recognize_lines(page_of, bx, narrow, flat=True)
+        assert e.value.code == native.E_RANGE and "line 4100 " in str(e.value)
+        again = dev.recognize_lines(page_of, bx, bw, flat=True)
+        for k in ("counts", "lengths", "offsets", "ids", "frames"):
+            assert np.array_equal(again[k], want[k])
+        assert np.array_equal(again["probs"].view(np.int32), want["probs"].view(np.int32))
+    finally:
+        dev.close()
