@@ -8,6 +8,12 @@
 // copy to the device on the copy stream.  Several memcpys run at once, so the host side keeps up
 // with the bus; the copy engine sends one chunk while the workers fill the next ones.  Pages in
 // pinned (page-locked) memory skip all this: the caller copies them straight from where they are.
+//
+// A chunk is written once by its worker and then read only by the copy engine, so the workers
+// write it with streaming (non-temporal) stores: no read of each destination line into the cache
+// before it is overwritten (an ordinary memcpy's read-for-ownership), one pass over host memory
+// fewer for every byte sent, and the caches left to the page rows being read.  A store fence
+// orders a chunk's stores before its copy is queued.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -20,8 +26,45 @@
 #include <string>
 #include <thread>
 #include <vector>
+#if defined(__x86_64__) || defined(_M_X64)
+#include <emmintrin.h>
+#define CREC_STREAM_STORES 1
+#endif
 
 namespace crec {
+
+// n bytes from src to dst with streaming stores of 16 bytes where dst is 16-byte aligned (its
+// unaligned head and the tail by memcpy); a plain memcpy where the target has no such stores.
+inline void copy_streaming(uint8_t* dst, const uint8_t* src, size_t n) {
+#ifdef CREC_STREAM_STORES
+  const size_t head = std::min(n, static_cast<size_t>((16 - (reinterpret_cast<uintptr_t>(dst) & 15)) & 15));
+  std::memcpy(dst, src, head);
+  dst += head;
+  src += head;
+  n -= head;
+  size_t i = 0;
+  for (; i + 64 <= n; i += 64) {
+    const __m128i a = _mm_loadu_si128(reinterpret_cast<const __m128i*>(src + i));
+    const __m128i b = _mm_loadu_si128(reinterpret_cast<const __m128i*>(src + i + 16));
+    const __m128i c = _mm_loadu_si128(reinterpret_cast<const __m128i*>(src + i + 32));
+    const __m128i d = _mm_loadu_si128(reinterpret_cast<const __m128i*>(src + i + 48));
+    _mm_stream_si128(reinterpret_cast<__m128i*>(dst + i), a);
+    _mm_stream_si128(reinterpret_cast<__m128i*>(dst + i + 16), b);
+    _mm_stream_si128(reinterpret_cast<__m128i*>(dst + i + 32), c);
+    _mm_stream_si128(reinterpret_cast<__m128i*>(dst + i + 48), d);
+  }
+  std::memcpy(dst + i, src + i, n - i);
+#else
+  std::memcpy(dst, src, n);
+#endif
+}
+
+// the streaming stores made so far visible before a copy engine reads their chunk
+inline void stores_visible() {
+#ifdef CREC_STREAM_STORES
+  _mm_sfence();
+#endif
+}
 
 // Rows [y0, y0 + rows) of a page (`stride` bytes apart, `width` bytes each) to device memory at
 // dst, rows `width` bytes apart there.
@@ -118,11 +161,12 @@ class Stager {
         if (me.used[c] && (e = cudaEventSynchronize(me.ev[c])) != cudaSuccess) break;  // its last copy has left
         uint8_t* h = me.host[c];
         if (p.stride == p.width) {
-          std::memcpy(h, p.src, static_cast<size_t>(p.rows) * p.width);
+          copy_streaming(h, p.src, static_cast<size_t>(p.rows) * p.width);
         } else {
           for (int r = 0; r < p.rows; ++r)
-            std::memcpy(h + static_cast<size_t>(r) * p.width, p.src + static_cast<long long>(r) * p.stride, p.width);
+            copy_streaming(h + static_cast<size_t>(r) * p.width, p.src + static_cast<long long>(r) * p.stride, p.width);
         }
+        stores_visible();
         e = cudaMemcpyAsync(p.dst, h, static_cast<size_t>(p.rows) * p.width, cudaMemcpyHostToDevice, stream);
         if (e == cudaSuccess) e = cudaEventRecord(me.ev[c], stream);
         me.used[c] = true;
