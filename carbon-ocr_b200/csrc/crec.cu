@@ -48,7 +48,7 @@ constexpr bool kNoBand = true;
 constexpr size_t kGuard = 64 << 10;
 constexpr int kPoolLines = 2048;    // a run's layout goes to the host pool from this many lines
 constexpr int kOrderBuckets = 1024;  // the crop kernel's claim order: a counting sort's buckets
-constexpr int kStagerWorkers = 8;    // threads staging pageable page rows through pinned chunks
+constexpr int kStagerWorkers = 8;    // at most, threads staging pageable page rows through pinned chunks
 
 struct Value {
   int c = 0, u8 = 0, ph = 0, pw = 0, zero = 0;
@@ -1928,9 +1928,13 @@ int upload_slot(crec_handle* h, crec_handle::PageSlot& sl, const crec_page* page
     at += (static_cast<size_t>(pg.height) * pg.width + 255) / 256 * 256;
   }
   if (!staged.empty()) {
-    // 8 workers: measured on a 16-CPU B200 host with config 5's pageable pages, 4 workers with plain
-    // memcpy sent 265-271 K lines/s, 8 with streaming stores 357 K; 12-14 no more, 16 fewer
-    if (!h->stager) h->stager = std::make_unique<crec::Stager>(h->device, kStagerWorkers);
+    // 8 workers where the host has 16 CPUs or more (half of them on smaller hosts, for the caller's
+    // own threads): measured on a 16-CPU B200 host with config 5's pageable pages, 4 workers with
+    // plain memcpy sent 265-271 K lines/s, 8 with streaming stores 357 K; 12-14 no more, 16 fewer
+    if (!h->stager) {
+      const int hw = static_cast<int>(std::thread::hardware_concurrency());
+      h->stager = std::make_unique<crec::Stager>(h->device, std::clamp(hw / 2, 2, kStagerWorkers));
+    }
     if ((rc = cuda(h->stager->send(staged, h->copy_stream), "staged page upload"))) return rc;
   }
   if (n > 0 &&
