@@ -53,8 +53,16 @@ constexpr int kMaxKRows = 12;  // input rows a tile's K runs over
 struct ConvParams {
   CUtensorMap tmap[kMaxKRows];  // one per input row of a tile (3rd coordinate: the tile's row group)
   const uint8_t* wimg;  // [n tile][ky][kb][nt rows][128 bytes], each block in the 128-byte swizzle
+                        // (row stacking: [ky][kb][st_n[ky] rows][128 bytes])
   int krows, nkb, last_steps;  // input rows; K blocks of 128 bytes a row; 32-byte K steps in a row's last block
   int q_rows, cq;              // output rows a tile; its channels an output row (cq = nt when q_rows is 1)
+  // row stacking: input row i of a tile serves output rows [st_q0[i], st_q0[i] + st_n[i] / cq), so
+  // its stages load those rows' weights only (st_n[i] rows of 128 bytes a K block, from byte
+  // st_off[i] of wimg) and its MMAs write those rows' accumulator columns; bit i of st_first: input
+  // row i is the first an output row reads (its kb 0 starts that row's sum)
+  int st_q0[kMaxKRows], st_n[kMaxKRows];
+  uint32_t st_off[kMaxKRows];
+  uint32_t st_first;
   int cq_inv;                  // ceil(65536 / (cq / 16)): a group g's output row is (g * cq_inv) >> 16 (exact for g < 16)
   int nt, n_tiles;          // output channels a tile (multiple of 16, <= 256), tiles across the channels
   int oh, ow, m_per_row, num_tiles;
@@ -291,10 +299,12 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
           if (leader) {
             uint8_t* a = smem + stage * p.stage_bytes;
             uint8_t* b = a + p.a_bytes;
-            mbar_expect_tx(&full[stage], p.a_bytes + p.b_bytes);
+            const uint32_t bb = kStack ? static_cast<uint32_t>(p.st_n[ky]) * 128u : p.b_bytes;
+            mbar_expect_tx(&full[stage], p.a_bytes + bb);
             tma_load_3d(a, &p.tmap[ky], kb * 128, ox0, oy, &full[stage]);
-            const uint8_t* w = p.wimg + (static_cast<size_t>((n * p.krows + ky) * p.nkb + kb)) * p.b_bytes;
-            bulk_load(b, w, p.b_bytes, &full[stage]);
+            const uint8_t* w = kStack ? p.wimg + p.st_off[ky] + static_cast<size_t>(kb) * bb
+                                      : p.wimg + (static_cast<size_t>((n * p.krows + ky) * p.nkb + kb)) * p.b_bytes;
+            bulk_load(b, w, bb, &full[stage]);
           }
           __syncwarp();
           if (++stage == p.stages) {
@@ -327,7 +337,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
       tc_fence_after();
       const uint32_t d = tmem + static_cast<uint32_t>(acc) * acc_cols;
       uint32_t accumulate = 0;
-      int kb = 0;
+      int kb = 0, ky = 0;
       for (int ks = 0; ks < ksteps_per_tile; ++ks) {
         if (!mbar_wait_warp(&full[stage], phase, p.err, kErrTimeoutFull, p.wait_ns)) {
           ok = false;
@@ -336,9 +346,37 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
         tc_fence_after();
         const uint64_t ad = a_desc0 + static_cast<uint64_t>(stage) * stage_step;
         const uint64_t bd = b_desc0 + static_cast<uint64_t>(stage) * stage_step;
+        const int kb_now = kb, ky_now = ky;
         const int steps = ++kb == p.nkb ? p.last_steps : 4;
-        if (kb == p.nkb) kb = 0;
-        if (leader) {
+        if (kb == p.nkb) {
+          kb = 0;
+          ++ky;
+        }
+        if constexpr (kStack) {
+          // the output rows this input row serves: one MMA over their columns, except at the first
+          // K step of the row that starts here, where that row's MMA begins its sum (accumulate 0)
+          // beside the earlier rows' (accumulate 1); B's rows are the served rows' in order, so the
+          // new row's are the last cq (whole 8-row groups: the swizzle is unchanged)
+          const int nq = p.st_n[ky_now];
+          const uint32_t dq = d + static_cast<uint32_t>(p.st_q0[ky_now] * p.cq);
+          const uint32_t id = kInt8 ? idesc_i8(nq) : idesc_f16(nq);
+          const bool starts = kb_now == 0 && ((p.st_first >> ky_now) & 1u);
+          const int nold = nq - p.cq;
+          if (leader) {
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+              if (s >= steps) continue;
+              if (s == 0 && starts) {
+                if (nold > 0) umma<kInt8>(dq, ad, bd, kInt8 ? idesc_i8(nold) : idesc_f16(nold), 1u);
+                umma<kInt8>(dq + static_cast<uint32_t>(nold), ad, bd + static_cast<uint64_t>((nold * 128) >> 4),
+                            kInt8 ? idesc_i8(p.cq) : idesc_f16(p.cq), 0u);
+              } else {
+                umma<kInt8>(dq, ad + 2 * s, bd + 2 * s, id, 1u);
+              }
+            }
+            umma_commit(&empty[stage]);
+          }
+        } else if (leader) {
 #pragma unroll
           for (int s = 0; s < 4; ++s)
             if (s < steps) umma<kInt8>(d, ad + 2 * s, bd + 2 * s, idesc, accumulate | static_cast<uint32_t>(s));

@@ -84,6 +84,9 @@ struct Layer {
   bool sat = false;         // INT8 conv: |v * inv_scale| < 2^21 always (round, then clamp while packing)
   int nkb = 0, last_steps = 0, nt = 0, n_tiles = 0, stages = 0, nchunk = 0, chunks = 0;
   int krows = 0, q_rows = 1, cq = 0;  // dense convs: input rows a tile reads, output rows it stacks, channels a row
+  // row stacking (ConvParams::st_*): the output rows input row i serves, its weight block's offset
+  int st_q0[kMaxKRows] = {}, st_n[kMaxKRows] = {};
+  uint32_t st_off[kMaxKRows] = {}, st_first = 0;
   uint32_t stage_bytes = 0, a_bytes = 0, b_bytes = 0, smem = 0;
   // band mode (conv_gemm.cuh): channel-plane ring slots, resident weights
   bool band = false;
@@ -746,7 +749,25 @@ int setup_layer(crec_handle* h, size_t li) {
       }
     }
   }
-  const std::vector<uint8_t> img = weight_image(h, l, x.cp, l.nt, l.n_tiles, l.nkb);
+  std::vector<uint8_t> img = weight_image(h, l, x.cp, l.nt, l.n_tiles, l.nkb);
+  if (l.q_rows > 1) {
+    // row stacking: input row i serves output rows q with 0 <= i - q * sh < kh; its blocks keep
+    // those rows' weights only (the others are zeros), in whole 16-row groups, so the swizzle holds
+    std::vector<uint8_t> packed;
+    l.st_first = 0;
+    for (int i = 0; i < l.krows; ++i) {
+      const int q0 = i < l.kh ? 0 : (i - l.kh + l.sh) / l.sh, q1 = std::min(l.q_rows - 1, i / l.sh);
+      l.st_q0[i] = q0;
+      l.st_n[i] = (q1 - q0 + 1) * l.cq;
+      l.st_off[i] = static_cast<uint32_t>(packed.size());
+      if (i % l.sh == 0 && i / l.sh < l.q_rows) l.st_first |= 1u << i;
+      for (int kb = 0; kb < l.nkb; ++kb) {
+        const uint8_t* blk = img.data() + (static_cast<size_t>(i) * l.nkb + kb) * l.nt * 128;
+        packed.insert(packed.end(), blk + static_cast<size_t>(q0) * l.cq * 128, blk + static_cast<size_t>(q1 + 1) * l.cq * 128);
+      }
+    }
+    img.swap(packed);
+  }
   if ((rc = upload(h, &l.wimg, img))) return rc;
   return CREC_OK;
 }
@@ -914,6 +935,12 @@ int launch_conv(crec_handle* h, size_t li, long long cols) {
   p.wimg = l.wimg;
   p.krows = l.krows;
   p.q_rows = l.q_rows;
+  for (int i = 0; i < l.krows; ++i) {
+    p.st_q0[i] = l.st_q0[i];
+    p.st_n[i] = l.st_n[i];
+    p.st_off[i] = l.st_off[i];
+  }
+  p.st_first = l.st_first;
   p.cq = l.cq;
   p.cq_inv = (65536 + l.cq / 16 - 1) / (l.cq / 16);
   p.nkb = l.nkb;
