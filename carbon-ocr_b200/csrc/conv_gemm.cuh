@@ -52,8 +52,15 @@ constexpr int kMaxKRows = 12;  // input rows a tile's K runs over
 // zeros where an output row does not read an input row.
 struct ConvParams {
   CUtensorMap tmap[kMaxKRows];  // one per input row of a tile (3rd coordinate: the tile's row group)
+  // a window's last K block when it holds 32 or 64 bytes (tail_bytes; else 128): boxes that wide in
+  // the 32- or 64-byte swizzle, the weights' block rows that wide too, so the block's loads carry
+  // no padding
+  CUtensorMap tmap_tail[kMaxKRows];
+  int tail_bytes;
+  uint32_t row_bytes;  // without row stacking: an input row's weight blocks, (nkb - 1) * b_bytes + nt * tail_bytes
   const uint8_t* wimg;  // [n tile][ky][kb][nt rows][128 bytes], each block in the 128-byte swizzle
-                        // (row stacking: [ky][kb][st_n[ky] rows][128 bytes])
+                        // (row stacking: [ky][kb][st_n[ky] rows][128 bytes]); the last kb's rows
+                        // tail_bytes wide in their swizzle
   int krows, nkb, last_steps;  // input rows; K blocks of 128 bytes a row; 32-byte K steps in a row's last block
   int q_rows, cq;              // output rows a tile; its channels an output row (cq = nt when q_rows is 1)
   // row stacking: input row i of a tile serves output rows [st_q0[i], st_q0[i] + st_n[i] / cq), so
@@ -104,6 +111,8 @@ struct ConvParams {
   uint32_t w_bytes;            // the resident weight image
   int row0;                    // the input's border rows less the layer's top padding: band row i is map row i + row0
 };
+
+static_assert(sizeof(ConvParams) <= 4096, "conv kernel parameters within the classic 4 KB");
 
 constexpr int kConvThreads = 576;
 constexpr int kMaxAcc = 8;
@@ -299,11 +308,15 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
           if (leader) {
             uint8_t* a = smem + stage * p.stage_bytes;
             uint8_t* b = a + p.a_bytes;
-            const uint32_t bb = kStack ? static_cast<uint32_t>(p.st_n[ky]) * 128u : p.b_bytes;
-            mbar_expect_tx(&full[stage], p.a_bytes + bb);
-            tma_load_3d(a, &p.tmap[ky], kb * 128, ox0, oy, &full[stage]);
-            const uint8_t* w = kStack ? p.wimg + p.st_off[ky] + static_cast<size_t>(kb) * bb
-                                      : p.wimg + (static_cast<size_t>((n * p.krows + ky) * p.nkb + kb)) * p.b_bytes;
+            const bool tail = kb == p.nkb - 1 && p.tail_bytes < 128;
+            const uint32_t pitch = tail ? static_cast<uint32_t>(p.tail_bytes) : 128u;  // a block row's bytes
+            const uint32_t rows = kStack ? static_cast<uint32_t>(p.st_n[ky]) : static_cast<uint32_t>(p.nt);
+            const uint32_t ab = 128u * pitch, bb = rows * pitch;
+            mbar_expect_tx(&full[stage], ab + bb);
+            tma_load_3d(a, tail ? &p.tmap_tail[ky] : &p.tmap[ky], kb * 128, ox0, oy, &full[stage]);
+            const uint8_t* w = kStack ? p.wimg + p.st_off[ky] + static_cast<size_t>(kb) * rows * 128u
+                                      : p.wimg + static_cast<size_t>(n * p.krows + ky) * p.row_bytes +
+                                            static_cast<size_t>(kb) * p.b_bytes;
             bulk_load(b, w, bb, &full[stage]);
           }
           __syncwarp();
@@ -325,6 +338,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
     // the stages' descriptors differ only in the start address (bits 0..13, address >> 4): a
     // K step of 32 bytes adds 2, a stage stage_bytes >> 4
     const uint64_t a_desc0 = umma_desc_sw128(smem_u32(smem)), b_desc0 = umma_desc_sw128(smem_u32(smem) + p.a_bytes);
+    const bool narrow = p.tail_bytes < 128;
+    const uint32_t tail_row = narrow ? static_cast<uint32_t>(p.tail_bytes) : 128u;
+    const uint64_t a_tail0 = narrow ? umma_desc_narrow(smem_u32(smem), tail_row) : a_desc0;
+    const uint64_t b_tail0 = narrow ? umma_desc_narrow(smem_u32(smem) + p.a_bytes, tail_row) : b_desc0;
     const uint32_t stage_step = p.stage_bytes >> 4;
     int stage = 0;
     uint32_t phase = 0;
@@ -344,9 +361,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
           break;
         }
         tc_fence_after();
-        const uint64_t ad = a_desc0 + static_cast<uint64_t>(stage) * stage_step;
-        const uint64_t bd = b_desc0 + static_cast<uint64_t>(stage) * stage_step;
         const int kb_now = kb, ky_now = ky;
+        const bool tail = narrow && kb_now == p.nkb - 1;
+        const uint64_t ad = (tail ? a_tail0 : a_desc0) + static_cast<uint64_t>(stage) * stage_step;
+        const uint64_t bd = (tail ? b_tail0 : b_desc0) + static_cast<uint64_t>(stage) * stage_step;
         const int steps = ++kb == p.nkb ? p.last_steps : 4;
         if (kb == p.nkb) {
           kb = 0;
@@ -368,7 +386,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_gemm_kernel(const __grid
               if (s >= steps) continue;
               if (s == 0 && starts) {
                 if (nold > 0) umma<kInt8>(dq, ad, bd, kInt8 ? idesc_i8(nold) : idesc_f16(nold), 1u);
-                umma<kInt8>(dq + static_cast<uint32_t>(nold), ad, bd + static_cast<uint64_t>((nold * 128) >> 4),
+                const uint32_t pitch = tail ? tail_row : 128u;
+                umma<kInt8>(dq + static_cast<uint32_t>(nold), ad, bd + static_cast<uint64_t>((static_cast<uint32_t>(nold) * pitch) >> 4),
                             kInt8 ? idesc_i8(p.cq) : idesc_f16(p.cq), 0u);
               } else {
                 umma<kInt8>(dq, ad + 2 * s, bd + 2 * s, id, 1u);

@@ -87,6 +87,8 @@ struct Layer {
   // row stacking (ConvParams::st_*): the output rows input row i serves, its weight block's offset
   int st_q0[kMaxKRows] = {}, st_n[kMaxKRows] = {};
   uint32_t st_off[kMaxKRows] = {}, st_first = 0;
+  int tail = 128;           // the last K block's row bytes (ConvParams::tail_bytes)
+  uint32_t row_bytes = 0;   // without row stacking: an input row's weight blocks (ConvParams::row_bytes)
   uint32_t stage_bytes = 0, a_bytes = 0, b_bytes = 0, smem = 0;
   // band mode (conv_gemm.cuh): channel-plane ring slots, resident weights
   bool band = false;
@@ -465,6 +467,13 @@ int plan_model(crec_handle* h) {
 
 // The 128-byte swizzle of a K-major operand block: byte b of row j.
 inline size_t swz(int j, int b) { return static_cast<size_t>(j) * 128 + (((b >> 4) ^ (j & 7)) << 4) + (b & 15); }
+// Byte b of row j of a K-major block whose rows are `pitch` bytes (128, 64 or 32) in that width's
+// swizzle: the 16-byte chunk index XOR the row's bits above the atom's (Swizzle<3|2|1, 4, 3>).
+inline size_t swz_pitch(int j, int b, int pitch) {
+  const int chunks = pitch / 16, mask = chunks - 1;
+  const int shift = pitch == 128 ? 0 : pitch == 64 ? 1 : 2;
+  return static_cast<size_t>(j) * pitch + ((((b >> 4) ^ (j >> shift)) & mask) << 4) + (b & 15);
+}
 
 // A dense layer's (or the head's) weights as the swizzled image the kernels bulk-copy:
 // [n tile][ky][kb][nt rows][128 bytes]; byte `off` of kernel row ky's window is (kx, channel, byte).
@@ -472,17 +481,19 @@ std::vector<uint8_t> weight_image(const crec_handle* h, const Layer& l, int cp_i
   const int eb = h->eb, taps = l.kh * l.kw, window = l.kw * cp_in * eb;
   // blocks [n tile][input row i][kb]; tile column j is output row q = j / cq of the tile's
   // stacked rows, channel co; it reads input row i through kernel row i - q * sh (zeros where
-  // that is outside the kernel)
-  std::vector<uint8_t> img(static_cast<size_t>(n_tiles) * l.krows * nkb * nt * 128, 0);
+  // that is outside the kernel).  A block has nt rows of 128 bytes, the last kb's of l.tail.
+  const size_t row_bytes = static_cast<size_t>(nkb - 1) * nt * 128 + static_cast<size_t>(nt) * l.tail;
+  std::vector<uint8_t> img(static_cast<size_t>(n_tiles) * l.krows * row_bytes, 0);
   for (int n = 0; n < n_tiles; ++n)
     for (int i = 0; i < l.krows; ++i)
       for (int kb = 0; kb < nkb; ++kb) {
-        uint8_t* blk = img.data() + (static_cast<size_t>((n * l.krows + i) * nkb + kb)) * nt * 128;
+        uint8_t* blk = img.data() + static_cast<size_t>(n * l.krows + i) * row_bytes + static_cast<size_t>(kb) * nt * 128;
+        const int pitch = kb == nkb - 1 ? l.tail : 128;
         for (int j = 0; j < nt; ++j) {
           const int q = l.q_rows > 1 ? j / l.cq : 0;
           const int co = n * nt + j - q * l.cq, ky = i - q * l.sh;
           if (co >= l.cout || ky < 0 || ky >= l.kh) continue;
-          for (int b = 0; b < 128; ++b) {
+          for (int b = 0; b < pitch; ++b) {
             const int off = kb * 128 + b;
             if (off >= window) break;
             const int kx = off / (cp_in * eb), rem = off % (cp_in * eb), c = rem / eb, byte = rem % eb;
@@ -495,7 +506,7 @@ std::vector<uint8_t> weight_image(const crec_handle* h, const Layer& l, int cp_i
               const uint16_t hb = half_bits(l.wf[wi]);
               val = static_cast<uint8_t>(byte ? hb >> 8 : hb & 0xff);
             }
-            blk[swz(j, b)] = val;
+            blk[swz_pitch(j, b, pitch)] = val;
           }
         }
       }
@@ -697,8 +708,26 @@ int setup_layer(crec_handle* h, size_t li) {
     if (l.q_rows > 1) l.n_tiles = 1;
     l.a_bytes = 16384;
     l.b_bytes = static_cast<uint32_t>(l.nt) * 128;
+    // a window's last K block of one or two 32-byte steps: boxes and weight rows that wide
+    l.tail = l.last_steps <= 2 ? 32 * l.last_steps : 128;
+    l.row_bytes = static_cast<uint32_t>(l.nkb - 1) * l.b_bytes + static_cast<uint32_t>(l.nt * l.tail);
+    if (l.q_rows > 1) {
+      // row stacking: input row i serves output rows q with 0 <= i - q * sh < kh, so its stages
+      // carry those rows' weights only; a stage holds the most any input row needs
+      int most = 0;
+      l.st_first = 0;
+      for (int i = 0; i < l.krows; ++i) {
+        const int q0 = i < l.kh ? 0 : (i - l.kh + l.sh) / l.sh, q1 = std::min(l.q_rows - 1, i / l.sh);
+        l.st_q0[i] = q0;
+        l.st_n[i] = (q1 - q0 + 1) * l.cq;
+        most = std::max(most, l.st_n[i]);
+        if (i % l.sh == 0 && i / l.sh < l.q_rows) l.st_first |= 1u << i;
+      }
+      l.b_bytes = static_cast<uint32_t>(most) * 128;
+    }
     l.stage_bytes = l.a_bytes + l.b_bytes;
-    l.stages = std::min<int>(8, (200 * 1024) / l.stage_bytes);
+    // stacked layers' stages are smaller: a deeper ring in a little more of the shared memory
+    l.stages = std::min<int>(8, ((l.q_rows > 1 ? 216 : 200) * 1024) / l.stage_bytes);
     l.smem = 1024 + l.stages * l.stage_bytes + (2 * l.stages + 2 * kMaxAcc + 2) * 8 + 16 + 12 * y.cp + 64;
     if (h->int8 && (rc = upload_offsets(h, l, x.zero, colsum, y.cp))) return rc;
     if (h->int8) l.sat = round_first(h, l, x, y, scale, bias);
@@ -751,19 +780,16 @@ int setup_layer(crec_handle* h, size_t li) {
   }
   std::vector<uint8_t> img = weight_image(h, l, x.cp, l.nt, l.n_tiles, l.nkb);
   if (l.q_rows > 1) {
-    // row stacking: input row i serves output rows q with 0 <= i - q * sh < kh; its blocks keep
-    // those rows' weights only (the others are zeros), in whole 16-row groups, so the swizzle holds
+    // row stacking: input row i's blocks keep the weights of the output rows it serves only (the
+    // others are zeros), in whole 16-row groups, so the swizzle holds
     std::vector<uint8_t> packed;
-    l.st_first = 0;
     for (int i = 0; i < l.krows; ++i) {
-      const int q0 = i < l.kh ? 0 : (i - l.kh + l.sh) / l.sh, q1 = std::min(l.q_rows - 1, i / l.sh);
-      l.st_q0[i] = q0;
-      l.st_n[i] = (q1 - q0 + 1) * l.cq;
+      const int q0 = l.st_q0[i], q1 = q0 + l.st_n[i] / l.cq - 1;
       l.st_off[i] = static_cast<uint32_t>(packed.size());
-      if (i % l.sh == 0 && i / l.sh < l.q_rows) l.st_first |= 1u << i;
       for (int kb = 0; kb < l.nkb; ++kb) {
-        const uint8_t* blk = img.data() + (static_cast<size_t>(i) * l.nkb + kb) * l.nt * 128;
-        packed.insert(packed.end(), blk + static_cast<size_t>(q0) * l.cq * 128, blk + static_cast<size_t>(q1 + 1) * l.cq * 128);
+        const size_t pitch = kb == l.nkb - 1 ? static_cast<size_t>(l.tail) : 128;
+        const uint8_t* blk = img.data() + static_cast<size_t>(i) * l.row_bytes + static_cast<size_t>(kb) * l.nt * 128;
+        packed.insert(packed.end(), blk + static_cast<size_t>(q0) * l.cq * pitch, blk + static_cast<size_t>(q1 + 1) * l.cq * pitch);
       }
     }
     img.swap(packed);
@@ -787,14 +813,17 @@ int alloc_values(crec_handle* h) {
 }
 
 int encode_map(crec_handle* h, CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
-               uint64_t s2) {
+               uint64_t s2, uint32_t inner = 128) {
   const cuuint64_t dims[3] = {d0, d1, d2};
   const cuuint64_t strides[2] = {s1, s2};
-  const cuuint32_t box[3] = {128, 128, 1};
+  const cuuint32_t box[3] = {inner, 128, 1};  // inner bytes (128, 64 or 32) in that width's swizzle
   const cuuint32_t es[3] = {1, 1, 1};
+  const CUtensorMapSwizzle sw = inner == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : inner == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_32B;
   const CUresult r = h->encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
-                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(h, CREC_E_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
   return CREC_OK;
 }
@@ -930,8 +959,14 @@ int launch_conv(crec_handle* h, size_t li, long long cols) {
     int rc = encode_map(h, &p.tmap[i], base, static_cast<uint64_t>(l.nkb) * 128, static_cast<uint64_t>(ow),
                         static_cast<uint64_t>(oh / l.q_rows), static_cast<uint64_t>(l.sw) * px,
                         static_cast<uint64_t>(l.q_rows) * l.sh * in_pitch);
+    if (!rc && l.tail < 128)
+      rc = encode_map(h, &p.tmap_tail[i], base, static_cast<uint64_t>(l.nkb) * 128, static_cast<uint64_t>(ow),
+                      static_cast<uint64_t>(oh / l.q_rows), static_cast<uint64_t>(l.sw) * px,
+                      static_cast<uint64_t>(l.q_rows) * l.sh * in_pitch, static_cast<uint32_t>(l.tail));
     if (rc) return rc;
   }
+  p.tail_bytes = l.band ? 128 : l.tail;
+  p.row_bytes = l.row_bytes;
   p.wimg = l.wimg;
   p.krows = l.krows;
   p.q_rows = l.q_rows;

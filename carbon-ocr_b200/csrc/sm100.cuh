@@ -175,6 +175,18 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
   return d;
 }
 
+// K-major operand in the 64- or 32-byte swizzle (layout types 4 and 6 of the descriptor's 3-bit
+// field; 2 is the 128-byte one): rows of `row` bytes (64 or 32), 8-row atoms 8 * row bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_narrow(uint32_t addr, uint32_t row) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;                     // leading byte offset (unused by K-major swizzled)
+  d |= static_cast<uint64_t>(((8u * row) >> 4) & 0x3FFFu) << 32;  // stride byte offset: 8 rows
+  d |= static_cast<uint64_t>(1u) << 46;                     // version (sm_100)
+  d |= static_cast<uint64_t>(row == 64 ? 4u : 6u) << 61;    // SWIZZLE_64B or SWIZZLE_32B
+  return d;
+}
+
 // K-major operand without swizzle: 8-row core matrices of 16 bytes (128 contiguous bytes each);
 // `lbo` the byte step between core matrices along K, `sbo` along M (or N) -- checked on the GPU
 // against a host product, both ways round (only this reading gives it).
