@@ -780,44 +780,54 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
   }
   __syncthreads();
 
-  // the stem, into the line's segment of the stem tensor: a thread an output pixel and all its channels
+  // the stem, into the line's segment of the stem tensor: a thread two output pixels, (oy, ox) and
+  // (oy + 1, ox), and all their channels; INT8: each weight and per-channel constant read from
+  // shared memory serves both (the pixels' arithmetic is each its own, as for one pixel alone)
   const int oh = (H + 2 * p.pt - p.kh) / p.sh + 1, ow = (bw + 2 * p.pl - p.kw) / p.sw + 1;
+  const int ph = (oh + 1) >> 1;  // pixel pairs down a column
   const long long col0 = static_cast<long long>(L.seg) >> p.out_shift;
   const int eb = kInt8 ? 1 : 2;
   const float lo = p.relu ? 0.0f : static_cast<float>(-p.out_zero), hi = static_cast<float>(255 - p.out_zero);
   const int32_t zc = p.out_zero - kMagicBits;
   const bool windows = kInt8 && p.kh <= 3 && p.kw <= 4 && p.pt >= 0 && p.pt <= 2 && p.pl >= 0 && p.pl <= 4;
-  // pixel i = tid + k * nthr as (oy, ox), advanced without a division a step
+  // pair i = tid + k * nthr as (pair row, ox), advanced without a division a step
   const int step_y = nthr / ow, step_x = nthr - step_y * ow;
-  int oy = tid / ow, ox = tid - oy * ow;
-  for (int i = tid; i < oh * ow; i += nthr, oy += step_y, ox += step_x) {
+  int py = tid / ow, ox = tid - py * ow;
+  for (int i = tid; i < ph * ow; i += nthr, py += step_y, ox += step_x) {
     if (ox >= ow) {
       ox -= ow;
-      ++oy;
+      ++py;
     }
+    const int oy = 2 * py;
+    const bool two = oy + 1 < oh;  // the pair's second pixel exists
     uint8_t* dst = p.out + (oy + p.out_ph) * p.out_pitch + (col0 + ox) * p.cp_out * eb;
+    uint8_t* dst1 = dst + p.out_pitch;
     if constexpr (kInt8) {
       // a kernel row's taps, 4 bytes a word (past kw: anything, the weights there are 0); the
       // border reads the zero point: real zero
-      uint32_t a[3] = {0, 0, 0};
-      if (windows) {
-        const int cs = ox * p.sw - p.pl + 4, rs = oy * p.sh - p.pt + 2;
-        const int al = cs & ~3;
-        const uint32_t sel = 0x3210u + static_cast<uint32_t>(cs & 3) * 0x1111u;
+      uint32_t a[2][3] = {{0, 0, 0}, {0, 0, 0}};
 #pragma unroll
-        for (int ky = 0; ky < 3; ++ky) {
-          if (ky < p.kh) {
-            const uint8_t* rp = qb + (rs + ky) * qpitch + al;
-            a[ky] = __byte_perm(*reinterpret_cast<const uint32_t*>(rp), *reinterpret_cast<const uint32_t*>(rp + 4), sel);
+      for (int e = 0; e < 2; ++e) {
+        const int y0 = oy + e;
+        if (windows) {
+          const int cs = ox * p.sw - p.pl + 4, rs = y0 * p.sh - p.pt + 2;
+          const int al = cs & ~3;
+          const uint32_t sel = 0x3210u + static_cast<uint32_t>(cs & 3) * 0x1111u;
+#pragma unroll
+          for (int ky = 0; ky < 3; ++ky) {
+            if (ky < p.kh && (e == 0 || two)) {
+              const uint8_t* rp = qb + (rs + ky) * qpitch + al;
+              a[e][ky] = __byte_perm(*reinterpret_cast<const uint32_t*>(rp), *reinterpret_cast<const uint32_t*>(rp + 4), sel);
+            }
           }
+        } else if (e == 0 || two) {
+          for (int ky = 0; ky < p.kh && ky < 3; ++ky)
+            for (int kx = 0; kx < p.kw && kx < 4; ++kx) {
+              const int y = y0 * p.sh - p.pt + ky, x = ox * p.sw - p.pl + kx;
+              const uint32_t q = (y >= 0 && y < H && x >= 0 && x < bw) ? px(y, x) : static_cast<uint32_t>(p.in_zero);
+              a[e][ky] |= q << (8 * kx);
+            }
         }
-      } else {
-        for (int ky = 0; ky < p.kh && ky < 3; ++ky)
-          for (int kx = 0; kx < p.kw && kx < 4; ++kx) {
-            const int y = oy * p.sh - p.pt + ky, x = ox * p.sw - p.pl + kx;
-            const uint32_t q = (y >= 0 && y < H && x >= 0 && x < bw) ? px(y, x) : static_cast<uint32_t>(p.in_zero);
-            a[ky] |= q << (8 * kx);
-          }
       }
       // sum over taps of (a - zero) * w = dp4a(a, w) - zero * colsum, exact in int32; then the
       // output stage with exact conversions (kMagic), rounded before the clamp where the host's
@@ -825,7 +835,7 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
       auto channels = [&](auto round_first) {
       constexpr bool kRound = decltype(round_first)::value;
       for (int c16 = 0; c16 < p.cp_out; c16 += 16) {
-        uint32_t wv[4];
+        uint32_t wv[2][4];
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           const int j = c16 + 4 * c4;
@@ -837,77 +847,85 @@ __global__ void __launch_bounds__(kCropThreads, 2) crop_stem_kernel(const __grid
           const float4 b4 = *reinterpret_cast<const float4*>(sbias + j);
           const int32_t oo[4] = {o4.x, o4.y, o4.z, o4.w};
           const float ss[4] = {s4.x, s4.y, s4.z, s4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
-          int32_t code[4], acc[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            acc[u] = dp4a_us(a[0], w[3 * u], oo[u]);
-            acc[u] = dp4a_us(a[1], w[3 * u + 1], acc[u]);
-            acc[u] = dp4a_us(a[2], w[3 * u + 2], acc[u]);
-          }
+          for (int e = 0; e < 2; ++e) {
+            int32_t code[4], acc[4];
 #pragma unroll
-          for (int u = 0; u < 4; u += 2) {  // two channels at a time on the packed FP32 pipe
-            float2 q = out_stage2(acc[u], acc[u + 1], make_float2(ss[u], ss[u + 1]), make_float2(bb[u], bb[u + 1]),
-                                  p.out_inv_scale);
-            if (!kRound) {
-              q.x = fminf(fmaxf(q.x, lo), hi);
-              q.y = fminf(fmaxf(q.y, lo), hi);
+            for (int u = 0; u < 4; ++u) {
+              acc[u] = dp4a_us(a[e][0], w[3 * u], oo[u]);
+              acc[u] = dp4a_us(a[e][1], w[3 * u + 1], acc[u]);
+              acc[u] = dp4a_us(a[e][2], w[3 * u + 2], acc[u]);
             }
-            int32_t t0, t1;
-            magic_rint_bits2(q, t0, t1);
-            code[u] = t0 + zc;
-            code[u + 1] = t1 + zc;
+#pragma unroll
+            for (int u = 0; u < 4; u += 2) {  // two channels at a time on the packed FP32 pipe
+              float2 q = out_stage2(acc[u], acc[u + 1], make_float2(ss[u], ss[u + 1]), make_float2(bb[u], bb[u + 1]),
+                                    p.out_inv_scale);
+              if (!kRound) {
+                q.x = fminf(fmaxf(q.x, lo), hi);
+                q.y = fminf(fmaxf(q.y, lo), hi);
+              }
+              int32_t t0, t1;
+              magic_rint_bits2(q, t0, t1);
+              code[u] = t0 + zc;
+              code[u + 1] = t1 + zc;
+            }
+            wv[e][c4] = pack_sat_u8x4(code);
           }
-          wv[c4] = pack_sat_u8x4(code);
         }
-        *reinterpret_cast<uint4*>(dst + c16) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        *reinterpret_cast<uint4*>(dst + c16) = make_uint4(wv[0][0], wv[0][1], wv[0][2], wv[0][3]);
+        if (two) *reinterpret_cast<uint4*>(dst1 + c16) = make_uint4(wv[1][0], wv[1][1], wv[1][2], wv[1][3]);
       }
       };
       if (p.sat) channels(std::true_type{});
       else channels(std::false_type{});
     } else {
-      float in[9];
-#pragma unroll
-      for (int t = 0; t < 9; ++t) {
-        in[t] = 0.0f;
-        if (t >= taps_stem) continue;
-        const int y = oy * p.sh - p.pt + t / p.kw, x = ox * p.sw - p.pl + t % p.kw;
-        if (y < 0 || y >= H || x < 0 || x >= bw) continue;  // the border: real zero
-        in[t] = ftab[px(y, x)];
-      }
-      // 16 channels as 8 pairs: an fma chain over the taps in tap order from 0 on the packed
-      // FP32 pipe (the FP16 engine is graded by tolerance), + bias, ReLU, to FP16
-      for (int c0 = 0; c0 < p.cp_out; c0 += 16) {
-        float2 acc[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = make_float2(0.0f, 0.0f);
+      // each pixel of the pair on its own: 16 channels as 8 pairs, an fma chain over the taps in tap
+      // order from 0 on the packed FP32 pipe (the FP16 engine is graded by tolerance), + bias,
+      // ReLU, to FP16 (pairing the pixels as INT8 does was slower here: more registers, narrower stores)
+      for (int e = 0; e < (two ? 2 : 1); ++e) {
+        float in[9];
 #pragma unroll
         for (int t = 0; t < 9; ++t) {
-          if (t >= taps_stem) break;
-          const float2 x2 = make_float2(in[t], in[t]);
-          const float4* w4 = reinterpret_cast<const float4*>(swf + t * kStemMaxOut + c0);
+          in[t] = 0.0f;
+          if (t >= taps_stem) continue;
+          const int y = (oy + e) * p.sh - p.pt + t / p.kw, x = ox * p.sw - p.pl + t % p.kw;
+          if (y < 0 || y >= H || x < 0 || x >= bw) continue;  // the border: real zero
+          in[t] = ftab[px(y, x)];
+        }
+        uint8_t* d = e ? dst1 : dst;
+        for (int c0 = 0; c0 < p.cp_out; c0 += 16) {
+          float2 acc[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] = make_float2(0.0f, 0.0f);
+#pragma unroll
+          for (int t = 0; t < 9; ++t) {
+            if (t >= taps_stem) break;
+            const float2 x2 = make_float2(in[t], in[t]);
+            const float4* w4 = reinterpret_cast<const float4*>(swf + t * kStemMaxOut + c0);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float4 w = w4[k];
+              acc[2 * k] = __ffma2_rn(x2, make_float2(w.x, w.y), acc[2 * k]);
+              acc[2 * k + 1] = __ffma2_rn(x2, make_float2(w.z, w.w), acc[2 * k + 1]);
+            }
+          }
+          alignas(16) __half2 o[8];
+          const float4* b4 = reinterpret_cast<const float4*>(sbias + c0);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const float4 w = w4[k];
-            acc[2 * k] = __ffma2_rn(x2, make_float2(w.x, w.y), acc[2 * k]);
-            acc[2 * k + 1] = __ffma2_rn(x2, make_float2(w.z, w.w), acc[2 * k + 1]);
-          }
-        }
-        alignas(16) __half2 o[8];
-        const float4* b4 = reinterpret_cast<const float4*>(sbias + c0);
+            const float4 b = b4[k];
+            float v[4] = {__fadd_rn(acc[2 * k].x, b.x), __fadd_rn(acc[2 * k].y, b.y), __fadd_rn(acc[2 * k + 1].x, b.z),
+                          __fadd_rn(acc[2 * k + 1].y, b.w)};
+            if (p.relu) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float4 b = b4[k];
-          float v[4] = {__fadd_rn(acc[2 * k].x, b.x), __fadd_rn(acc[2 * k].y, b.y), __fadd_rn(acc[2 * k + 1].x, b.z),
-                        __fadd_rn(acc[2 * k + 1].y, b.w)};
-          if (p.relu) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) v[u] = v[u] > 0.0f ? v[u] : 0.0f;
+              for (int u = 0; u < 4; ++u) v[u] = v[u] > 0.0f ? v[u] : 0.0f;
+            }
+            o[2 * k] = __floats2half2_rn(v[0], v[1]);
+            o[2 * k + 1] = __floats2half2_rn(v[2], v[3]);
           }
-          o[2 * k] = __floats2half2_rn(v[0], v[1]);
-          o[2 * k + 1] = __floats2half2_rn(v[2], v[3]);
+          *reinterpret_cast<uint4*>(d + c0 * 2) = *reinterpret_cast<const uint4*>(o);
+          *reinterpret_cast<uint4*>(d + c0 * 2 + 16) = *reinterpret_cast<const uint4*>(o + 4);
         }
-        *reinterpret_cast<uint4*>(dst + c0 * 2) = *reinterpret_cast<const uint4*>(o);
-        *reinterpret_cast<uint4*>(dst + c0 * 2 + 16) = *reinterpret_cast<const uint4*>(o + 4);
       }
     }
   }
