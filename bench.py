@@ -131,10 +131,10 @@ def reduce_sum(v: float, world: int, device: str) -> float:
 
 
 # measured by ncu: dram__bytes_read.sum + dram__bytes_write.sum of the 11 conv_gemm launches of
-# one 524,288-column run of 128 config-5 pages, 631.4 MB, / 11,
+# one 524,288-column run of 128 config-5 pages, 630.4 MB, / 11,
 # x 4 (a 2,097,152-column run); scaled by columns to the bench's runs below (a lower bound: at the
 # capture's size the outputs mostly stay in L2)
-CONV_TRAFFIC_PER_LAUNCH = 631.4e6 / 11 * 4
+CONV_TRAFFIC_PER_LAUNCH = 630.4e6 / 11 * 4
 
 
 class ClockSampler:
