@@ -857,21 +857,39 @@ __global__ void collapse_kernel(const __grid_constant__ CollapseParams p) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= p.n) return;
   const int f0 = p.line_frame0[i], len = p.length[i];
+  // the frames' ids and probabilities eight at a time, loaded before any of the eight is written
+  // out (the outputs are other arrays, but the compiler cannot know that, so a load after a store
+  // would wait for it); the current character's highest probability kept in a register
+  const int32_t* __restrict__ fid = p.frame_id + f0;
+  const float* __restrict__ fpr = p.frame_prob + f0;
   int k = 0, prev = 0;
-  for (int t = 0; t < len; ++t) {
-    const int id = p.frame_id[f0 + t];
-    const float q = p.frame_prob[f0 + t];
-    if (id != 0 && id != prev) {
-      p.ids[f0 + k] = id;
-      p.frames[f0 + k] = t;
-      p.probs[f0 + k] = q;
-      ++k;
-    } else if (id != 0) {
-      const float last = p.probs[f0 + k - 1];
-      p.probs[f0 + k - 1] = last > q ? last : q;
+  float best = 0.0f;
+  for (int t0 = 0; t0 < len; t0 += 8) {
+    int32_t id8[8];
+    float q8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      id8[u] = t0 + u < len ? __ldg(fid + t0 + u) : 0;
+      q8[u] = t0 + u < len ? __ldg(fpr + t0 + u) : 0.0f;
     }
-    prev = id;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (t0 + u >= len) break;
+      const int id = id8[u];
+      const float q = q8[u];
+      if (id != 0 && id != prev) {
+        if (k > 0) p.probs[f0 + k - 1] = best;
+        p.ids[f0 + k] = id;
+        p.frames[f0 + k] = t0 + u;
+        best = q;
+        ++k;
+      } else if (id != 0) {
+        best = best > q ? best : q;
+      }
+      prev = id;
+    }
   }
+  if (k > 0) p.probs[f0 + k - 1] = best;
   p.count[i] = k;
 }
 
