@@ -20,7 +20,11 @@
  * Plain pointers and sizes only.  Every call returns a status (CREC_OK or an error code);
  * no exception crosses the ABI; crec_last_error() gives the message.  A handle drives one
  * GPU and is not safe to call from two threads at once (the reference's recognize stage
- * calls its device from one thread, pipeline.h:92-93); open one handle per GPU.
+ * calls its device from one thread, pipeline.h:92-93); open one handle per GPU.  A handle
+ * starts threads of its own when it first needs them and ends them at crec_close: up to 8 that
+ * stage pageable page rows into pinned chunks (half the host's CPUs, at most 8), one uploader
+ * for crec_prefetch_pages, and up to 7 that lay out a call's runs of 2,048 lines or more; they
+ * sleep or wait on the GPU between calls.
  */
 #ifndef CARBON_REC_H_
 #define CARBON_REC_H_
